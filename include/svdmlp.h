@@ -1,0 +1,245 @@
+/*
+ * svdmlp.h -- C ABI of the B200 (sm_100a) SVD-compressed LLaMA MLP library.
+ *
+ * The library computes one SwiGLU MLP layer whose gate, up and down weights are
+ * low-rank factor pairs:
+ *
+ *     H   = SiLU((X . u_gate) . v_gate) * ((X . u_up) . v_up)      "gate/up"
+ *     out = (H . u_down) . v_down                                 "XUV down"
+ *
+ * with bf16 inputs, fp32 accumulation and one bf16 rounding per GEMM boundary.
+ * Factor names follow the reference Python (kernels/reference.py:54-93):
+ * u_* is the first factor [in, r], v_* the second factor [r, out].
+ *
+ * Conventions
+ *  - Every entry point returns an int status: 0 = SVDMLP_OK, negative = error.
+ *  - All device buffers are owned by the caller; no entry point allocates
+ *    device memory, and none synchronises the stream except
+ *    svdmlp_check_device_status().
+ *  - Matrices are row-major bf16 (uint16 storage) with an explicit leading
+ *    dimension in elements; `void*` pointers are device pointers.
+ *  - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
+ *    legacy default stream).
+ *  - Weights are packed once (svdmlp_pack) into K-major, TMA-legal layouts;
+ *    the reference rebuilds/pads its weights outside timing in the same way
+ *    (test_speedup.py:809-812, _pad at test_speedup.py:52).
+ */
+#ifndef SVDMLP_H_
+#define SVDMLP_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define SVDMLP_OK 0
+#define SVDMLP_ERR_INVALID_VALUE (-1)   /* non-positive size, NULL pointer        */
+#define SVDMLP_ERR_SHAPE_MISMATCH (-2)  /* contraction dims / gate-up shapes      */
+#define SVDMLP_ERR_ALIGNMENT (-3)       /* pointer or leading dim not 16-byte legal */
+#define SVDMLP_ERR_DTYPE (-4)           /* unsupported element type                */
+#define SVDMLP_ERR_WORKSPACE (-5)       /* workspace too small                     */
+#define SVDMLP_ERR_DEVICE_TIMEOUT (-6)  /* a bounded device-side wait expired      */
+#define SVDMLP_ERR_CUDA (-7)            /* CUDA runtime/driver error               */
+#define SVDMLP_ERR_BUDGET (-8)          /* SMEM/TMEM budget exceeds the device     */
+#define SVDMLP_ERR_DEVICE (-9)          /* device is not sm_100 (B200 class)       */
+
+/* Human-readable text for a status code. */
+const char* svdmlp_status_string(int status);
+
+/* Last CUDA error code seen by the library on this thread (0 if none). */
+int svdmlp_last_cuda_error(void);
+
+/* ------------------------------------------------------------------ layout */
+#define SVDMLP_KIND_SVD 1   /* low-rank factor pairs                     */
+#define SVDMLP_KIND_DENSE 2 /* dense SwiGLU weights, same kernels        */
+
+/*
+ * Packed-weight layout of one MLP layer.  Filled by svdmlp_layout_init() /
+ * svdmlp_dense_layout_init(); callers treat it as read-only.
+ *
+ * SVD kind (ranks r_gu for gate and up, r_d for down; a rank of 0 leaves that
+ * half out, so a down-only layout serves xuv_matmul and a gate/up-only layout
+ * serves fused_gate_up):
+ *   w1 [2*rp_gu, ld_d]  bf16  rows [0,r_gu) = u_gate^T, rows [rp_gu, rp_gu+r_gu) = u_up^T
+ *   vg [ff, rp_gu]      fp16  v_gate^T
+ *   vu [ff, rp_gu]      fp16  v_up^T
+ *   ud [rp_d, ld_ff]    fp16  u_down^T  (bf16 when r_gu == 0, see ud_f16)
+ *   vd [d, rp_d]        fp16  v_down^T
+ * Dense kind:
+ *   vg [ff, ld_d] bf16 w_gate^T,  vu [ff, ld_d] bf16 w_up^T,  ud [d, ld_ff] fp16 w_down^T
+ * Pads are zero.  rp_* and ld_* are multiples of 8 elements (16 bytes).
+ *
+ * Precision: inputs and outputs are bf16.  The intermediates X.u (rank r),
+ * H (ff) and H.u_down (rank r) are kept in fp16 (saturating at +-65504), so
+ * every weight that multiplies an intermediate is packed as fp16.  bf16 ->
+ * fp16 is exact for magnitudes in [2^-14, 65504]; smaller weights become fp16
+ * subnormals (absolute error <= 2^-25).  All accumulation is fp32.
+ */
+typedef struct svdmlp_layout {
+  int32_t kind;
+  int32_t d, ff, r_gu, r_d;
+  int32_t rp_gu, rp_d, ld_d, ld_ff;
+  int32_t ud_f16; /* 1: ud is stored as fp16 (full layers), 0: bf16 (down-only layouts) */
+  int64_t off_w1, off_vg, off_vu, off_ud, off_vd; /* byte offsets into the packed buffer */
+  int64_t packed_bytes;
+} svdmlp_layout;
+
+/* SVD layer layout.  Replaces the rank/shape planning of the reference
+ * launchers (test_speedup.py:169-191, _fusion_shape test_speedup.py:267-299).
+ * Errors: INVALID_VALUE if d or ff <= 0, or r_gu < 0, r_d < 0, or both ranks 0. */
+int svdmlp_layout_init(svdmlp_layout* layout, int d, int ff, int r_gu, int r_d);
+
+/* Dense SwiGLU layer layout (the dense arm, kernels/reference.py:96-106). */
+int svdmlp_dense_layout_init(svdmlp_layout* layout, int d, int ff);
+
+/*
+ * Packs the six factors (natural reference layouts, row-major bf16) into
+ * `packed` (layout->packed_bytes bytes, 256-byte aligned).  Factors of a
+ * half that the layout leaves out may be NULL.
+ *   u_gate, u_up [d, r_gu]   v_gate, v_up [r_gu, ff]
+ *   u_down [ff, r_d]         v_down [r_d, d]
+ * Replaces the loader transposes of the reference (models/hf_svd.py:130-196)
+ * and the padding in test_speedup.py:514-518, 538-543.
+ */
+int svdmlp_pack(const svdmlp_layout* layout, const void* u_gate, int64_t ld_u_gate, const void* v_gate,
+                int64_t ld_v_gate, const void* u_up, int64_t ld_u_up, const void* v_up, int64_t ld_v_up,
+                const void* u_down, int64_t ld_u_down, const void* v_down, int64_t ld_v_down, void* packed,
+                void* stream);
+
+/* Packs dense weights w_gate, w_up [d, ff] and w_down [ff, d]. */
+int svdmlp_dense_pack(const svdmlp_layout* layout, const void* w_gate, int64_t ld_w_gate, const void* w_up,
+                      int64_t ld_w_up, const void* w_down, int64_t ld_w_down, void* packed, void* stream);
+
+/* --------------------------------------------------------------- workspace */
+/* Bytes of workspace needed by any entry point below for up to `max_m` tokens. */
+int64_t svdmlp_workspace_bytes(const svdmlp_layout* layout, int max_m);
+
+/* Zeroes the workspace control block (error word and split-K counters).
+ * Call once after allocating a workspace; the kernels keep it clean after. */
+int svdmlp_workspace_init(void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Synchronises `stream`, then reports SVDMLP_ERR_DEVICE_TIMEOUT if a device
+ * wait expired in an earlier launch on this workspace (and re-arms the
+ * control block), SVDMLP_ERR_CUDA on a sticky CUDA error, else SVDMLP_OK. */
+int svdmlp_check_device_status(void* workspace, int64_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- operators */
+/*
+ * Fused low-rank gate/up operator: h[M, ff] = SiLU(x.u_gate.v_gate) * (x.u_up.v_up).
+ * Replaces kernels/reference.py:54-72 (fused_gate_up_ref), the Pallas
+ * launcher fused_mlp_up_T (test_speedup.py:522-544, which returns the
+ * transpose; this returns the natural [M, ff] layout) and
+ * pallas_ops.fused_gate_up (called at bench/smoke.py:81-83).
+ */
+int svdmlp_gate_up(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x, int m, void* h,
+                   int64_t ld_h, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * XUV down operator: y[M, d] = (h . u_down) . v_down.
+ * Replaces kernels/reference.py:75-82 (fused_xuv_ref), the Pallas launcher
+ * fused_three_mm_XTUV (test_speedup.py:500-519) and pallas_ops.xuv_matmul
+ * (bench/latency.py:346, bench/profile_xuv.py:32-39).
+ */
+int svdmlp_xuv(const svdmlp_layout* layout, const void* packed, const void* h, int64_t ld_h, int m, void* y,
+               int64_t ld_y, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Full SVD layer y = xuv(gate_up(x)) (two operators, four GEMM launches).
+ * Replaces kernels/reference.py:85-93 (svd_mlp_ref),
+ * svd_mlp_with_fused_kernel (test_speedup.py:631-655) and pallas_ops.svd_mlp
+ * (bench/latency.py:402-404, models/modeling_llama.py:851-862).
+ * With a non-NULL `residual` (ld_residual) the result is y = residual + mlp(x),
+ * added in the last GEMM's epilogue (the decoder's residual,
+ * models/modeling_llama.py:998-1002).
+ */
+int svdmlp_forward(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x, int m, void* y,
+                   int64_t ld_y, const void* residual, int64_t ld_residual, void* workspace,
+                   int64_t workspace_bytes, void* stream);
+
+/*
+ * Dense SwiGLU layer y = (SiLU(x.w_gate) * (x.w_up)) . w_down from the same
+ * kernels.  Replaces kernels/reference.py:96-106 (dense_mlp_ref), nki_baseline
+ * (test_speedup.py:669-678) and pallas_ops.dense_mlp
+ * (models/modeling_llama.py:930-937).  `residual` as in svdmlp_forward.
+ */
+int svdmlp_dense_forward(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x, int m,
+                         void* y, int64_t ld_y, const void* residual, int64_t ld_residual, void* workspace,
+                         int64_t workspace_bytes, void* stream);
+
+/* ------------------------------------------------------ tensor parallel (ff) */
+/*
+ * First half of the down operator on an ff-shard: partial[M, r_d] (fp32) =
+ * h_p . u_down_p, where h_p = [M, ff/P] and u_down_p = rows of u_down owned by
+ * this rank.  The caller all-reduces `partial` (sum) across ranks, then calls
+ * svdmlp_down_finish.  The reference has no multi-device path
+ * (models/README.md:26-27); this is the exchange point of the ff-sharded
+ * layer.
+ */
+int svdmlp_down_partial(const svdmlp_layout* layout, const void* packed, const void* h, int64_t ld_h, int m,
+                        float* partial, int64_t ld_partial, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Stages 1-3 of an ff-shard in one call: partial[M, r_d] (fp32) =
+ * gate_up_p(x) . u_down_p, the rank-local contribution that is all-reduced. */
+int svdmlp_forward_partial(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x, int m,
+                           float* partial, int64_t ld_partial, void* workspace, int64_t workspace_bytes,
+                           void* stream);
+
+/* Second half: y[M, d] = fp16(partial) . v_down (+ residual if non-NULL). */
+int svdmlp_down_finish(const svdmlp_layout* layout, const void* packed, const float* partial,
+                       int64_t ld_partial, int m, void* y, int64_t ld_y, const void* residual,
+                       int64_t ld_residual, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------- building blocks */
+/*
+ * c[M, N] = a[M, K] . b[K, N] given b pre-transposed as bt[N, K] (K-major):
+ * the dense GEMM of the reference's nki_matmul_fully_optimized_
+ * (test_speedup.py:548-615) and pallas_ops.dense_matmul
+ * (bench/diagnose_down.py:121), on the same tcgen05 kernel.
+ */
+int svdmlp_gemm(const void* a, int64_t ld_a, const void* bt, int64_t ld_bt, void* c, int64_t ld_c, int m, int n,
+                int k, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes svdmlp_gemm needs for this shape (control block, split-K
+ * counters and partials). */
+int64_t svdmlp_gemm_workspace_bytes(int m, int n, int k);
+
+/* dst[i][j] = src[j][i] for i < cols, j < rows; zero for i < dst_rows, j < dst_cols outside. */
+int svdmlp_transpose_pack(const void* src, int64_t ld_src, int rows, int cols, void* dst, int64_t ld_dst,
+                          int dst_rows, int dst_cols, void* stream);
+
+/* RMSNorm y = x * rsqrt(mean(x^2) + eps) * w over rows of length n (bf16 in/out,
+ * fp32 math); the decoder norm of models/modeling_llama.py:245-262. */
+int svdmlp_rmsnorm(const void* x, int64_t ld_x, const void* w, void* y, int64_t ld_y, int m, int n, float eps,
+                   void* stream);
+
+/* --------------------------------------------------------------- diagnostics */
+/*
+ * Launches one CTA whose only work is a bounded wait on an mbarrier that
+ * nothing completes, with a limit of `limit_ns` nanoseconds.  The wait expires,
+ * records the timeout in the workspace error word and the kernel returns;
+ * svdmlp_check_device_status() then reports SVDMLP_ERR_DEVICE_TIMEOUT.  Used by
+ * the failure-detection tests; the device context stays usable.
+ */
+int svdmlp_debug_wait_timeout(void* workspace, int64_t workspace_bytes, int64_t limit_ns, void* stream);
+
+/*
+ * Tuning hooks (the analogue of the reference's block autotuner,
+ * bench/tune.py:34-100).  Stage ids: 0 = X.[u_g|u_u], 1 = gate/up SwiGLU GEMM,
+ * 2 = H.u_down, 3 = T.v_down, 4 = dense gate/up, 5 = dense down,
+ * 6 = svdmlp_gemm.  `splits` = 0 restores the built-in split-K planner.
+ * svdmlp_plan_info writes {m_tiles, n_tiles, k_blocks, splits, units, grid}.
+ */
+int svdmlp_set_split_override(int stage, int splits);
+int svdmlp_plan_info(int stage, int m, int n, int k, int* out6);
+
+/* Number of kernel launches the library has enqueued since load (all entry points). */
+int64_t svdmlp_launch_count(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SVDMLP_H_ */

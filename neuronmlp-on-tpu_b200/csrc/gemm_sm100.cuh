@@ -1,0 +1,452 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+//   C[M, N] = epilogue( A[M, K] . B[N, K]^T )        (both operands K-major, bf16)
+//
+// Dual form (NB == 2): two accumulators per tile, C = silu(A.Bg^T) * (A2.Bu^T);
+// this is the fused low-rank gate/up operator's second stage (the SwiGLU
+// epilogue of kernels/reference.py:54-72 applied on fp32 accumulators).
+//
+// Operands are bf16 or fp16 (both the same type in one MMA); the output is
+// bf16, fp16 or fp32.  The SVD layer keeps its rank-r and ff intermediates in
+// fp16: its unit roundoff (2^-11) is 8x smaller than bf16's, at the same
+// tensor-core rate, which keeps the layer well inside the max-abs error bound
+// that bf16 intermediates overshoot.
+//
+// Roles (192 threads, one CTA per SM):
+//   warps 0-3  epilogue: TMEM -> registers -> (math) -> swizzled smem -> TMA store
+//   warp  4    TMA producer: STAGES-deep smem ring of 128B-swizzled K-major tiles
+//   warp  5    TMEM allocator + single-thread tcgen05.mma issuer
+// Accumulators are double-buffered in TMEM so the epilogue of one tile
+// overlaps the main loop of the next.
+//
+// Work units are (m_tile, split, n_tile) with m fastest: the CTAs that run at
+// the same time share the same weight (B) tile, so each weight tile is read
+// from HBM once and served from L2 to the other M-tiles.
+//
+// Split-K: every split writes an fp32 partial tile to the workspace and bumps
+// a per-tile counter; the split that arrives last sums all partials in split
+// order (deterministic) and runs the epilogue.  Nothing ever waits on another
+// CTA, so split-K cannot deadlock.  The last split resets the counter.
+#pragma once
+
+#include "ptx.cuh"
+
+namespace svdmlp {
+
+enum EpiKind : int { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESID = 2 };
+enum OutKind : int { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2 };
+
+// Error sites recorded in the device error word when a bounded wait expires.
+enum ErrSite : int {
+  SITE_PRODUCER_EMPTY = 1,
+  SITE_MMA_FULL = 2,
+  SITE_MMA_ACC_EMPTY = 3,
+  SITE_EPI_ACC_FULL = 4,
+  SITE_DRAIN_LOADS = 5,
+  SITE_DRAIN_MMA = 6,
+  SITE_PROBE = 7,
+};
+
+struct GemmParams {
+  int M, N, K;  // N is the per-branch width for dual GEMMs
+  int m_tiles, n_tiles, k_blocks;
+  int splits, kb_per_split;
+  int num_units;
+  float* partials;  // split-K partial tiles  [tiles][splits][NB][BM*BN]
+  int* counters;    // split-K arrival counters [tiles], zero between launches
+  int* err;         // device error word
+  unsigned long long timeout_ns;
+  const __nv_bfloat16* residual;  // EPI_RESID: C = acc + residual (bf16)
+  long long ld_residual;
+};
+
+template <int BN_, int NB_, bool SHARED_A_, int STAGES_, int EPI_, bool IN_F16_, int OUT_>
+struct GemmCfg {
+  static constexpr int BM = 128, BK = 64;
+  static constexpr int BN = BN_, NB = NB_, STAGES = STAGES_, EPI = EPI_, OUT = OUT_;
+  static constexpr bool IN_F16 = IN_F16_;
+  static constexpr bool SHARED_A = SHARED_A_;
+  static constexpr int NA = (NB == 2 && !SHARED_A) ? 2 : 1;
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
+  static_assert(NB == 1 || NB == 2, "one or two accumulators per tile");
+  static_assert(NB == 1 || EPI == EPI_SWIGLU, "dual GEMMs use the SwiGLU epilogue");
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
+  static constexpr bool IS_F32 = (OUT == OUT_F32);
+  static constexpr int OUT_ELT = IS_F32 ? 4 : 2;
+  static constexpr int STG_BYTES = 32 * 32 * OUT_ELT;  // one 32x32 output box per warp buffer
+  static constexpr int BSTRIDE = BN <= 128 ? 128 : 256;  // TMEM columns between the two branches
+  static constexpr int ACC_STRIDE = NB * BSTRIDE;        // TMEM columns per accumulator buffer
+  static_assert(2 * ACC_STRIDE <= 512, "double-buffered accumulators must fit in 512 TMEM columns");
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t IDESC = make_idesc_16bit(BM, BN, IN_F16);
+
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_A2 = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_B = OFF_A2 + (NA == 2 ? STAGES * A_BYTES : 0);
+  static constexpr int OFF_B2 = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_STG = OFF_B2 + (NB == 2 ? STAGES * B_BYTES : 0);
+  static constexpr int OFF_BAR = OFF_STG + 4 * 2 * STG_BYTES;
+  static constexpr int NUM_BARS = 2 * STAGES + 5;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;  // + slack for 1024-byte alignment
+  static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
+};
+
+template <class Cfg>
+struct UnitCoord {
+  int m_t, n_t, ks, kb0, kb1, tile;
+};
+
+template <class Cfg>
+SVD_DEV UnitCoord<Cfg> decode_unit(const GemmParams& p, int u) {
+  UnitCoord<Cfg> c;
+  c.m_t = u % p.m_tiles;
+  const int rest = u / p.m_tiles;
+  c.ks = rest % p.splits;
+  c.n_t = rest / p.splits;
+  c.kb0 = c.ks * p.kb_per_split;
+  c.kb1 = min(c.kb0 + p.kb_per_split, p.k_blocks);
+  c.tile = c.n_t * p.m_tiles + c.m_t;
+  return c;
+}
+
+// Writes one 32-row x 32-column output box (this warp's rows) through a
+// swizzled staging buffer and a TMA store.  `v` holds this thread's row.
+template <class Cfg>
+SVD_DEV void store_box(const CUtensorMap* tm_out, uint8_t* stg_warp, int& stg_buf, const float (&v)[32], int x,
+                       int y, int M, int N) {
+  const uint32_t lane = lane_id();
+  uint8_t* stg = stg_warp + stg_buf * Cfg::STG_BYTES;
+  // The TMA store issued two boxes ago used this buffer; make sure it has
+  // finished reading it (at most one group, the other buffer's, may remain).
+  if (lane == 0) bulk_wait_group_read<1>();
+  __syncwarp();
+  if constexpr (Cfg::IS_F32) {
+    // 128-byte rows, 128-byte swizzle: 16-byte chunk j lands at j ^ (row & 7).
+    const uint32_t base = smem_addr(stg) + lane * 128;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t phys = static_cast<uint32_t>(j) ^ (lane & 7u);
+      st_shared_v4(base + phys * 16, __float_as_uint(v[4 * j]), __float_as_uint(v[4 * j + 1]),
+                   __float_as_uint(v[4 * j + 2]), __float_as_uint(v[4 * j + 3]));
+    }
+  } else {
+    // 64-byte rows, 64-byte swizzle: 16-byte chunk j lands at j ^ ((row >> 1) & 3).
+    const uint32_t base = smem_addr(stg) + lane * 64;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t phys = static_cast<uint32_t>(j) ^ ((lane >> 1) & 3u);
+      if constexpr (Cfg::OUT == OUT_F16)
+        st_shared_v4(base + phys * 16, pack_f16x2_sat(v[8 * j], v[8 * j + 1]), pack_f16x2_sat(v[8 * j + 2], v[8 * j + 3]),
+                     pack_f16x2_sat(v[8 * j + 4], v[8 * j + 5]), pack_f16x2_sat(v[8 * j + 6], v[8 * j + 7]));
+      else
+        st_shared_v4(base + phys * 16, pack_bf16x2(v[8 * j], v[8 * j + 1]), pack_bf16x2(v[8 * j + 2], v[8 * j + 3]),
+                     pack_bf16x2(v[8 * j + 4], v[8 * j + 5]), pack_bf16x2(v[8 * j + 6], v[8 * j + 7]));
+    }
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    // Boxes that lie wholly outside the output (rows >= M or columns >= N)
+    // are skipped; partly outside boxes are clipped by the TMA unit.
+    if (y < M && x < N) tma_store_2d(tm_out, stg, x, y);
+    bulk_commit_group();
+  }
+  stg_buf ^= 1;
+}
+
+SVD_DEV float silu_mul(float g, float u) {
+  // g * sigmoid(g) * u; for g << 0 the denominator overflows to +inf and the
+  // quotient is the correct limit 0.
+  return __fdividef(g, 1.0f + __expf(-g)) * u;
+}
+
+// Applies the epilogue to one 32-column chunk of this thread's row.
+template <class Cfg>
+SVD_DEV void epilogue_math(const GemmParams& p, float (&v)[32], const float (&u)[32], int row, int col) {
+  if constexpr (Cfg::EPI == EPI_SWIGLU) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = silu_mul(v[j], u[j]);
+  } else if constexpr (Cfg::EPI == EPI_RESID) {
+    if (row < p.M) {
+      const __nv_bfloat16* r = p.residual + static_cast<long long>(row) * p.ld_residual + col;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (col + 8 * q + 8 <= p.N) {
+          const uint4 w = __ldg(reinterpret_cast<const uint4*>(r + 8 * q));
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&w);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = __bfloat1622float2(h[e]);
+            v[8 * q + 2 * e] += f.x;
+            v[8 * q + 2 * e + 1] += f.y;
+          }
+        }
+      }
+    }
+  }
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(192, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a2,
+                      const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b2,
+                      const __grid_constant__ CUtensorMap tm_out, const GemmParams p) {
+  constexpr int STAGES = Cfg::STAGES;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* fix_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* epi_abort = reinterpret_cast<volatile int*>(tmem_slot + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *fix_flag = 0;
+    *epi_abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tensormap(&tm_a);
+    if (Cfg::NA == 2) prefetch_tensormap(&tm_a2);
+    prefetch_tensormap(&tm_b);
+    if (Cfg::NB == 2) prefetch_tensormap(&tm_b2);
+    prefetch_tensormap(&tm_out);
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtx ctx{abort_flag, p.err, p.timeout_ns};
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      grid_dependency_wait();  // inputs of this launch come from the previous one
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        const UnitCoord<Cfg> c = decode_unit<Cfg>(p, u);
+        for (int kb = c.kb0; kb < c.kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, ctx, SITE_PRODUCER_EMPTY)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
+          const int kx = kb * Cfg::BK;
+          tma_load_2d(&tm_a, &full[s], smem + Cfg::OFF_A + s * Cfg::A_BYTES, kx, c.m_t * Cfg::BM);
+          if constexpr (Cfg::NA == 2)
+            tma_load_2d(&tm_a2, &full[s], smem + Cfg::OFF_A2 + s * Cfg::A_BYTES, kx, c.m_t * Cfg::BM);
+          tma_load_2d(&tm_b, &full[s], smem + Cfg::OFF_B + s * Cfg::B_BYTES, kx, c.n_t * Cfg::BN);
+          if constexpr (Cfg::NB == 2)
+            tma_load_2d(&tm_b2, &full[s], smem + Cfg::OFF_B2 + s * Cfg::B_BYTES, kx, c.n_t * Cfg::BN);
+        }
+      }
+      grid_launch_dependents();
+      // Drain: every stage's most recent load must have landed before the CTA
+      // may exit (on the normal path these waits return at once).
+      for (int s = 0; s < STAGES; ++s) {
+        if (it > s) {
+          const int last = s + ((it - 1 - s) / STAGES) * STAGES;
+          mbar_wait(&full[s], static_cast<uint32_t>(last / STAGES) & 1u, ctx, SITE_DRAIN_LOADS, false);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0, acc_it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
+        const UnitCoord<Cfg> c = decode_unit<Cfg>(p, u);
+        const int b = acc_it & 1;
+        const uint32_t aph = static_cast<uint32_t>(acc_it >> 1) & 1u;
+        if (!mbar_wait(&acc_empty[b], aph ^ 1u, ctx, SITE_MMA_ACC_EMPTY)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
+        for (int kb = c.kb0; kb < c.kb1; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+          if (!mbar_wait(&full[s], ph, ctx, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(smem + Cfg::OFF_A + s * Cfg::A_BYTES);
+          const uint32_t a2_addr =
+              Cfg::NA == 2 ? smem_addr(smem + Cfg::OFF_A2 + s * Cfg::A_BYTES) : a_addr;
+          const uint32_t b_addr = smem_addr(smem + Cfg::OFF_B + s * Cfg::B_BYTES);
+          const uint32_t b2_addr = smem_addr(smem + Cfg::OFF_B2 + s * Cfg::B_BYTES);
+#pragma unroll
+          for (int k = 0; k < Cfg::BK / 16; ++k) {
+            const uint32_t acc = (kb > c.kb0 || k > 0) ? 1u : 0u;
+            umma_f16kind(d, make_sw128_desc(a_addr + k * 32), make_sw128_desc(b_addr + k * 32), Cfg::IDESC, acc);
+            if constexpr (Cfg::NB == 2)
+              umma_f16kind(d + Cfg::BSTRIDE, make_sw128_desc(a2_addr + k * 32), make_sw128_desc(b2_addr + k * 32),
+                        Cfg::IDESC, acc);
+          }
+          umma_commit(&empty[s]);  // frees the smem stage once these MMAs have read it
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[b]);  // accumulator ready for the epilogue
+        ++acc_it;
+      }
+      // Drain: all issued MMAs must be complete before TMEM is released.
+      umma_commit(drain);
+      mbar_wait(drain, 0, ctx, SITE_DRAIN_MMA, false);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp;  // TMEM lane quarter == rows [32q, 32q + 32) of the tile
+    uint8_t* stg_warp = smem + Cfg::OFF_STG + q * 2 * Cfg::STG_BYTES;
+    int stg_buf = 0;
+    int acc_it = 0;
+    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
+      const UnitCoord<Cfg> c = decode_unit<Cfg>(p, u);
+      const int b = acc_it & 1;
+      const uint32_t aph = static_cast<uint32_t>(acc_it >> 1) & 1u;
+      bool ok = mbar_wait(&acc_full[b], aph, ctx, SITE_EPI_ACC_FULL);
+      ok = __all_sync(0xffffffffu, ok);
+      // The four epilogue warps take the same decision, so that none of them
+      // is left alone at a named barrier below.
+      if (!ok && lane == 0) *epi_abort = 1;
+      named_barrier_sync(2, 128);
+      if (*epi_abort) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
+      const int row_in_tile = q * 32 + static_cast<int>(lane);
+      const int grow = c.m_t * Cfg::BM + row_in_tile;
+      const int n0 = c.n_t * Cfg::BN;
+      const int y_box = c.m_t * Cfg::BM + q * 32;
+
+      if (p.splits == 1) {
+#pragma unroll 1
+        for (int ch = 0; ch < Cfg::BN / 32; ++ch) {
+          uint32_t rg[32];
+          uint32_t ru[32];
+          tmem_ld_x32(tacc + ch * 32, rg);
+          if constexpr (Cfg::NB == 2) tmem_ld_x32(tacc + Cfg::BSTRIDE + ch * 32, ru);
+          tmem_ld_wait();
+          float v[32], w[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            v[j] = __uint_as_float(rg[j]);
+            w[j] = Cfg::NB == 2 ? __uint_as_float(ru[j]) : 0.0f;
+          }
+          epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
+          store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);
+      } else {
+        // Pass 1: publish this split's fp32 partial tile.
+        float* slot = p.partials + static_cast<size_t>(c.tile * p.splits + c.ks) * Cfg::NB * (Cfg::BM * Cfg::BN);
+#pragma unroll 1
+        for (int ch = 0; ch < Cfg::BN / 32; ++ch) {
+#pragma unroll
+          for (int br = 0; br < Cfg::NB; ++br) {
+            uint32_t r[32];
+            tmem_ld_x32(tacc + br * Cfg::BSTRIDE + ch * 32, r);
+            tmem_ld_wait();
+            float4* dst = reinterpret_cast<float4*>(slot + static_cast<size_t>(br) * (Cfg::BM * Cfg::BN) +
+                                                    ch * (Cfg::BM * 32) + row_in_tile * 32);
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&acc_empty[b]);  // TMEM no longer needed for this unit
+        __threadfence();
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 0) {
+          const int old = atomicAdd(&p.counters[c.tile], 1);
+          *fix_flag = (old == p.splits - 1) ? 1 : 0;
+        }
+        named_barrier_sync(1, 128);
+        if (*fix_flag) {
+          __threadfence();
+          const float* base = p.partials + static_cast<size_t>(c.tile * p.splits) * Cfg::NB * (Cfg::BM * Cfg::BN);
+#pragma unroll 1
+          for (int ch = 0; ch < Cfg::BN / 32; ++ch) {
+            float v[32], w[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] = 0.0f;
+              w[j] = 0.0f;
+            }
+#pragma unroll 1
+            for (int s = 0; s < p.splits; ++s) {
+              const float* src = base + static_cast<size_t>(s) * Cfg::NB * (Cfg::BM * Cfg::BN) + ch * (Cfg::BM * 32) +
+                                 row_in_tile * 32;
+              const float4* s4 = reinterpret_cast<const float4*>(src);
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float4 t = __ldcg(s4 + j);
+                v[4 * j] += t.x;
+                v[4 * j + 1] += t.y;
+                v[4 * j + 2] += t.z;
+                v[4 * j + 3] += t.w;
+              }
+              if constexpr (Cfg::NB == 2) {
+                const float4* u4 = reinterpret_cast<const float4*>(src + Cfg::BM * Cfg::BN);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                  const float4 t = __ldcg(u4 + j);
+                  w[4 * j] += t.x;
+                  w[4 * j + 1] += t.y;
+                  w[4 * j + 2] += t.z;
+                  w[4 * j + 3] += t.w;
+                }
+              }
+            }
+            epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
+            store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
+          }
+          if (threadIdx.x == 0) p.counters[c.tile] = 0;
+        }
+      }
+      ++acc_it;
+    }
+    if (lane == 0) bulk_wait_group<0>();  // all output boxes written before exit
+    __syncwarp();
+  }
+
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+}  // namespace svdmlp

@@ -1,0 +1,926 @@
+// Host side of the SVD-MLP library: C ABI, weight packing, workspace carving,
+// split-K planning, tensor-map encoding and launches of the sm_100a kernels.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+
+#include "../../include/svdmlp.h"
+#include "gemm_sm100.cuh"
+
+using bf16 = __nv_bfloat16;
+
+namespace svdmlp {
+
+// ------------------------------------------------------------------ state
+static thread_local int g_last_cuda_error = 0;
+static std::atomic<int64_t> g_launches{0};
+static int g_split_override[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+static unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s: far above any legal wait
+
+static int cuda_fail(cudaError_t e) {
+  g_last_cuda_error = static_cast<int>(e);
+  return SVDMLP_ERR_CUDA;
+}
+#define SVD_CUDA(call)                         \
+  do {                                         \
+    cudaError_t e_ = (call);                   \
+    if (e_ != cudaSuccess) return cuda_fail(e_); \
+  } while (0)
+#define SVD_CHECK(...)      \
+  do {                      \
+    int s_ = (__VA_ARGS__); \
+    if (s_ != SVDMLP_OK) return s_; \
+  } while (0)
+
+static int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+static int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+struct DeviceInfo {
+  int sms = 0;
+  int major = 0;
+  bool attrs_set = false;
+};
+static std::mutex g_dev_mu;
+static DeviceInfo g_dev[64];
+
+static int device_info(DeviceInfo** out) {
+  int dev = 0;
+  SVD_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return SVDMLP_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.sms == 0) {
+    SVD_CUDA(cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev));
+    SVD_CUDA(cudaDeviceGetAttribute(&d.major, cudaDevAttrComputeCapabilityMajor, dev));
+  }
+  if (d.major != 10) return SVDMLP_ERR_DEVICE;
+  *out = &d;
+  return SVDMLP_OK;
+}
+
+// Number of SMs used for planning: the current device's, or 148 (B200) when
+// no device is visible (workspace sizing on a host without a GPU).
+static int planning_sms() {
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess &&
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess && sms > 0)
+    return sms;
+  cudaGetLastError();
+  return 148;
+}
+
+// ------------------------------------------------------------- tensor maps
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+enum class DT { BF16, F16, F32 };
+
+// 2-D row-major tensor [outer, inner] with leading dimension `ld` elements.
+static int make_map(CUtensorMap* map, const void* base, DT dt, int64_t inner, int64_t outer, int64_t ld,
+                    uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return cuda_fail(cudaErrorInitializationError);
+  const int elt = dt == DT::F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || (ld * elt) % 16 != 0) return SVDMLP_ERR_ALIGNMENT;
+  const CUtensorMapDataType t = dt == DT::F32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                : dt == DT::F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(inner), static_cast<cuuint64_t>(outer)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elt)};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, t, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return SVDMLP_ERR_ALIGNMENT;
+  return SVDMLP_OK;
+}
+
+// Operand tile map: rows of 64 16-bit elements (128 bytes, 128-byte swizzle).
+static int operand_map(CUtensorMap* m, const void* base, bool f16, int64_t k, int64_t rows, int64_t ld,
+                       int box_rows) {
+  return make_map(m, base, f16 ? DT::F16 : DT::BF16, k, rows, ld, 64, static_cast<uint32_t>(box_rows),
+                  CU_TENSOR_MAP_SWIZZLE_128B);
+}
+// Output map: 32 x 32 boxes (16-bit: 64-byte rows, 64B swizzle; fp32: 128-byte rows, 128B swizzle).
+template <class Cfg>
+static int output_map(CUtensorMap* m, const void* base, int64_t n, int64_t rows, int64_t ld) {
+  const DT dt = Cfg::OUT == OUT_F32 ? DT::F32 : Cfg::OUT == OUT_F16 ? DT::F16 : DT::BF16;
+  return make_map(m, base, dt, n, rows, ld, 32, 32,
+                  dt == DT::F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+}
+
+// ------------------------------------------------------------------ planner
+struct Plan {
+  int m_tiles, n_tiles, k_blocks, splits, kb_per_split, units, grid;
+};
+
+// Chooses the split-K factor that minimises a wave-quantisation cost model:
+// rounds of units over the SMs times the k-blocks per unit, plus a per-unit
+// pipeline/epilogue overhead and the fix-up reads of the last split.
+static Plan plan_gemm(int M, int N, int K, int BN, int sms, int forced_splits) {
+  Plan p{};
+  p.m_tiles = static_cast<int>(cdiv(M, 128));
+  p.n_tiles = static_cast<int>(cdiv(N, BN));
+  p.k_blocks = static_cast<int>(cdiv(K, 64));
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+  int best_s = 1;
+  if (forced_splits > 0) {
+    best_s = std::min(forced_splits, p.k_blocks);
+  } else {
+    double best = 1e30;
+    for (int s = 1; s <= 16; ++s) {
+      const int kbs = static_cast<int>(cdiv(p.k_blocks, s));
+      if (s > 1 && kbs < 4) break;
+      const int s_eff = static_cast<int>(cdiv(p.k_blocks, kbs));
+      if (s > 1 && s_eff != s) continue;
+      const int64_t units = tiles * s_eff;
+      const int64_t rounds = cdiv(units, sms);
+      const double cost = static_cast<double>(rounds) * (kbs + 1.5) + (s_eff > 1 ? 1.0 + 0.75 * s_eff : 0.0);
+      if (cost < best * 0.97) {
+        best = cost;
+        best_s = s_eff;
+      }
+    }
+  }
+  p.kb_per_split = static_cast<int>(cdiv(p.k_blocks, best_s));
+  p.splits = static_cast<int>(cdiv(p.k_blocks, p.kb_per_split));
+  p.units = static_cast<int>(tiles * p.splits);
+  p.grid = std::min(p.units, sms);
+  return p;
+}
+
+// Bytes of split-K partials a plan needs (NB accumulators of BM x BN fp32).
+static int64_t partial_bytes(const Plan& p, int BN, int NB) {
+  if (p.splits <= 1) return 0;
+  return static_cast<int64_t>(p.units) * NB * 128 * BN * 4;
+}
+
+// ------------------------------------------------------------ kernel configs
+//            BN  NB shared STG epilogue   fp16-in out
+using CfgXU     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_F16>;   // X.[u_g|u_u] -> XU (fp16)
+using CfgGU     = GemmCfg<128, 2, false, 3, EPI_SWIGLU, true,  OUT_F16>;   // XU.v -> H (fp16, internal)
+using CfgGUbf   = GemmCfg<128, 2, false, 3, EPI_SWIGLU, true,  OUT_BF16>;  // XU.v -> H (bf16, to the caller)
+using CfgDU     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_F16>;   // H.u_down -> T (fp16)
+using CfgDUbf   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_F16>;   // bf16 H.u_down (down-only layout)
+using CfgDUf32  = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_F32>;   // H.u_down -> fp32 partial (TP)
+using CfgDV     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_BF16>;  // T.v_down -> y
+using CfgDVres  = GemmCfg<256, 1, false, 4, EPI_RESID,  true,  OUT_BF16>;  // T.v_down + residual -> y
+using CfgDenseGU = GemmCfg<128, 2, true, 4, EPI_SWIGLU, false, OUT_F16>;   // X.[w_g|w_u] -> H (fp16)
+using CfgGemm   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_BF16>;  // plain bf16 GEMM
+
+enum Stage : int { ST_XU = 0, ST_GATEUP = 1, ST_DOWN_U = 2, ST_DOWN_V = 3, ST_DENSE_GU = 4, ST_DENSE_D = 5, ST_GEMM = 6 };
+
+// Workspace carving.  The control block holds the error word (int 0) and the
+// split-K counters; the rest holds the intermediates.
+struct Workspace {
+  int* err;
+  int* counters;
+  __half* xu;  // [M, 2*rp_gu]  fp16
+  __half* h;   // [M, ld_ff]    fp16 (or bf16 staging of a caller's H)
+  __half* t;   // [M, rp_d]     fp16
+  bf16* xs;   // [M, ld_d] staging for unaligned x
+  bf16* ys;   // [M, ld_d] staging for unaligned y
+  float* partials;
+  int64_t partial_cap;
+};
+
+static constexpr int64_t kCtlBytes = 256;
+static int64_t counters_bytes(const svdmlp_layout* L, int max_m) {
+  const int64_t widest = std::max<int64_t>({2LL * L->rp_gu, L->ff, L->rp_d, L->d, 1});
+  return round_up(cdiv(max_m, 128) * cdiv(widest, 32) * 4, 256);
+}
+
+template <class Cfg>
+static int64_t stage_partials(int M, int N, int K, int sms, int stage) {
+  const Plan p = plan_gemm(M, N, K, Cfg::BN, sms, g_split_override[stage]);
+  return partial_bytes(p, Cfg::BN, Cfg::NB);
+}
+
+// Largest split-K partial buffer any M <= max_m can ask for.
+static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
+  int64_t best = 0;
+  const int64_t mt = cdiv(max_m, 128);
+  for (int64_t t = 1; t <= mt; ++t) {
+    const int M = static_cast<int>(std::min<int64_t>(t * 128, max_m));
+    if (L->kind == SVDMLP_KIND_SVD) {
+      if (L->r_gu > 0) {
+        best = std::max(best, stage_partials<CfgXU>(M, 2 * L->rp_gu, L->d, sms, ST_XU));
+        best = std::max(best, stage_partials<CfgGU>(M, L->ff, L->r_gu, sms, ST_GATEUP));
+      }
+      if (L->r_d > 0) {
+        best = std::max(best, stage_partials<CfgDU>(M, L->r_d, L->ff, sms, ST_DOWN_U));
+        best = std::max(best, stage_partials<CfgDV>(M, L->d, L->r_d, sms, ST_DOWN_V));
+      }
+    } else {
+      best = std::max(best, stage_partials<CfgDenseGU>(M, L->ff, L->d, sms, ST_DENSE_GU));
+      best = std::max(best, stage_partials<CfgDV>(M, L->d, L->ff, sms, ST_DENSE_D));
+    }
+  }
+  return round_up(best, 256);
+}
+
+static int64_t ws_bytes_for(const svdmlp_layout* L, int max_m, int sms) {
+  const int64_t M = max_m;
+  int64_t b = kCtlBytes + counters_bytes(L, max_m);
+  b += round_up(M * 2 * L->rp_gu * 2, 256);
+  b += round_up(M * L->ld_ff * 2, 256);
+  b += round_up(M * L->rp_d * 2, 256);
+  b += 2 * round_up(M * L->ld_d * 2, 256);
+  b += max_partials(L, max_m, sms);
+  return b;
+}
+
+static int carve(const svdmlp_layout* L, int M, void* ws, int64_t ws_bytes, Workspace* w) {
+  if (!ws) return SVDMLP_ERR_INVALID_VALUE;
+  if ((reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return SVDMLP_ERR_ALIGNMENT;
+  const int sms = planning_sms();
+  const int64_t need = ws_bytes_for(L, M, sms);
+  if (ws_bytes < need) return SVDMLP_ERR_WORKSPACE;
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  w->err = reinterpret_cast<int*>(p);
+  p += kCtlBytes;
+  w->counters = reinterpret_cast<int*>(p);
+  p += counters_bytes(L, M);
+  w->xu = reinterpret_cast<__half*>(p);
+  p += round_up(static_cast<int64_t>(M) * 2 * L->rp_gu * 2, 256);
+  w->h = reinterpret_cast<__half*>(p);
+  p += round_up(static_cast<int64_t>(M) * L->ld_ff * 2, 256);
+  w->t = reinterpret_cast<__half*>(p);
+  p += round_up(static_cast<int64_t>(M) * L->rp_d * 2, 256);
+  w->xs = reinterpret_cast<bf16*>(p);
+  p += round_up(static_cast<int64_t>(M) * L->ld_d * 2, 256);
+  w->ys = reinterpret_cast<bf16*>(p);
+  p += round_up(static_cast<int64_t>(M) * L->ld_d * 2, 256);
+  w->partials = reinterpret_cast<float*>(p);
+  w->partial_cap = static_cast<uint8_t*>(ws) + ws_bytes - p;
+  return SVDMLP_OK;
+}
+
+// ------------------------------------------------------------------ launches
+template <class Cfg>
+static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& b, const CUtensorMap& b2,
+                       const CUtensorMap& out, int M, int N, int K, int stage, const Workspace& w,
+                       const bf16* residual, int64_t ld_res, cudaStream_t stream) {
+  DeviceInfo* dev = nullptr;
+  SVD_CHECK(device_info(&dev));
+  static std::mutex mu;
+  {
+    // The dynamic shared memory opt-in is a per-function attribute; set it on
+    // first use for each device.
+    int cur = 0;
+    SVD_CUDA(cudaGetDevice(&cur));
+    static uint64_t done_mask = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!(done_mask & (1ull << cur))) {
+      SVD_CUDA(cudaFuncSetAttribute(gemm_sm100_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg::SMEM_BYTES));
+      done_mask |= 1ull << cur;
+    }
+  }
+  const Plan pl = plan_gemm(M, N, K, Cfg::BN, dev->sms, g_split_override[stage]);
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.m_tiles = pl.m_tiles;
+  p.n_tiles = pl.n_tiles;
+  p.k_blocks = pl.k_blocks;
+  p.splits = pl.splits;
+  p.kb_per_split = pl.kb_per_split;
+  p.num_units = pl.units;
+  p.partials = w.partials;
+  p.counters = w.counters;
+  p.err = w.err;
+  p.timeout_ns = g_wait_limit_ns;
+  p.residual = residual;
+  p.ld_residual = ld_res;
+  if (partial_bytes(pl, Cfg::BN, Cfg::NB) > w.partial_cap) return SVDMLP_ERR_WORKSPACE;
+
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  SVD_CUDA(cudaLaunchKernelEx(&cfg, gemm_sm100_kernel<Cfg>, a, a2, b, b2, out, p));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return SVDMLP_OK;
+}
+
+// ----------------------------------------------------------- small kernels
+template <typename T>
+SVD_DEV T from_float(float v);
+template <>
+SVD_DEV bf16 from_float<bf16>(float v) { return __float2bfloat16(v); }
+template <>
+SVD_DEV __half from_float<__half>(float v) { return __float2half_rn(fminf(fmaxf(v, -65504.f), 65504.f)); }
+
+// dst[i][j] = src[j][i] (bf16 in, bf16 or fp16 out); zero outside the source.
+template <typename TO>
+__global__ void transpose_pack_kernel(const bf16* __restrict__ src, long long ld_src, int rows, int cols,
+                                      TO* __restrict__ dst, long long ld_dst, int dst_rows, int dst_cols) {
+  __shared__ float tile[32][33];
+  const int i0 = blockIdx.y * 32;  // dst rows  == src columns
+  const int j0 = blockIdx.x * 32;  // dst cols  == src rows
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int j = j0 + k, i = i0 + threadIdx.x;
+    tile[k][threadIdx.x] = (j < rows && i < cols) ? __bfloat162float(src[static_cast<long long>(j) * ld_src + i]) : 0.f;
+  }
+  __syncthreads();
+  for (int k = threadIdx.y; k < 32; k += blockDim.y) {
+    const int i = i0 + k, j = j0 + threadIdx.x;
+    if (i < dst_rows && j < dst_cols) dst[static_cast<long long>(i) * ld_dst + j] = from_float<TO>(tile[threadIdx.x][k]);
+  }
+}
+
+// 2-D element-wise conversion with leading dimensions (fp32 -> fp16, bf16 -> fp16).
+template <typename TI, typename TO>
+__global__ void convert_kernel(const TI* __restrict__ src, long long ld_src, TO* __restrict__ dst, long long ld_dst,
+                               int rows, int cols) {
+  const long long total = static_cast<long long>(rows) * cols;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const long long r = i / cols, c = i % cols;
+    float v;
+    if constexpr (std::is_same<TI, float>::value) v = src[r * ld_src + c];
+    else v = __bfloat162float(src[r * ld_src + c]);
+    dst[r * ld_dst + c] = from_float<TO>(v);
+  }
+}
+
+__global__ void rmsnorm_kernel(const bf16* __restrict__ x, long long ld_x, const bf16* __restrict__ w,
+                               bf16* __restrict__ y, long long ld_y, int n, float eps) {
+  const bf16* xr = x + static_cast<long long>(blockIdx.x) * ld_x;
+  bf16* yr = y + static_cast<long long>(blockIdx.x) * ld_y;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = __bfloat162float(xr[i]);
+    ss += v * v;
+  }
+  __shared__ float red[32];
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  const float rstd = rsqrtf(red[0] / static_cast<float>(n) + eps);
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    yr[i] = __float2bfloat16(__bfloat162float(xr[i]) * rstd * __bfloat162float(w[i]));
+}
+
+// One CTA that waits, bounded, on an mbarrier nothing will complete.
+__global__ void wait_probe_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const WaitCtx ctx{&abort_flag, err, limit_ns};
+    mbar_wait(&bar, 0, ctx, SITE_PROBE);
+  }
+}
+
+template <typename TI, typename TO>
+static int launch_convert(const TI* src, int64_t ld_src, TO* dst, int64_t ld_dst, int rows, int cols,
+                          cudaStream_t s) {
+  const int64_t total = static_cast<int64_t>(rows) * cols;
+  const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cdiv(total, 256), 148 * 16)));
+  convert_kernel<TI, TO><<<blocks, 256, 0, s>>>(src, ld_src, dst, ld_dst, rows, cols);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+template <typename TO>
+static int launch_transpose(const void* src, int64_t ld_src, int rows, int cols, void* dst, int64_t ld_dst,
+                            int dst_rows, int dst_cols, cudaStream_t s) {
+  if (!src || !dst || rows <= 0 || cols <= 0 || dst_rows <= 0 || dst_cols <= 0 || ld_src < cols ||
+      ld_dst < dst_cols)
+    return SVDMLP_ERR_INVALID_VALUE;
+  dim3 grid(static_cast<unsigned>(cdiv(dst_cols, 32)), static_cast<unsigned>(cdiv(dst_rows, 32)));
+  transpose_pack_kernel<TO><<<grid, dim3(32, 8), 0, s>>>(static_cast<const bf16*>(src), ld_src, rows, cols,
+                                                         static_cast<TO*>(dst), ld_dst, dst_rows, dst_cols);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+// ------------------------------------------------------------ validation
+static bool aligned16(const void* p, int64_t ld) {
+  return (reinterpret_cast<uintptr_t>(p) & 15u) == 0 && ld % 8 == 0;
+}
+
+static int check_layout(const svdmlp_layout* L) {
+  if (!L || L->d <= 0 || L->ff <= 0) return SVDMLP_ERR_INVALID_VALUE;
+  if (L->kind != SVDMLP_KIND_SVD && L->kind != SVDMLP_KIND_DENSE) return SVDMLP_ERR_INVALID_VALUE;
+  return SVDMLP_OK;
+}
+
+// Brings a bf16 activation matrix to a TMA-legal buffer (16-byte aligned
+// rows), copying it into workspace staging when the caller's stride is not.
+static int stage_in(const void* src, int64_t ld, int rows, int cols, void* staging, int64_t ld_staging,
+                    const void** out, int64_t* out_ld, cudaStream_t s) {
+  if (aligned16(src, ld)) {
+    *out = src;
+    *out_ld = ld;
+    return SVDMLP_OK;
+  }
+  SVD_CUDA(cudaMemcpy2DAsync(staging, ld_staging * 2, src, ld * 2, static_cast<size_t>(cols) * 2, rows,
+                             cudaMemcpyDeviceToDevice, s));
+  *out = staging;
+  *out_ld = ld_staging;
+  return SVDMLP_OK;
+}
+
+static int finish_output(void* target, int64_t ld_target, const void* staged, int64_t ld_staged, int M, int cols,
+                         cudaStream_t s) {
+  if (staged == target) return SVDMLP_OK;
+  SVD_CUDA(cudaMemcpy2DAsync(target, ld_target * 2, staged, ld_staged * 2, static_cast<size_t>(cols) * 2, M,
+                             cudaMemcpyDeviceToDevice, s));
+  return SVDMLP_OK;
+}
+
+// ------------------------------------------------------------------ stages
+// Stage 1 + 2: h = silu(X.u_g.v_g) * (X.u_u.v_u); `h_bf16` selects the
+// caller-facing bf16 output instead of the internal fp16 H.
+static int run_gate_up(const svdmlp_layout* L, const uint8_t* packed, const void* x, int64_t ldx, int M, void* h,
+                       int64_t ldh, bool h_bf16, const Workspace& w, cudaStream_t s) {
+  CUtensorMap a, b, out, a_g, a_u, b_g, b_u, hmap;
+  const int64_t n1 = 2LL * L->rp_gu;
+  SVD_CHECK(operand_map(&a, x, false, L->d, M, ldx, 128));
+  SVD_CHECK(operand_map(&b, packed + L->off_w1, false, L->d, n1, L->ld_d, CfgXU::BN));
+  SVD_CHECK(output_map<CfgXU>(&out, w.xu, n1, M, n1));
+  SVD_CHECK(launch_gemm<CfgXU>(a, a, b, b, out, M, static_cast<int>(n1), L->d, ST_XU, w, nullptr, 0, s));
+  SVD_CHECK(operand_map(&a_g, w.xu, true, L->r_gu, M, n1, 128));
+  SVD_CHECK(operand_map(&a_u, w.xu + L->rp_gu, true, L->r_gu, M, n1, 128));
+  SVD_CHECK(operand_map(&b_g, packed + L->off_vg, true, L->r_gu, L->ff, L->rp_gu, CfgGU::BN));
+  SVD_CHECK(operand_map(&b_u, packed + L->off_vu, true, L->r_gu, L->ff, L->rp_gu, CfgGU::BN));
+  if (h_bf16) {
+    SVD_CHECK(output_map<CfgGUbf>(&hmap, h, L->ff, M, ldh));
+    return launch_gemm<CfgGUbf>(a_g, a_u, b_g, b_u, hmap, M, L->ff, L->r_gu, ST_GATEUP, w, nullptr, 0, s);
+  }
+  SVD_CHECK(output_map<CfgGU>(&hmap, h, L->ff, M, ldh));
+  return launch_gemm<CfgGU>(a_g, a_u, b_g, b_u, hmap, M, L->ff, L->r_gu, ST_GATEUP, w, nullptr, 0, s);
+}
+
+// Stage 3: H . u_down -> T (fp16, workspace) or an fp32 partial.  `h_f16`
+// says whether H is fp16 (it must then match an fp16 ud) or bf16 (bf16 ud).
+static int run_down_u(const svdmlp_layout* L, const uint8_t* packed, const void* h, int64_t ldh, bool h_f16, int M,
+                      float* partial, int64_t ldp, const Workspace& w, cudaStream_t s) {
+  CUtensorMap a, b, out;
+  SVD_CHECK(operand_map(&a, h, h_f16, L->ff, M, ldh, 128));
+  SVD_CHECK(operand_map(&b, packed + L->off_ud, h_f16, L->ff, L->r_d, L->ld_ff, CfgDU::BN));
+  if (partial) {
+    if (!h_f16) return SVDMLP_ERR_DTYPE;
+    SVD_CHECK(output_map<CfgDUf32>(&out, partial, L->r_d, M, ldp));
+    return launch_gemm<CfgDUf32>(a, a, b, b, out, M, L->r_d, L->ff, ST_DOWN_U, w, nullptr, 0, s);
+  }
+  if (h_f16) {
+    SVD_CHECK(output_map<CfgDU>(&out, w.t, L->r_d, M, L->rp_d));
+    return launch_gemm<CfgDU>(a, a, b, b, out, M, L->r_d, L->ff, ST_DOWN_U, w, nullptr, 0, s);
+  }
+  SVD_CHECK(output_map<CfgDUbf>(&out, w.t, L->r_d, M, L->rp_d));
+  return launch_gemm<CfgDUbf>(a, a, b, b, out, M, L->r_d, L->ff, ST_DOWN_U, w, nullptr, 0, s);
+}
+
+// Stage 4: T . v_down (+ residual) -> y (bf16)
+static int run_down_v(const svdmlp_layout* L, const uint8_t* packed, int M, void* y, int64_t ldy,
+                      const void* residual, int64_t ld_res, const Workspace& w, cudaStream_t s) {
+  CUtensorMap a, b, out;
+  SVD_CHECK(operand_map(&a, w.t, true, L->r_d, M, L->rp_d, 128));
+  SVD_CHECK(operand_map(&b, packed + L->off_vd, true, L->r_d, L->d, L->rp_d, CfgDV::BN));
+  SVD_CHECK(output_map<CfgDV>(&out, y, L->d, M, ldy));
+  if (residual)
+    return launch_gemm<CfgDVres>(a, a, b, b, out, M, L->d, L->r_d, ST_DOWN_V, w, static_cast<const bf16*>(residual),
+                                 ld_res, s);
+  return launch_gemm<CfgDV>(a, a, b, b, out, M, L->d, L->r_d, ST_DOWN_V, w, nullptr, 0, s);
+}
+
+// Output target: the caller's buffer when TMA-legal, else workspace staging.
+struct OutTarget {
+  void* ptr;
+  int64_t ld;
+};
+static OutTarget out_target(void* y, int64_t ldy, void* staging, int64_t ld_staging) {
+  if (aligned16(y, ldy)) return {y, ldy};
+  return {staging, ld_staging};
+}
+
+}  // namespace svdmlp
+
+using namespace svdmlp;
+
+// =================================================================== C ABI
+extern "C" {
+
+const char* svdmlp_status_string(int status) {
+  switch (status) {
+    case SVDMLP_OK: return "ok";
+    case SVDMLP_ERR_INVALID_VALUE: return "invalid value: sizes must be positive integers and pointers non-null";
+    case SVDMLP_ERR_SHAPE_MISMATCH: return "shape mismatch: contraction dimensions do not match";
+    case SVDMLP_ERR_ALIGNMENT: return "alignment: pointers and leading dimensions must be 16-byte aligned";
+    case SVDMLP_ERR_DTYPE: return "unsupported dtype: inputs must all be bfloat16";
+    case SVDMLP_ERR_WORKSPACE: return "workspace too small";
+    case SVDMLP_ERR_DEVICE_TIMEOUT: return "device-side wait exceeded its limit";
+    case SVDMLP_ERR_CUDA: return "CUDA error";
+    case SVDMLP_ERR_BUDGET: return "SMEM/TMEM budget exceeds the device";
+    case SVDMLP_ERR_DEVICE: return "device is not an sm_100 (B200) GPU";
+    default: return "unknown status";
+  }
+}
+
+int svdmlp_last_cuda_error(void) { return g_last_cuda_error; }
+
+int64_t svdmlp_launch_count(void) { return g_launches.load(); }
+
+int svdmlp_layout_init(svdmlp_layout* L, int d, int ff, int r_gu, int r_d) {
+  if (!L || d <= 0 || ff <= 0 || r_gu < 0 || r_d < 0 || (r_gu == 0 && r_d == 0)) return SVDMLP_ERR_INVALID_VALUE;
+  std::memset(L, 0, sizeof(*L));
+  L->kind = SVDMLP_KIND_SVD;
+  L->d = d;
+  L->ff = ff;
+  L->r_gu = r_gu;
+  L->r_d = r_d;
+  L->rp_gu = static_cast<int32_t>(round_up(r_gu, 8));
+  L->rp_d = static_cast<int32_t>(round_up(r_d, 8));
+  L->ld_d = static_cast<int32_t>(round_up(d, 8));
+  L->ld_ff = static_cast<int32_t>(round_up(ff, 8));
+  L->ud_f16 = r_gu > 0 ? 1 : 0;
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t o = off;
+    off += round_up(bytes, 256);
+    return o;
+  };
+  L->off_w1 = take(2LL * L->rp_gu * L->ld_d * 2);
+  L->off_vg = take(static_cast<int64_t>(ff) * L->rp_gu * 2);
+  L->off_vu = take(static_cast<int64_t>(ff) * L->rp_gu * 2);
+  L->off_ud = take(static_cast<int64_t>(L->rp_d) * L->ld_ff * 2);
+  L->off_vd = take(static_cast<int64_t>(d) * L->rp_d * 2);
+  L->packed_bytes = off;
+  return SVDMLP_OK;
+}
+
+int svdmlp_dense_layout_init(svdmlp_layout* L, int d, int ff) {
+  if (!L || d <= 0 || ff <= 0) return SVDMLP_ERR_INVALID_VALUE;
+  std::memset(L, 0, sizeof(*L));
+  L->kind = SVDMLP_KIND_DENSE;
+  L->d = d;
+  L->ff = ff;
+  L->ld_d = static_cast<int32_t>(round_up(d, 8));
+  L->ld_ff = static_cast<int32_t>(round_up(ff, 8));
+  L->ud_f16 = 1;
+  int64_t off = 0;
+  auto take = [&](int64_t bytes) {
+    const int64_t o = off;
+    off += round_up(bytes, 256);
+    return o;
+  };
+  L->off_vg = take(static_cast<int64_t>(ff) * L->ld_d * 2);
+  L->off_vu = take(static_cast<int64_t>(ff) * L->ld_d * 2);
+  L->off_ud = take(static_cast<int64_t>(d) * L->ld_ff * 2);
+  L->packed_bytes = off;
+  return SVDMLP_OK;
+}
+
+int svdmlp_transpose_pack(const void* src, int64_t ld_src, int rows, int cols, void* dst, int64_t ld_dst,
+                          int dst_rows, int dst_cols, void* stream) {
+  return launch_transpose<bf16>(src, ld_src, rows, cols, dst, ld_dst, dst_rows, dst_cols,
+                                static_cast<cudaStream_t>(stream));
+}
+
+int svdmlp_pack(const svdmlp_layout* L, const void* u_gate, int64_t ld_ug, const void* v_gate, int64_t ld_vg,
+                const void* u_up, int64_t ld_uu, const void* v_up, int64_t ld_vu, const void* u_down, int64_t ld_ud,
+                const void* v_down, int64_t ld_vd, void* packed, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || !packed) return SVDMLP_ERR_INVALID_VALUE;
+  if ((reinterpret_cast<uintptr_t>(packed) & 255u) != 0) return SVDMLP_ERR_ALIGNMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* P = static_cast<uint8_t*>(packed);
+  SVD_CUDA(cudaMemsetAsync(P, 0, static_cast<size_t>(L->packed_bytes), s));
+  if (L->r_gu > 0) {
+    if (!u_gate || !v_gate || !u_up || !v_up) return SVDMLP_ERR_INVALID_VALUE;
+    bf16* w1 = reinterpret_cast<bf16*>(P + L->off_w1);
+    // u [d, r] -> rows of w1 = u^T (bf16: it multiplies the bf16 input X)
+    SVD_CHECK(launch_transpose<bf16>(u_gate, ld_ug, L->d, L->r_gu, w1, L->ld_d, L->rp_gu, L->d, s));
+    SVD_CHECK(launch_transpose<bf16>(u_up, ld_uu, L->d, L->r_gu, w1 + static_cast<int64_t>(L->rp_gu) * L->ld_d,
+                                     L->ld_d, L->rp_gu, L->d, s));
+    // v [r, ff] -> v^T [ff, rp] (fp16: it multiplies the fp16 XU)
+    SVD_CHECK(launch_transpose<__half>(v_gate, ld_vg, L->r_gu, L->ff, P + L->off_vg, L->rp_gu, L->ff, L->rp_gu, s));
+    SVD_CHECK(launch_transpose<__half>(v_up, ld_vu, L->r_gu, L->ff, P + L->off_vu, L->rp_gu, L->ff, L->rp_gu, s));
+  }
+  if (L->r_d > 0) {
+    if (!u_down || !v_down) return SVDMLP_ERR_INVALID_VALUE;
+    // u_down [ff, r_d] -> [rp_d, ld_ff];  v_down [r_d, d] -> [d, rp_d]
+    if (L->ud_f16)
+      SVD_CHECK(launch_transpose<__half>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, L->ld_ff, L->rp_d, L->ff, s));
+    else
+      SVD_CHECK(launch_transpose<bf16>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, L->ld_ff, L->rp_d, L->ff, s));
+    SVD_CHECK(launch_transpose<__half>(v_down, ld_vd, L->r_d, L->d, P + L->off_vd, L->rp_d, L->d, L->rp_d, s));
+  }
+  return SVDMLP_OK;
+}
+
+int svdmlp_dense_pack(const svdmlp_layout* L, const void* w_gate, int64_t ld_wg, const void* w_up, int64_t ld_wu,
+                      const void* w_down, int64_t ld_wd, void* packed, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_DENSE || !packed || !w_gate || !w_up || !w_down) return SVDMLP_ERR_INVALID_VALUE;
+  if ((reinterpret_cast<uintptr_t>(packed) & 255u) != 0) return SVDMLP_ERR_ALIGNMENT;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* P = static_cast<uint8_t*>(packed);
+  SVD_CUDA(cudaMemsetAsync(P, 0, static_cast<size_t>(L->packed_bytes), s));
+  SVD_CHECK(launch_transpose<bf16>(w_gate, ld_wg, L->d, L->ff, P + L->off_vg, L->ld_d, L->ff, L->d, s));
+  SVD_CHECK(launch_transpose<bf16>(w_up, ld_wu, L->d, L->ff, P + L->off_vu, L->ld_d, L->ff, L->d, s));
+  SVD_CHECK(launch_transpose<__half>(w_down, ld_wd, L->ff, L->d, P + L->off_ud, L->ld_ff, L->d, L->ff, s));
+  return SVDMLP_OK;
+}
+
+int64_t svdmlp_workspace_bytes(const svdmlp_layout* L, int max_m) {
+  if (check_layout(L) != SVDMLP_OK || max_m <= 0) return SVDMLP_ERR_INVALID_VALUE;
+  return ws_bytes_for(L, max_m, planning_sms());
+}
+
+int svdmlp_workspace_init(void* ws, int64_t ws_bytes, void* stream) {
+  if (!ws || ws_bytes < kCtlBytes) return SVDMLP_ERR_INVALID_VALUE;
+  // The control block and the split-K counters sit at the front.
+  const int64_t n = std::min<int64_t>(ws_bytes, kCtlBytes + (4 << 20));
+  SVD_CUDA(cudaMemsetAsync(ws, 0, static_cast<size_t>(n), static_cast<cudaStream_t>(stream)));
+  return SVDMLP_OK;
+}
+
+int svdmlp_check_device_status(void* ws, int64_t ws_bytes, void* stream) {
+  if (!ws || ws_bytes < kCtlBytes) return SVDMLP_ERR_INVALID_VALUE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SVD_CUDA(cudaStreamSynchronize(s));
+  int err = 0;
+  SVD_CUDA(cudaMemcpy(&err, ws, sizeof(int), cudaMemcpyDeviceToHost));
+  if (err != 0) {
+    SVD_CHECK(svdmlp_workspace_init(ws, ws_bytes, stream));
+    SVD_CUDA(cudaStreamSynchronize(s));
+    return SVDMLP_ERR_DEVICE_TIMEOUT;
+  }
+  return SVDMLP_OK;
+}
+
+int svdmlp_gate_up(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* h,
+                   int64_t ldh, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || !packed || !x || !h || M <= 0 || ldx < L->d || ldh < L->ff)
+    return SVDMLP_ERR_INVALID_VALUE;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const void* xa;
+  int64_t ldxa;
+  SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
+  const OutTarget ht = out_target(h, ldh, w.h, L->ld_ff);
+  SVD_CHECK(run_gate_up(L, static_cast<const uint8_t*>(packed), xa, ldxa, M, ht.ptr, ht.ld, true, w, s));
+  return finish_output(h, ldh, ht.ptr, ht.ld, M, L->ff, s);
+}
+
+// Caller-facing bf16 H into the form the layout's ud expects.
+static int stage_h(const svdmlp_layout* L, const void* h, int64_t ldh, int M, const Workspace& w, const void** ha,
+                   int64_t* ldha, cudaStream_t s) {
+  if (L->ud_f16) {
+    SVD_CHECK(launch_convert<bf16, __half>(static_cast<const bf16*>(h), ldh, w.h, L->ld_ff, M, L->ff, s));
+    *ha = w.h;
+    *ldha = L->ld_ff;
+    return SVDMLP_OK;
+  }
+  return stage_in(h, ldh, M, L->ff, w.h, L->ld_ff, ha, ldha, s);
+}
+
+int svdmlp_xuv(const svdmlp_layout* L, const void* packed, const void* h, int64_t ldh, int M, void* y,
+               int64_t ldy, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_d <= 0 || !packed || !h || !y || M <= 0 || ldh < L->ff || ldy < L->d)
+    return SVDMLP_ERR_INVALID_VALUE;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const void* ha;
+  int64_t ldha;
+  SVD_CHECK(stage_h(L, h, ldh, M, w, &ha, &ldha, s));
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  SVD_CHECK(run_down_u(L, P, ha, ldha, L->ud_f16 != 0, M, nullptr, 0, w, s));
+  const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
+  SVD_CHECK(run_down_v(L, P, M, yt.ptr, yt.ld, nullptr, 0, w, s));
+  return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
+}
+
+int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* y,
+                   int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || L->r_d <= 0 || !packed || !x || !y || M <= 0 ||
+      ldx < L->d || ldy < L->d || (residual && ld_res < L->d))
+    return SVDMLP_ERR_INVALID_VALUE;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  const void* xa;
+  int64_t ldxa;
+  SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
+  SVD_CHECK(run_gate_up(L, P, xa, ldxa, M, w.h, L->ld_ff, false, w, s));
+  SVD_CHECK(run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, 0, w, s));
+  const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
+  const void* res = nullptr;
+  int64_t ldr = 0;
+  // An unaligned residual is staged in the x staging buffer once x is consumed.
+  if (residual) SVD_CHECK(stage_in(residual, ld_res, M, L->d, w.xs, L->ld_d, &res, &ldr, s));
+  SVD_CHECK(run_down_v(L, P, M, yt.ptr, yt.ld, res, ldr, w, s));
+  return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
+}
+
+int svdmlp_dense_forward(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* y,
+                         int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes,
+                         void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_DENSE || !packed || !x || !y || M <= 0 || ldx < L->d || ldy < L->d ||
+      (residual && ld_res < L->d))
+    return SVDMLP_ERR_INVALID_VALUE;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  const void* xa;
+  int64_t ldxa;
+  SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
+  CUtensorMap a, b_g, b_u, hmap;
+  SVD_CHECK(operand_map(&a, xa, false, L->d, M, ldxa, 128));
+  SVD_CHECK(operand_map(&b_g, P + L->off_vg, false, L->d, L->ff, L->ld_d, CfgDenseGU::BN));
+  SVD_CHECK(operand_map(&b_u, P + L->off_vu, false, L->d, L->ff, L->ld_d, CfgDenseGU::BN));
+  SVD_CHECK(output_map<CfgDenseGU>(&hmap, w.h, L->ff, M, L->ld_ff));
+  SVD_CHECK(launch_gemm<CfgDenseGU>(a, a, b_g, b_u, hmap, M, L->ff, L->d, ST_DENSE_GU, w, nullptr, 0, s));
+  const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
+  const void* res = nullptr;
+  int64_t ldr = 0;
+  if (residual) SVD_CHECK(stage_in(residual, ld_res, M, L->d, w.xs, L->ld_d, &res, &ldr, s));
+  CUtensorMap ha, bd, out;
+  SVD_CHECK(operand_map(&ha, w.h, true, L->ff, M, L->ld_ff, 128));
+  SVD_CHECK(operand_map(&bd, P + L->off_ud, true, L->ff, L->d, L->ld_ff, CfgDV::BN));
+  SVD_CHECK(output_map<CfgDV>(&out, yt.ptr, L->d, M, yt.ld));
+  if (res)
+    SVD_CHECK(launch_gemm<CfgDVres>(ha, ha, bd, bd, out, M, L->d, L->ff, ST_DENSE_D, w,
+                                    static_cast<const bf16*>(res), ldr, s));
+  else
+    SVD_CHECK(launch_gemm<CfgDV>(ha, ha, bd, bd, out, M, L->d, L->ff, ST_DENSE_D, w, nullptr, 0, s));
+  return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
+}
+
+int svdmlp_forward_partial(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M,
+                           float* partial, int64_t ldp, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || L->r_d <= 0 || !packed || !x || !partial || M <= 0 ||
+      ldx < L->d || ldp < L->r_d)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if ((reinterpret_cast<uintptr_t>(partial) & 15u) != 0 || ldp % 4 != 0) return SVDMLP_ERR_ALIGNMENT;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  const void* xa;
+  int64_t ldxa;
+  SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
+  SVD_CHECK(run_gate_up(L, P, xa, ldxa, M, w.h, L->ld_ff, false, w, s));
+  return run_down_u(L, P, w.h, L->ld_ff, true, M, partial, ldp, w, s);
+}
+
+int svdmlp_down_partial(const svdmlp_layout* L, const void* packed, const void* h, int64_t ldh, int M,
+                        float* partial, int64_t ldp, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_d <= 0 || !packed || !h || !partial || M <= 0 || ldh < L->ff ||
+      ldp < L->r_d)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if (!L->ud_f16) return SVDMLP_ERR_DTYPE;
+  if ((reinterpret_cast<uintptr_t>(partial) & 15u) != 0 || ldp % 4 != 0) return SVDMLP_ERR_ALIGNMENT;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const void* ha;
+  int64_t ldha;
+  SVD_CHECK(stage_h(L, h, ldh, M, w, &ha, &ldha, s));
+  return run_down_u(L, static_cast<const uint8_t*>(packed), ha, ldha, true, M, partial, ldp, w, s);
+}
+
+int svdmlp_down_finish(const svdmlp_layout* L, const void* packed, const float* partial, int64_t ldp, int M,
+                       void* y, int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes,
+                       void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_d <= 0 || !packed || !partial || !y || M <= 0 || ldp < L->r_d ||
+      ldy < L->d || (residual && ld_res < L->d))
+    return SVDMLP_ERR_INVALID_VALUE;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SVD_CHECK(launch_convert<float, __half>(partial, ldp, w.t, L->rp_d, M, L->r_d, s));
+  const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
+  const void* res = nullptr;
+  int64_t ldr = 0;
+  if (residual) SVD_CHECK(stage_in(residual, ld_res, M, L->d, w.xs, L->ld_d, &res, &ldr, s));
+  SVD_CHECK(run_down_v(L, static_cast<const uint8_t*>(packed), M, yt.ptr, yt.ld, res, ldr, w, s));
+  return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
+}
+
+int64_t svdmlp_gemm_workspace_bytes(int M, int N, int K) {
+  if (M <= 0 || N <= 0 || K <= 0) return SVDMLP_ERR_INVALID_VALUE;
+  const Plan pl = plan_gemm(M, N, K, CfgGemm::BN, planning_sms(), g_split_override[ST_GEMM]);
+  return kCtlBytes + round_up(static_cast<int64_t>(pl.m_tiles) * pl.n_tiles * 4, 256) +
+         round_up(partial_bytes(pl, CfgGemm::BN, 1), 256);
+}
+
+int svdmlp_gemm(const void* a, int64_t lda, const void* bt, int64_t ldb, void* c, int64_t ldc, int M, int N, int K,
+                void* ws, int64_t ws_bytes, void* stream) {
+  if (!a || !bt || !c || M <= 0 || N <= 0 || K <= 0 || lda < K || ldb < K || ldc < N) return SVDMLP_ERR_INVALID_VALUE;
+  if (!aligned16(a, lda) || !aligned16(bt, ldb) || !aligned16(c, ldc)) return SVDMLP_ERR_ALIGNMENT;
+  if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return SVDMLP_ERR_INVALID_VALUE;
+  const int sms = planning_sms();
+  const Plan pl = plan_gemm(M, N, K, CfgGemm::BN, sms, g_split_override[ST_GEMM]);
+  const int64_t cnt = round_up(static_cast<int64_t>(pl.m_tiles) * pl.n_tiles * 4, 256);
+  if (ws_bytes < svdmlp_gemm_workspace_bytes(M, N, K)) return SVDMLP_ERR_WORKSPACE;
+  Workspace w{};
+  uint8_t* p = static_cast<uint8_t*>(ws);
+  w.err = reinterpret_cast<int*>(p);
+  w.counters = reinterpret_cast<int*>(p + kCtlBytes);
+  w.partials = reinterpret_cast<float*>(p + kCtlBytes + cnt);
+  w.partial_cap = ws_bytes - kCtlBytes - cnt;
+  CUtensorMap am, bm, cm;
+  SVD_CHECK(operand_map(&am, a, false, K, M, lda, 128));
+  SVD_CHECK(operand_map(&bm, bt, false, K, N, ldb, CfgGemm::BN));
+  SVD_CHECK(output_map<CfgGemm>(&cm, c, N, M, ldc));
+  return launch_gemm<CfgGemm>(am, am, bm, bm, cm, M, N, K, ST_GEMM, w, nullptr, 0,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int svdmlp_rmsnorm(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy, int M, int n, float eps,
+                   void* stream) {
+  if (!x || !w || !y || M <= 0 || n <= 0 || ldx < n || ldy < n || !(eps >= 0.f)) return SVDMLP_ERR_INVALID_VALUE;
+  rmsnorm_kernel<<<static_cast<unsigned>(M), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const bf16*>(x), ldx, static_cast<const bf16*>(w), static_cast<bf16*>(y), ldy, n, eps);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+int svdmlp_debug_wait_timeout(void* ws, int64_t ws_bytes, int64_t limit_ns, void* stream) {
+  if (!ws || ws_bytes < kCtlBytes || limit_ns <= 0) return SVDMLP_ERR_INVALID_VALUE;
+  wait_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<int*>(ws),
+                                                                      static_cast<unsigned long long>(limit_ns));
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+int svdmlp_set_split_override(int stage, int splits) {
+  if (stage < 0 || stage >= 8 || splits < 0 || splits > 64) return SVDMLP_ERR_INVALID_VALUE;
+  g_split_override[stage] = splits;
+  return SVDMLP_OK;
+}
+
+int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
+  if (!out6 || M <= 0 || N <= 0 || K <= 0 || stage < 0 || stage >= 8) return SVDMLP_ERR_INVALID_VALUE;
+  const int bn = (stage == ST_GATEUP || stage == ST_DENSE_GU) ? 128 : 256;
+  const Plan p = plan_gemm(M, N, K, bn, planning_sms(), g_split_override[stage]);
+  out6[0] = p.m_tiles;
+  out6[1] = p.n_tiles;
+  out6[2] = p.k_blocks;
+  out6[3] = p.splits;
+  out6[4] = p.units;
+  out6[5] = p.grid;
+  return SVDMLP_OK;
+}
+
+}  // extern "C"
