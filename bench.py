@@ -1,0 +1,408 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 SVD-MLP hot path (one JSON line on rank 0).
+
+Default workload (N=1): BASELINE config 1, one Llama-3-8B SVD-compressed MLP
+layer, d=4096, ff=14336, ratio 0.9 -> r=2867, 1024 tokens, bf16 inputs,
+synthetic seeded factors (u ~ N(0,1/in), v ~ N(0,1/r), x ~ N(0,1)).
+A step is one full layer forward (gate/up + down: 4 GEMM launches).
+
+N>1 (torchrun, one rank per GPU): the same layer tensor-parallel over ff
+(strong scaling): v_gate/v_up column-sharded, u_down row-sharded, one NCCL
+all-reduce of the fp32 [M, r] partial per step.
+
+--impl reference: the reference's CPU path (the NumPy oracle restatement of
+kernels/reference.py) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+for _p in (ROOT / "neuronmlp-on-tpu_b200", ROOT / "oracle"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "SVD-MLP µs/layer & TFLOP/s (Llama-3-8B, seq 1024); tokens/s at 1/2/4/8 B200"
+
+WORKLOADS = {
+    # BASELINE config 1 (the metric's configuration)
+    "llama3-8b-layer": dict(d=4096, ff=14336, ratio=0.9, tokens=1024),
+    # BASELINE config 2 (decode regime), M = 1
+    "llama3-8b-decode": dict(d=4096, ff=14336, ratio=0.9, tokens=1),
+    # BASELINE config 4 (70B layer)
+    "llama3-70b-layer": dict(d=8192, ff=28672, ratio=0.8, tokens=4096),
+}
+
+
+def rank_for(d, ff, ratio):
+    return int(ratio * d * ff // (d + ff))
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        j = json.loads(p.read_text())
+        return j, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the run."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, uuid: str | None, period_ms: int = 100):
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", f"-lms={period_ms}"]
+        if uuid:
+            cmd.insert(1, f"-i={uuid}")
+        self.lines: list[str] = []
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        sm, mx, power = [], [], []
+        reasons = set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "power_w_max": max(power) if power else None,
+            "reasons": sorted(reasons),
+            "samples": len(sm),
+        }
+
+
+# ------------------------------------------------------------- CPU oracle
+def cpu_baseline(wl: dict, reps: int, warmup: int = 1, rows: int | None = None) -> dict:
+    """Times the reference CPU path (oracle restatement of kernels/reference.py,
+    NumPy fp32 on OpenBLAS) on the host cores; tokens/s."""
+    import numpy as np
+
+    import svdmlp_oracle as orc
+    try:
+        from threadpoolctl import threadpool_info
+        threads = max([i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"] or [1])
+    except Exception:  # noqa: BLE001
+        threads = os.cpu_count() or 1
+    d, ff, m = wl["d"], wl["ff"], wl["tokens"]
+    r = rank_for(d, ff, wl["ratio"])
+    m_s = min(m, rows) if rows else m
+    x, f = orc.make_inputs(1, m_s, d, ff, r)
+    for _ in range(warmup):
+        orc.svd_mlp(x, *f)
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        orc.svd_mlp(x, *f)
+        times.append(time.perf_counter() - t0)
+    med = statistics.median(times)
+    return {
+        "value": m_s / med,
+        "unit": "tokens/s",
+        "cores": int(threads),
+        "kind": "port",
+        "sample": f"{m_s} tokens x 1 layer (d={d}, ff={ff}, r={r}) fp32 NumPy/OpenBLAS, median of {reps} after {warmup} warm-up",
+        "seconds_per_sample": med,
+        "cpu_count": os.cpu_count(),
+    }
+
+
+def run_reference_arm(args, wl) -> None:
+    """--impl reference: the reference CPU implementation of the path."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    d, ff, m = wl["d"], wl["ff"], wl["tokens"]
+    r = rank_for(d, ff, wl["ratio"])
+    # bounded sample per step: the full layer for the 8B workloads, a row
+    # sample for the 70B layer (same per-token work, fewer tokens)
+    rows = m if d * ff <= 4096 * 14336 else 256
+    base = cpu_baseline(wl, reps=max(1, args.steps), warmup=max(0, min(args.warmup, 3)), rows=rows)
+    line = {
+        "metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": base["seconds_per_sample"] * 1e3, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": args.workload, "d": d, "ff": ff, "r": r, "tokens": m, "ratio": wl["ratio"],
+                   "parallelism": "cpu"},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------- GPU arm
+def make_factors(d, ff, r, seed, device):
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+
+    def mat(rows, cols):
+        return (torch.randn(rows, cols, generator=g, device=device) / math.sqrt(rows)).to(torch.bfloat16)
+
+    return mat(d, r), mat(r, ff), mat(d, r), mat(r, ff), mat(ff, r), mat(r, d)
+
+
+def parity_sample(x, factors, y, nrows=16):
+    """rel-Frobenius and max-abs/RMS of sampled output rows against the oracle."""
+    import numpy as np
+
+    import svdmlp_oracle as orc
+    m = x.shape[0]
+    rows = np.unique(np.linspace(0, m - 1, min(nrows, m)).astype(np.int64))
+    xs = x[rows].float().cpu().numpy()
+    f = [t.float().cpu().numpy() for t in factors]
+    ref = orc.svd_mlp(xs, *f)
+    return orc.error_metrics(y[rows].float().cpu().numpy(), ref)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3-8b-layer")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-reps", type=int, default=3)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    wl = WORKLOADS[args.workload]
+    if args.impl == "reference":
+        run_reference_arm(args, wl)
+        return
+
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    from svdflash_b200 import _build, _lib
+    from svdflash_b200.kernels import ops
+    from svdflash_b200.tp import TensorParallelSvdMlp
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    if _build.is_stale() and rank == 0 and world == 1:
+        _build.build()
+    lib = _lib.load()
+
+    d, ff, m = wl["d"], wl["ff"], wl["tokens"]
+    r = rank_for(d, ff, wl["ratio"])
+    flops_layer = 6.0 * m * r * (d + ff)
+    factors = make_factors(d, ff, r, args.seed, dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(args.seed + 1)
+    x = torch.randn(m, d, generator=g, device=dev).to(torch.bfloat16)
+
+    if world == 1:
+        layer = ops.pack_svd_layer(*factors)
+        y = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
+
+        def step(inp, out=y):
+            return ops.svd_mlp_packed(layer, inp, out=out)
+    else:
+        tp = TensorParallelSvdMlp(*factors, rank=rank, world=world)
+        y = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
+
+        def step(inp, out=y):
+            return tp.forward(inp, out=out)
+
+    # correctness spot check against the oracle (rank 0)
+    step(x)
+    torch.cuda.synchronize()
+    parity = parity_sample(x, factors, y) if rank == 0 else None
+    weight_bytes = sum(t.numel() for t in factors) * 2
+    del factors
+    torch.cuda.empty_cache()
+
+    uuid = None
+    try:
+        uuid = str(torch.cuda.get_device_properties(dev).uuid)
+        if uuid and not uuid.startswith("GPU-"):
+            uuid = "GPU-" + uuid
+    except Exception:  # noqa: BLE001
+        uuid = None
+    sampler = ClockSampler(uuid) if local == 0 or world == 1 else None
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    launches0 = int(lib.svdmlp_launch_count())
+    stream = torch.cuda.current_stream(dev)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step(x)
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = int(lib.svdmlp_launch_count()) - launches0
+    elapsed_ms = ev0.elapsed_time(ev1)
+    t = torch.tensor([elapsed_ms], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    barrier()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms_per_step = float(t.item()) / args.steps
+
+    # ---- end to end through the public API: pinned host in, host out
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty(m, d, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+    e2e_steps = max(10, min(args.steps, 200))
+    for _ in range(3):
+        x_dev.copy_(x_host, non_blocking=True)
+        step(x_dev)
+        y_host.copy_(y, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        step(x_dev)
+        y_host.copy_(y, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item()) / e2e_steps
+
+    # ---- per-stage kernel durations (events around each launch, separate pass)
+    lib.svdmlp_stage_timing(1)
+    prof_steps = 50
+    for _ in range(prof_steps):
+        step(x)
+    torch.cuda.synchronize()
+    ms_arr = (ctypes.c_double * 8)()
+    cnt_arr = (ctypes.c_int64 * 8)()
+    lib.svdmlp_stage_times(ms_arr, cnt_arr, 8)
+    lib.svdmlp_stage_timing(0)
+    stage_us = {}
+    names = {0: "xu", 1: "gate_up", 2: "down_u", 3: "down_v"}
+    for i, nm in names.items():
+        if cnt_arr[i]:
+            stage_us[nm] = 1e3 * ms_arr[i] / cnt_arr[i]
+    r_loc = r
+    ff_loc = ff // world
+    stage_flops = {"xu": 4.0 * m * d * r_loc, "gate_up": 4.0 * m * r_loc * ff_loc, "down_u": 2.0 * m * ff_loc * r_loc,
+                   "down_v": 2.0 * m * r_loc * d}
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks, peak_src = load_peaks()
+    dominant = max(stage_us, key=stage_us.get) if stage_us else None
+    roofline = None
+    if dominant:
+        achieved = stage_flops[dominant] / (stage_us[dominant] * 1e-6) / 1e12
+        peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+        traffic = None
+        tfile = ROOT / "profiles" / "traffic_per_launch.json"
+        if tfile.exists():
+            traffic = json.loads(tfile.read_text()).get(f"{args.workload}/{dominant}")
+        roofline = {"bound": "tensor", "kernel": f"{dominant} ({'dual SwiGLU' if dominant == 'gate_up' else 'plain'} tcgen05 GEMM)",
+                    "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                    "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long run)",
+                    "traffic": traffic,
+                    "algorithmic_flops_per_launch": stage_flops[dominant]}
+    tokens_per_s = m / (ms_per_step * 1e-3)
+    line = {
+        "metric": METRIC,
+        "value": tokens_per_s,
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": args.workload, "d": d, "ff": ff, "r": r, "tokens": m, "ratio": wl["ratio"],
+                   "parallelism": f"tp-ff{world}" if world > 1 else "single-gpu",
+                   "l2": f"inputs larger than L2: {weight_bytes / 1e6:.0f} MB of factors streamed per step"},
+        "us_per_layer": ms_per_step * 1e3,
+        "tflops": flops_layer / (ms_per_step * 1e-3) / 1e12,
+        "stage_us": stage_us,
+        "roofline": roofline,
+        "e2e": {"value": m / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": m * d * 2,
+                "d2h_bytes_per_step": m * d * 2, "ms_per_step": e2e_ms},
+        "gpu_launches": launches,
+        "clocks": clocks,
+        "parity_sample": parity,
+    }
+    if not args.no_cpu_baseline and world == 1:
+        line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, reps=args.cpu_reps).items()
+                                if k in ("value", "unit", "cores", "kind", "sample")}
+    print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

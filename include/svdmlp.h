@@ -235,6 +235,15 @@ int svdmlp_debug_wait_timeout(void* workspace, int64_t workspace_bytes, int64_t 
 int svdmlp_set_split_override(int stage, int splits);
 int svdmlp_plan_info(int stage, int m, int n, int k, int* out6);
 
+/*
+ * Per-stage timing for profiling passes: with timing enabled every GEMM launch
+ * is bracketed by CUDA events on its stream (which serialises it with its
+ * neighbours); svdmlp_stage_times() waits for them and returns, per stage id,
+ * the summed milliseconds and launch counts, then resets.  Off by default.
+ */
+int svdmlp_stage_timing(int enable);
+int svdmlp_stage_times(double* ms_out, int64_t* counts_out, int n);
+
 /* Number of kernel launches the library has enqueued since load (all entry points). */
 int64_t svdmlp_launch_count(void);
 

@@ -1,6 +1,6 @@
 // Persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
-//   C[M, N] = epilogue( A[M, K] . B[N, K]^T )        (both operands K-major, bf16)
+//   C[M, N] = epilogue( A[M, K] . B[N, K]^T )        (both operands K-major)
 //
 // Dual form (NB == 2): two accumulators per tile, C = silu(A.Bg^T) * (A2.Bu^T);
 // this is the fused low-rank gate/up operator's second stage (the SwiGLU
@@ -12,21 +12,32 @@
 // tensor-core rate, which keeps the layer well inside the max-abs error bound
 // that bf16 intermediates overshoot.
 //
-// Roles (192 threads, one CTA per SM):
+// Roles (192 threads per CTA, one CTA per SM):
 //   warps 0-3  epilogue: TMEM -> registers -> (math) -> swizzled smem -> TMA store
 //   warp  4    TMA producer: STAGES-deep smem ring of 128B-swizzled K-major tiles
 //   warp  5    TMEM allocator + single-thread tcgen05.mma issuer
 // Accumulators are double-buffered in TMEM so the epilogue of one tile
 // overlaps the main loop of the next.
 //
+// CTAS == 2 (a cluster of two CTAs on two SMs): a tile is 256 x BN; each CTA
+// loads its own 128 rows of A and half (BN/2 rows) of B, and the even CTA
+// issues tcgen05.mma.cta_group::2, which reads both CTAs' shared memory and
+// writes each CTA's 128 accumulator rows into its own TMEM.  Each SM thus
+// streams half of the B tile, halving the shared-memory and L2 traffic per
+// FLOP against a one-SM 128 x BN tile.  Loads of both CTAs complete on the
+// even CTA's `full` barrier; MMA commits arrive on the `empty` / `acc_full`
+// barriers of both CTAs; both epilogues release the accumulator on the even
+// CTA's `acc_empty` barrier.
+//
 // Work units are (m_tile, split, n_tile) with m fastest: the CTAs that run at
 // the same time share the same weight (B) tile, so each weight tile is read
 // from HBM once and served from L2 to the other M-tiles.
 //
-// Split-K: every split writes an fp32 partial tile to the workspace and bumps
-// a per-tile counter; the split that arrives last sums all partials in split
-// order (deterministic) and runs the epilogue.  Nothing ever waits on another
-// CTA, so split-K cannot deadlock.  The last split resets the counter.
+// Split-K (one-CTA configurations only): every split writes an fp32 partial
+// tile (its valid rows) to the workspace and bumps a per-tile counter; the
+// split that arrives last sums all partials in split order (deterministic) and
+// runs the epilogue.  Nothing ever waits on another CTA, so split-K cannot
+// deadlock.  The last split resets the counter.
 #pragma once
 
 #include "ptx.cuh"
@@ -60,19 +71,23 @@ struct GemmParams {
   long long ld_residual;
 };
 
-template <int BN_, int NB_, bool SHARED_A_, int STAGES_, int EPI_, bool IN_F16_, int OUT_>
+template <int BN_, int NB_, bool SHARED_A_, int STAGES_, int EPI_, bool IN_F16_, int OUT_, int CTAS_ = 1>
 struct GemmCfg {
-  static constexpr int BM = 128, BK = 64;
-  static constexpr int BN = BN_, NB = NB_, STAGES = STAGES_, EPI = EPI_, OUT = OUT_;
+  static constexpr int BM = 128, BK = 64;  // rows per CTA, K per stage
+  static constexpr int BN = BN_, NB = NB_, STAGES = STAGES_, EPI = EPI_, OUT = OUT_, CTAS = CTAS_;
   static constexpr bool IN_F16 = IN_F16_;
   static constexpr bool SHARED_A = SHARED_A_;
   static constexpr int NA = (NB == 2 && !SHARED_A) ? 2 : 1;
+  static constexpr int TILE_M = BM * CTAS;  // rows of one work unit
+  static constexpr int B_ROWS = BN / CTAS;  // rows of B loaded by each CTA
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
+  static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair per tile");
+  static_assert(B_ROWS % 8 == 0, "B half-tile must hold whole 8-row core-matrix groups");
   static_assert(NB == 1 || NB == 2, "one or two accumulators per tile");
   static_assert(NB == 1 || EPI == EPI_SWIGLU, "dual GEMMs use the SwiGLU epilogue");
   static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BN * BK * 2;
-  static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;
+  static constexpr int B_BYTES = B_ROWS * BK * 2;
+  static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;  // per CTA
   static constexpr bool IS_F32 = (OUT == OUT_F32);
   static constexpr int OUT_ELT = IS_F32 ? 4 : 2;
   static constexpr int STG_BYTES = 32 * 32 * OUT_ELT;  // one 32x32 output box per warp buffer
@@ -80,7 +95,7 @@ struct GemmCfg {
   static constexpr int ACC_STRIDE = NB * BSTRIDE;        // TMEM columns per accumulator buffer
   static_assert(2 * ACC_STRIDE <= 512, "double-buffered accumulators must fit in 512 TMEM columns");
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t IDESC = make_idesc_16bit(BM, BN, IN_F16);
+  static constexpr uint32_t IDESC = make_idesc_16bit(TILE_M, BN, IN_F16);
 
   static constexpr int OFF_A = 0;
   static constexpr int OFF_A2 = OFF_A + STAGES * A_BYTES;
@@ -91,17 +106,16 @@ struct GemmCfg {
   static constexpr int NUM_BARS = 2 * STAGES + 5;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;  // + slack for 1024-byte alignment
+  static_assert(B_BYTES % 1024 == 0, "operand stage buffers must stay 1024-byte aligned");
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
 };
 
-template <class Cfg>
 struct UnitCoord {
   int m_t, n_t, ks, kb0, kb1, tile;
 };
 
-template <class Cfg>
-SVD_DEV UnitCoord<Cfg> decode_unit(const GemmParams& p, int u) {
-  UnitCoord<Cfg> c;
+SVD_DEV UnitCoord decode_unit(const GemmParams& p, int u) {
+  UnitCoord c;
   c.m_t = u % p.m_tiles;
   const int rest = u / p.m_tiles;
   c.ks = rest % p.splits;
@@ -189,12 +203,49 @@ SVD_DEV void epilogue_math(const GemmParams& p, float (&v)[32], const float (&u)
   }
 }
 
+// acc += t0 then acc += t1, element by element (the split order).
+SVD_DEV void add_partials(float (&acc)[32], const float4 (&t0)[8], const float4 (&t1)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    acc[4 * j] += t0[j].x;
+    acc[4 * j + 1] += t0[j].y;
+    acc[4 * j + 2] += t0[j].z;
+    acc[4 * j + 3] += t0[j].w;
+    acc[4 * j] += t1[j].x;
+    acc[4 * j + 1] += t1[j].y;
+    acc[4 * j + 2] += t1[j].z;
+    acc[4 * j + 3] += t1[j].w;
+  }
+}
+
+template <class Cfg>
+SVD_DEV void issue_stage_loads(const CUtensorMap* tm_a, const CUtensorMap* tm_a2, const CUtensorMap* tm_b,
+                               const CUtensorMap* tm_b2, uint8_t* smem, int s, uint64_t* full_local,
+                               uint32_t full_leader, int kx, int a_row, int b_row) {
+  uint8_t* a = smem + Cfg::OFF_A + s * Cfg::A_BYTES;
+  uint8_t* a2 = smem + Cfg::OFF_A2 + s * Cfg::A_BYTES;
+  uint8_t* b = smem + Cfg::OFF_B + s * Cfg::B_BYTES;
+  uint8_t* b2 = smem + Cfg::OFF_B2 + s * Cfg::B_BYTES;
+  if constexpr (Cfg::CTAS == 1) {
+    tma_load_2d(tm_a, full_local, a, kx, a_row);
+    if constexpr (Cfg::NA == 2) tma_load_2d(tm_a2, full_local, a2, kx, a_row);
+    tma_load_2d(tm_b, full_local, b, kx, b_row);
+    if constexpr (Cfg::NB == 2) tma_load_2d(tm_b2, full_local, b2, kx, b_row);
+  } else {
+    tma_load_2d_pair(tm_a, full_leader, a, kx, a_row);
+    if constexpr (Cfg::NA == 2) tma_load_2d_pair(tm_a2, full_leader, a2, kx, a_row);
+    tma_load_2d_pair(tm_b, full_leader, b, kx, b_row);
+    if constexpr (Cfg::NB == 2) tma_load_2d_pair(tm_b2, full_leader, b2, kx, b_row);
+  }
+}
+
 template <class Cfg>
 __global__ void __launch_bounds__(192, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a2,
                       const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b2,
                       const __grid_constant__ CUtensorMap tm_out, const GemmParams p) {
   constexpr int STAGES = Cfg::STAGES;
+  constexpr bool PAIR = Cfg::CTAS == 2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
@@ -209,6 +260,10 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = lane_id();
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
+  const int unit0 = PAIR ? static_cast<int>(blockIdx.x >> 1) : static_cast<int>(blockIdx.x);
+  const int unit_step = PAIR ? static_cast<int>(gridDim.x >> 1) : static_cast<int>(gridDim.x);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -217,7 +272,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 4 * Cfg::CTAS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -233,11 +288,17 @@ __global__ void __launch_bounds__(192, 1)
     prefetch_tensormap(&tm_out);
   }
   if (warp == 5) {
-    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // both CTAs' barriers exist before any remote signal
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const WaitCtx ctx{abort_flag, p.err, p.timeout_ns};
@@ -246,10 +307,13 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       grid_dependency_wait();  // inputs of this launch come from the previous one
+      const uint32_t full_leader0 = PAIR ? mapa_shared(smem_addr(&full[0]), 0) : 0u;
       int it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
-        const UnitCoord<Cfg> c = decode_unit<Cfg>(p, u);
+      for (int u = unit0; u < p.num_units && ok; u += unit_step) {
+        const UnitCoord c = decode_unit(p, u);
+        const int a_row = c.m_t * Cfg::TILE_M + static_cast<int>(rank) * Cfg::BM;
+        const int b_row = c.n_t * Cfg::BN + static_cast<int>(rank) * Cfg::B_ROWS;
         for (int kb = c.kb0; kb < c.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
@@ -257,34 +321,35 @@ __global__ void __launch_bounds__(192, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES);
-          const int kx = kb * Cfg::BK;
-          tma_load_2d(&tm_a, &full[s], smem + Cfg::OFF_A + s * Cfg::A_BYTES, kx, c.m_t * Cfg::BM);
-          if constexpr (Cfg::NA == 2)
-            tma_load_2d(&tm_a2, &full[s], smem + Cfg::OFF_A2 + s * Cfg::A_BYTES, kx, c.m_t * Cfg::BM);
-          tma_load_2d(&tm_b, &full[s], smem + Cfg::OFF_B + s * Cfg::B_BYTES, kx, c.n_t * Cfg::BN);
-          if constexpr (Cfg::NB == 2)
-            tma_load_2d(&tm_b2, &full[s], smem + Cfg::OFF_B2 + s * Cfg::B_BYTES, kx, c.n_t * Cfg::BN);
+          if (leader) mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES * Cfg::CTAS);
+          issue_stage_loads<Cfg>(&tm_a, &tm_a2, &tm_b, &tm_b2, smem, s, &full[s], full_leader0 + 8u * s,
+                                 kb * Cfg::BK, a_row, b_row);
         }
       }
       grid_launch_dependents();
       // Drain: every stage's most recent load must have landed before the CTA
-      // may exit (on the normal path these waits return at once).
+      // may exit (on the normal path these waits return at once).  In a pair
+      // the loads complete on the even CTA's barrier, so the odd CTA waits for
+      // the MMA that consumed them (its `empty` barrier) instead.
       for (int s = 0; s < STAGES; ++s) {
         if (it > s) {
           const int last = s + ((it - 1 - s) / STAGES) * STAGES;
-          mbar_wait(&full[s], static_cast<uint32_t>(last / STAGES) & 1u, ctx, SITE_DRAIN_LOADS, false);
+          const uint32_t par = static_cast<uint32_t>(last / STAGES) & 1u;
+          if (PAIR && !leader)
+            mbar_wait(&empty[s], par, ctx, SITE_DRAIN_LOADS, false);
+          else
+            mbar_wait(&full[s], par, ctx, SITE_DRAIN_LOADS, false);
         }
       }
     }
     __syncwarp();
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       int it = 0, acc_it = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < p.num_units && ok; u += gridDim.x) {
-        const UnitCoord<Cfg> c = decode_unit<Cfg>(p, u);
+      for (int u = unit0; u < p.num_units && ok; u += unit_step) {
+        const UnitCoord c = decode_unit(p, u);
         const int b = acc_it & 1;
         const uint32_t aph = static_cast<uint32_t>(acc_it >> 1) & 1u;
         if (!mbar_wait(&acc_empty[b], aph ^ 1u, ctx, SITE_MMA_ACC_EMPTY)) break;
@@ -299,37 +364,46 @@ __global__ void __launch_bounds__(192, 1)
           }
           tc_fence_after();
           const uint32_t a_addr = smem_addr(smem + Cfg::OFF_A + s * Cfg::A_BYTES);
-          const uint32_t a2_addr =
-              Cfg::NA == 2 ? smem_addr(smem + Cfg::OFF_A2 + s * Cfg::A_BYTES) : a_addr;
+          const uint32_t a2_addr = Cfg::NA == 2 ? smem_addr(smem + Cfg::OFF_A2 + s * Cfg::A_BYTES) : a_addr;
           const uint32_t b_addr = smem_addr(smem + Cfg::OFF_B + s * Cfg::B_BYTES);
           const uint32_t b2_addr = smem_addr(smem + Cfg::OFF_B2 + s * Cfg::B_BYTES);
 #pragma unroll
           for (int k = 0; k < Cfg::BK / 16; ++k) {
             const uint32_t acc = (kb > c.kb0 || k > 0) ? 1u : 0u;
-            umma_f16kind(d, make_sw128_desc(a_addr + k * 32), make_sw128_desc(b_addr + k * 32), Cfg::IDESC, acc);
-            if constexpr (Cfg::NB == 2)
-              umma_f16kind(d + Cfg::BSTRIDE, make_sw128_desc(a2_addr + k * 32), make_sw128_desc(b2_addr + k * 32),
-                        Cfg::IDESC, acc);
+            const uint64_t ad = make_sw128_desc(a_addr + k * 32), bd = make_sw128_desc(b_addr + k * 32);
+            if constexpr (PAIR) umma_f16kind_pair(d, ad, bd, Cfg::IDESC, acc);
+            else umma_f16kind(d, ad, bd, Cfg::IDESC, acc);
+            if constexpr (Cfg::NB == 2) {
+              const uint64_t ad2 = make_sw128_desc(a2_addr + k * 32), bd2 = make_sw128_desc(b2_addr + k * 32);
+              if constexpr (PAIR) umma_f16kind_pair(d + Cfg::BSTRIDE, ad2, bd2, Cfg::IDESC, acc);
+              else umma_f16kind(d + Cfg::BSTRIDE, ad2, bd2, Cfg::IDESC, acc);
+            }
           }
-          umma_commit(&empty[s]);  // frees the smem stage once these MMAs have read it
+          // frees the smem stage (of both CTAs) once these MMAs have read it
+          if constexpr (PAIR) umma_commit_pair_multicast(&empty[s], 0x3);
+          else umma_commit(&empty[s]);
         }
         if (!ok) break;
-        umma_commit(&acc_full[b]);  // accumulator ready for the epilogue
+        // accumulator ready for the epilogue (of both CTAs)
+        if constexpr (PAIR) umma_commit_pair_multicast(&acc_full[b], 0x3);
+        else umma_commit(&acc_full[b]);
         ++acc_it;
       }
       // Drain: all issued MMAs must be complete before TMEM is released.
-      umma_commit(drain);
+      if constexpr (PAIR) umma_commit_pair(drain);
+      else umma_commit(drain);
       mbar_wait(drain, 0, ctx, SITE_DRAIN_MMA, false);
     }
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp;  // TMEM lane quarter == rows [32q, 32q + 32) of the tile
+    const int q = warp;  // TMEM lane quarter == rows [32q, 32q + 32) of this CTA's rows
     uint8_t* stg_warp = smem + Cfg::OFF_STG + q * 2 * Cfg::STG_BYTES;
+    const uint32_t acc_empty_leader0 = PAIR ? mapa_shared(smem_addr(&acc_empty[0]), 0) : 0u;
     int stg_buf = 0;
     int acc_it = 0;
-    for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
-      const UnitCoord<Cfg> c = decode_unit<Cfg>(p, u);
+    for (int u = unit0; u < p.num_units; u += unit_step) {
+      const UnitCoord c = decode_unit(p, u);
       const int b = acc_it & 1;
       const uint32_t aph = static_cast<uint32_t>(acc_it >> 1) & 1u;
       bool ok = mbar_wait(&acc_full[b], aph, ctx, SITE_EPI_ACC_FULL);
@@ -341,10 +415,11 @@ __global__ void __launch_bounds__(192, 1)
       if (*epi_abort) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
+      const int row_base = c.m_t * Cfg::TILE_M + static_cast<int>(rank) * Cfg::BM;  // this CTA's first row
       const int row_in_tile = q * 32 + static_cast<int>(lane);
-      const int grow = c.m_t * Cfg::BM + row_in_tile;
+      const int grow = row_base + row_in_tile;
       const int n0 = c.n_t * Cfg::BN;
-      const int y_box = c.m_t * Cfg::BM + q * 32;
+      const int y_box = row_base + q * 32;
 
       if (p.splits == 1) {
 #pragma unroll 1
@@ -354,6 +429,15 @@ __global__ void __launch_bounds__(192, 1)
           tmem_ld_x32(tacc + ch * 32, rg);
           if constexpr (Cfg::NB == 2) tmem_ld_x32(tacc + Cfg::BSTRIDE + ch * 32, ru);
           tmem_ld_wait();
+          if (ch == Cfg::BN / 32 - 1) {
+            // Every TMEM read of this buffer has returned: release it early.
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) {
+              if constexpr (PAIR) mbar_arrive_cluster(acc_empty_leader0 + 8u * b);
+              else mbar_arrive(&acc_empty[b]);
+            }
+          }
           float v[32], w[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
@@ -363,12 +447,10 @@ __global__ void __launch_bounds__(192, 1)
           epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
           store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
         }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);
       } else {
-        // Pass 1: publish this split's fp32 partial tile.
+        // Pass 1: publish this split's fp32 partial tile (valid rows only).
         float* slot = p.partials + static_cast<size_t>(c.tile * p.splits + c.ks) * Cfg::NB * (Cfg::BM * Cfg::BN);
+        const bool row_ok = grow < p.M;
 #pragma unroll 1
         for (int ch = 0; ch < Cfg::BN / 32; ++ch) {
 #pragma unroll
@@ -376,12 +458,14 @@ __global__ void __launch_bounds__(192, 1)
             uint32_t r[32];
             tmem_ld_x32(tacc + br * Cfg::BSTRIDE + ch * 32, r);
             tmem_ld_wait();
-            float4* dst = reinterpret_cast<float4*>(slot + static_cast<size_t>(br) * (Cfg::BM * Cfg::BN) +
-                                                    ch * (Cfg::BM * 32) + row_in_tile * 32);
+            if (row_ok) {
+              float4* dst = reinterpret_cast<float4*>(slot + static_cast<size_t>(br) * (Cfg::BM * Cfg::BN) +
+                                                      ch * (Cfg::BM * 32) + row_in_tile * 32);
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                          __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+              for (int j = 0; j < 8; ++j)
+                __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+            }
           }
         }
         tc_fence_before();
@@ -405,28 +489,26 @@ __global__ void __launch_bounds__(192, 1)
               v[j] = 0.0f;
               w[j] = 0.0f;
             }
+            if (row_ok) {
 #pragma unroll 1
-            for (int s = 0; s < p.splits; ++s) {
-              const float* src = base + static_cast<size_t>(s) * Cfg::NB * (Cfg::BM * Cfg::BN) + ch * (Cfg::BM * 32) +
-                                 row_in_tile * 32;
-              const float4* s4 = reinterpret_cast<const float4*>(src);
+              for (int s = 0; s < p.splits; s += 2) {
+                // two splits' loads in flight per step; the sum order is the split order
+                const bool two = s + 1 < p.splits;
+                const float* src0 = base + static_cast<size_t>(s) * Cfg::NB * (Cfg::BM * Cfg::BN) +
+                                    ch * (Cfg::BM * 32) + row_in_tile * 32;
+                const float* src1 = src0 + static_cast<size_t>(Cfg::NB) * (Cfg::BM * Cfg::BN);
 #pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float4 t = __ldcg(s4 + j);
-                v[4 * j] += t.x;
-                v[4 * j + 1] += t.y;
-                v[4 * j + 2] += t.z;
-                v[4 * j + 3] += t.w;
-              }
-              if constexpr (Cfg::NB == 2) {
-                const float4* u4 = reinterpret_cast<const float4*>(src + Cfg::BM * Cfg::BN);
+                for (int br = 0; br < Cfg::NB; ++br) {
+                  const float4* s0 = reinterpret_cast<const float4*>(src0 + br * (Cfg::BM * Cfg::BN));
+                  const float4* s1 = reinterpret_cast<const float4*>(src1 + br * (Cfg::BM * Cfg::BN));
+                  float4 t0[8], t1[8];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                  const float4 t = __ldcg(u4 + j);
-                  w[4 * j] += t.x;
-                  w[4 * j + 1] += t.y;
-                  w[4 * j + 2] += t.z;
-                  w[4 * j + 3] += t.w;
+                  for (int j = 0; j < 8; ++j) {
+                    t0[j] = __ldcg(s0 + j);
+                    t1[j] = two ? __ldcg(s1 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  }
+                  if (br == 0) add_partials(v, t0, t1);
+                  else add_partials(w, t0, t1);
                 }
               }
             }
@@ -443,9 +525,11 @@ __global__ void __launch_bounds__(192, 1)
   }
 
   __syncthreads();
+  if constexpr (PAIR) cluster_sync();  // the peer's MMAs and arrivals are done
   if (warp == 5) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+    if constexpr (PAIR) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+    else tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
   }
 }
 

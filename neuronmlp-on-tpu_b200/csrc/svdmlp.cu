@@ -14,6 +14,7 @@
 #include <cstring>
 #include <mutex>
 #include <type_traits>
+#include <vector>
 
 #include "../../include/svdmlp.h"
 #include "gemm_sm100.cuh"
@@ -27,6 +28,16 @@ static thread_local int g_last_cuda_error = 0;
 static std::atomic<int64_t> g_launches{0};
 static int g_split_override[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 static unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s: far above any legal wait
+
+// Optional per-stage event timing (a diagnostics pass; off by default).
+struct TimedLaunch {
+  int stage;
+  cudaEvent_t start, stop;
+};
+static std::mutex g_timing_mu;
+static bool g_timing = false;
+static std::vector<TimedLaunch> g_timed;
+static size_t g_timed_used = 0;
 
 static int cuda_fail(cudaError_t e) {
   g_last_cuda_error = static_cast<int>(e);
@@ -135,28 +146,32 @@ struct Plan {
   int m_tiles, n_tiles, k_blocks, splits, kb_per_split, units, grid;
 };
 
-// Chooses the split-K factor that minimises a wave-quantisation cost model:
-// rounds of units over the SMs times the k-blocks per unit, plus a per-unit
-// pipeline/epilogue overhead and the fix-up reads of the last split.
-static Plan plan_gemm(int M, int N, int K, int BN, int sms, int forced_splits) {
+// One-CTA plans (decode-sized M): chooses the split-K factor that minimises a
+// wave-quantisation cost model in units of one k-block's MMA time: rounds of
+// units over the SMs times the k-blocks per unit, plus a per-unit pipeline
+// and epilogue overhead, plus the fix-up traffic of the partial tiles (valid
+// rows only), which is latency-bound at roughly 20 bytes per SM cycle.
+static Plan plan_gemm(int M, int N, int K, int BN, int NB, int sms, int forced_splits) {
   Plan p{};
   p.m_tiles = static_cast<int>(cdiv(M, 128));
   p.n_tiles = static_cast<int>(cdiv(N, BN));
   p.k_blocks = static_cast<int>(cdiv(K, 64));
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+  const double rows = static_cast<double>(std::min(M, 128));
   int best_s = 1;
   if (forced_splits > 0) {
     best_s = std::min(forced_splits, p.k_blocks);
   } else {
     double best = 1e30;
-    for (int s = 1; s <= 16; ++s) {
+    for (int s = 1; s <= 32; ++s) {
       const int kbs = static_cast<int>(cdiv(p.k_blocks, s));
-      if (s > 1 && kbs < 4) break;
+      if (s > 1 && kbs < 2) break;
       const int s_eff = static_cast<int>(cdiv(p.k_blocks, kbs));
       if (s > 1 && s_eff != s) continue;
       const int64_t units = tiles * s_eff;
       const int64_t rounds = cdiv(units, sms);
-      const double cost = static_cast<double>(rounds) * (kbs + 1.5) + (s_eff > 1 ? 1.0 + 0.75 * s_eff : 0.0);
+      double cost = static_cast<double>(rounds) * (kbs + 1.5);
+      if (s_eff > 1) cost += 1.0 + 2.0 * s_eff * rows * BN * NB * 4.0 / 20.0 / 512.0;
       if (cost < best * 0.97) {
         best = cost;
         best_s = s_eff;
@@ -170,6 +185,30 @@ static Plan plan_gemm(int M, int N, int K, int BN, int sms, int forced_splits) {
   return p;
 }
 
+// CTA-pair plans (prefill-sized M): 256-row tiles, no split-K, one cluster of
+// two CTAs per pair of SMs.
+static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms) {
+  Plan p{};
+  p.m_tiles = static_cast<int>(cdiv(M, 256));
+  p.n_tiles = static_cast<int>(cdiv(N, BN));
+  p.k_blocks = static_cast<int>(cdiv(K, 64));
+  p.splits = 1;
+  p.kb_per_split = p.k_blocks;
+  p.units = p.m_tiles * p.n_tiles;
+  p.grid = 2 * std::min(p.units, sms / 2);
+  return p;
+}
+
+template <class Cfg>
+static Plan plan_for(int M, int N, int K, int sms, int forced_splits) {
+  if constexpr (Cfg::CTAS == 2) return plan_gemm_pair(M, N, K, Cfg::BN, sms);
+  else return plan_gemm(M, N, K, Cfg::BN, Cfg::NB, sms, forced_splits);
+}
+
+// Token counts above this use the CTA-pair kernels; below, one-CTA kernels
+// with split-K stream the weights across all SMs.
+static constexpr int kPairMinM = 129;
+
 // Bytes of split-K partials a plan needs (NB accumulators of BM x BN fp32).
 static int64_t partial_bytes(const Plan& p, int BN, int NB) {
   if (p.splits <= 1) return 0;
@@ -177,17 +216,29 @@ static int64_t partial_bytes(const Plan& p, int BN, int NB) {
 }
 
 // ------------------------------------------------------------ kernel configs
-//            BN  NB shared STG epilogue   fp16-in out
-using CfgXU     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_F16>;   // X.[u_g|u_u] -> XU (fp16)
-using CfgGU     = GemmCfg<128, 2, false, 3, EPI_SWIGLU, true,  OUT_F16>;   // XU.v -> H (fp16, internal)
-using CfgGUbf   = GemmCfg<128, 2, false, 3, EPI_SWIGLU, true,  OUT_BF16>;  // XU.v -> H (bf16, to the caller)
-using CfgDU     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_F16>;   // H.u_down -> T (fp16)
-using CfgDUbf   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_F16>;   // bf16 H.u_down (down-only layout)
-using CfgDUf32  = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_F32>;   // H.u_down -> fp32 partial (TP)
-using CfgDV     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_BF16>;  // T.v_down -> y
-using CfgDVres  = GemmCfg<256, 1, false, 4, EPI_RESID,  true,  OUT_BF16>;  // T.v_down + residual -> y
-using CfgDenseGU = GemmCfg<128, 2, true, 4, EPI_SWIGLU, false, OUT_F16>;   // X.[w_g|w_u] -> H (fp16)
-using CfgGemm   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_BF16>;  // plain bf16 GEMM
+// Prefill (M > 128): CTA pairs, 256-row tiles.
+//                          BN  NB shared STG epilogue   fp16-in out       CTAs
+using CfgXU     = GemmCfg<256, 1, false, 6, EPI_PLAIN,  false, OUT_F16,  2>;  // X.[u_g|u_u] -> XU (fp16)
+using CfgGU     = GemmCfg<128, 2, false, 4, EPI_SWIGLU, true,  OUT_F16,  2>;  // XU.v -> H (fp16, internal)
+using CfgGUbf   = GemmCfg<128, 2, false, 4, EPI_SWIGLU, true,  OUT_BF16, 2>;  // XU.v -> H (bf16, to the caller)
+using CfgDU     = GemmCfg<256, 1, false, 6, EPI_PLAIN,  true,  OUT_F16,  2>;  // H.u_down -> T (fp16)
+using CfgDUbf   = GemmCfg<256, 1, false, 6, EPI_PLAIN,  false, OUT_F16,  2>;  // bf16 H.u_down (down-only layout)
+using CfgDUf32  = GemmCfg<256, 1, false, 6, EPI_PLAIN,  true,  OUT_F32,  2>;  // H.u_down -> fp32 partial (TP)
+using CfgDV     = GemmCfg<256, 1, false, 6, EPI_PLAIN,  true,  OUT_BF16, 2>;  // T.v_down -> y
+using CfgDVres  = GemmCfg<256, 1, false, 6, EPI_RESID,  true,  OUT_BF16, 2>;  // T.v_down + residual -> y
+using CfgDenseGU = GemmCfg<128, 2, true, 6, EPI_SWIGLU, false, OUT_F16,  2>;  // X.[w_g|w_u] -> H (fp16)
+using CfgGemm   = GemmCfg<256, 1, false, 6, EPI_PLAIN,  false, OUT_BF16, 2>;  // plain bf16 GEMM
+// Decode (M <= 128): one CTA per tile, split-K across the SMs.
+using CfgXU1     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_F16>;
+using CfgGU1     = GemmCfg<128, 2, false, 3, EPI_SWIGLU, true,  OUT_F16>;
+using CfgGUbf1   = GemmCfg<128, 2, false, 3, EPI_SWIGLU, true,  OUT_BF16>;
+using CfgDU1     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_F16>;
+using CfgDUbf1   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_F16>;
+using CfgDUf321  = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_F32>;
+using CfgDV1     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_BF16>;
+using CfgDVres1  = GemmCfg<256, 1, false, 4, EPI_RESID,  true,  OUT_BF16>;
+using CfgDenseGU1 = GemmCfg<128, 2, true, 4, EPI_SWIGLU, false, OUT_F16>;
+using CfgGemm1   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_BF16>;
 
 enum Stage : int { ST_XU = 0, ST_GATEUP = 1, ST_DOWN_U = 2, ST_DOWN_V = 3, ST_DENSE_GU = 4, ST_DENSE_D = 5, ST_GEMM = 6 };
 
@@ -213,29 +264,27 @@ static int64_t counters_bytes(const svdmlp_layout* L, int max_m) {
 
 template <class Cfg>
 static int64_t stage_partials(int M, int N, int K, int sms, int stage) {
-  const Plan p = plan_gemm(M, N, K, Cfg::BN, sms, g_split_override[stage]);
-  return partial_bytes(p, Cfg::BN, Cfg::NB);
+  const Plan p = plan_for<Cfg>(M, N, K, sms, g_split_override[stage]);
+  return Cfg::CTAS == 1 ? partial_bytes(p, Cfg::BN, Cfg::NB) : 0;
 }
 
-// Largest split-K partial buffer any M <= max_m can ask for.
+// Largest split-K partial buffer any M <= max_m can ask for (split-K runs
+// only in the one-CTA kernels, i.e. for M <= 128).
 static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
+  const int M = std::min(max_m, kPairMinM - 1);
   int64_t best = 0;
-  const int64_t mt = cdiv(max_m, 128);
-  for (int64_t t = 1; t <= mt; ++t) {
-    const int M = static_cast<int>(std::min<int64_t>(t * 128, max_m));
-    if (L->kind == SVDMLP_KIND_SVD) {
-      if (L->r_gu > 0) {
-        best = std::max(best, stage_partials<CfgXU>(M, 2 * L->rp_gu, L->d, sms, ST_XU));
-        best = std::max(best, stage_partials<CfgGU>(M, L->ff, L->r_gu, sms, ST_GATEUP));
-      }
-      if (L->r_d > 0) {
-        best = std::max(best, stage_partials<CfgDU>(M, L->r_d, L->ff, sms, ST_DOWN_U));
-        best = std::max(best, stage_partials<CfgDV>(M, L->d, L->r_d, sms, ST_DOWN_V));
-      }
-    } else {
-      best = std::max(best, stage_partials<CfgDenseGU>(M, L->ff, L->d, sms, ST_DENSE_GU));
-      best = std::max(best, stage_partials<CfgDV>(M, L->d, L->ff, sms, ST_DENSE_D));
+  if (L->kind == SVDMLP_KIND_SVD) {
+    if (L->r_gu > 0) {
+      best = std::max(best, stage_partials<CfgXU1>(M, 2 * L->rp_gu, L->d, sms, ST_XU));
+      best = std::max(best, stage_partials<CfgGU1>(M, L->ff, L->r_gu, sms, ST_GATEUP));
     }
+    if (L->r_d > 0) {
+      best = std::max(best, stage_partials<CfgDU1>(M, L->r_d, L->ff, sms, ST_DOWN_U));
+      best = std::max(best, stage_partials<CfgDV1>(M, L->d, L->r_d, sms, ST_DOWN_V));
+    }
+  } else {
+    best = std::max(best, stage_partials<CfgDenseGU1>(M, L->ff, L->d, sms, ST_DENSE_GU));
+    best = std::max(best, stage_partials<CfgDV1>(M, L->d, L->ff, sms, ST_DENSE_D));
   }
   return round_up(best, 256);
 }
@@ -298,7 +347,7 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
       done_mask |= 1ull << cur;
     }
   }
-  const Plan pl = plan_gemm(M, N, K, Cfg::BN, dev->sms, g_split_override[stage]);
+  const Plan pl = plan_for<Cfg>(M, N, K, dev->sms, g_split_override[stage]);
   GemmParams p{};
   p.M = M;
   p.N = N;
@@ -322,12 +371,26 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = Cfg::CTAS;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
+  TimedLaunch* tl = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_timing_mu);
+    if (g_timing && g_timed_used < g_timed.size()) {
+      tl = &g_timed[g_timed_used++];
+      tl->stage = stage;
+    }
+  }
+  if (tl) SVD_CUDA(cudaEventRecord(tl->start, stream));
   SVD_CUDA(cudaLaunchKernelEx(&cfg, gemm_sm100_kernel<Cfg>, a, a2, b, b2, out, p));
+  if (tl) SVD_CUDA(cudaEventRecord(tl->stop, stream));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return SVDMLP_OK;
 }
@@ -474,59 +537,99 @@ static int finish_output(void* target, int64_t ld_target, const void* staged, in
 }
 
 // ------------------------------------------------------------------ stages
+// A K-major operand: `rows` rows of `k` 16-bit elements, leading dim `ld`.
+struct Operand {
+  const void* ptr;
+  bool f16;
+  int64_t k, rows, ld;
+};
+struct Output {
+  void* ptr;
+  int64_t n, rows, ld;
+};
+
+template <class Cfg>
+static int gemm_cfg(const Operand& a, const Operand& a2, const Operand& b, const Operand& b2, const Output& o, int M,
+                    int N, int K, int stage, const Workspace& w, const void* residual, int64_t ld_res,
+                    cudaStream_t s) {
+  CUtensorMap ma, ma2, mb, mb2, mo;
+  SVD_CHECK(operand_map(&ma, a.ptr, a.f16, a.k, a.rows, a.ld, Cfg::BM));
+  SVD_CHECK(operand_map(&ma2, a2.ptr, a2.f16, a2.k, a2.rows, a2.ld, Cfg::BM));
+  SVD_CHECK(operand_map(&mb, b.ptr, b.f16, b.k, b.rows, b.ld, Cfg::B_ROWS));
+  SVD_CHECK(operand_map(&mb2, b2.ptr, b2.f16, b2.k, b2.rows, b2.ld, Cfg::B_ROWS));
+  SVD_CHECK(output_map<Cfg>(&mo, o.ptr, o.n, o.rows, o.ld));
+  return launch_gemm<Cfg>(ma, ma2, mb, mb2, mo, M, N, K, stage, w, static_cast<const bf16*>(residual), ld_res, s);
+}
+
+// Runs one GEMM stage with the CTA-pair config for prefill-sized M and the
+// one-CTA split-K config for decode-sized M.
+template <class CPair, class COne>
+static int gemm_stage(const Operand& a, const Operand& a2, const Operand& b, const Operand& b2, const Output& o,
+                      int M, int N, int K, int stage, const Workspace& w, cudaStream_t s,
+                      const void* residual = nullptr, int64_t ld_res = 0) {
+  if (M >= kPairMinM) return gemm_cfg<CPair>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
+  return gemm_cfg<COne>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
+}
+
 // Stage 1 + 2: h = silu(X.u_g.v_g) * (X.u_u.v_u); `h_bf16` selects the
 // caller-facing bf16 output instead of the internal fp16 H.
 static int run_gate_up(const svdmlp_layout* L, const uint8_t* packed, const void* x, int64_t ldx, int M, void* h,
                        int64_t ldh, bool h_bf16, const Workspace& w, cudaStream_t s) {
-  CUtensorMap a, b, out, a_g, a_u, b_g, b_u, hmap;
   const int64_t n1 = 2LL * L->rp_gu;
-  SVD_CHECK(operand_map(&a, x, false, L->d, M, ldx, 128));
-  SVD_CHECK(operand_map(&b, packed + L->off_w1, false, L->d, n1, L->ld_d, CfgXU::BN));
-  SVD_CHECK(output_map<CfgXU>(&out, w.xu, n1, M, n1));
-  SVD_CHECK(launch_gemm<CfgXU>(a, a, b, b, out, M, static_cast<int>(n1), L->d, ST_XU, w, nullptr, 0, s));
-  SVD_CHECK(operand_map(&a_g, w.xu, true, L->r_gu, M, n1, 128));
-  SVD_CHECK(operand_map(&a_u, w.xu + L->rp_gu, true, L->r_gu, M, n1, 128));
-  SVD_CHECK(operand_map(&b_g, packed + L->off_vg, true, L->r_gu, L->ff, L->rp_gu, CfgGU::BN));
-  SVD_CHECK(operand_map(&b_u, packed + L->off_vu, true, L->r_gu, L->ff, L->rp_gu, CfgGU::BN));
-  if (h_bf16) {
-    SVD_CHECK(output_map<CfgGUbf>(&hmap, h, L->ff, M, ldh));
-    return launch_gemm<CfgGUbf>(a_g, a_u, b_g, b_u, hmap, M, L->ff, L->r_gu, ST_GATEUP, w, nullptr, 0, s);
-  }
-  SVD_CHECK(output_map<CfgGU>(&hmap, h, L->ff, M, ldh));
-  return launch_gemm<CfgGU>(a_g, a_u, b_g, b_u, hmap, M, L->ff, L->r_gu, ST_GATEUP, w, nullptr, 0, s);
+  const Operand xa{x, false, L->d, M, ldx};
+  const Operand w1{packed + L->off_w1, false, L->d, n1, L->ld_d};
+  SVD_CHECK(gemm_stage<CfgXU, CfgXU1>(xa, xa, w1, w1, Output{w.xu, n1, M, n1}, M, static_cast<int>(n1), L->d, ST_XU,
+                                      w, s));
+  const Operand ag{w.xu, true, L->r_gu, M, n1};
+  const Operand au{w.xu + L->rp_gu, true, L->r_gu, M, n1};
+  const Operand bg{packed + L->off_vg, true, L->r_gu, L->ff, L->rp_gu};
+  const Operand bu{packed + L->off_vu, true, L->r_gu, L->ff, L->rp_gu};
+  const Output ho{h, L->ff, M, ldh};
+  if (h_bf16) return gemm_stage<CfgGUbf, CfgGUbf1>(ag, au, bg, bu, ho, M, L->ff, L->r_gu, ST_GATEUP, w, s);
+  return gemm_stage<CfgGU, CfgGU1>(ag, au, bg, bu, ho, M, L->ff, L->r_gu, ST_GATEUP, w, s);
 }
 
 // Stage 3: H . u_down -> T (fp16, workspace) or an fp32 partial.  `h_f16`
 // says whether H is fp16 (it must then match an fp16 ud) or bf16 (bf16 ud).
 static int run_down_u(const svdmlp_layout* L, const uint8_t* packed, const void* h, int64_t ldh, bool h_f16, int M,
                       float* partial, int64_t ldp, const Workspace& w, cudaStream_t s) {
-  CUtensorMap a, b, out;
-  SVD_CHECK(operand_map(&a, h, h_f16, L->ff, M, ldh, 128));
-  SVD_CHECK(operand_map(&b, packed + L->off_ud, h_f16, L->ff, L->r_d, L->ld_ff, CfgDU::BN));
+  const Operand ha{h, h_f16, L->ff, M, ldh};
+  const Operand ud{packed + L->off_ud, h_f16, L->ff, L->r_d, L->ld_ff};
   if (partial) {
     if (!h_f16) return SVDMLP_ERR_DTYPE;
-    SVD_CHECK(output_map<CfgDUf32>(&out, partial, L->r_d, M, ldp));
-    return launch_gemm<CfgDUf32>(a, a, b, b, out, M, L->r_d, L->ff, ST_DOWN_U, w, nullptr, 0, s);
+    return gemm_stage<CfgDUf32, CfgDUf321>(ha, ha, ud, ud, Output{partial, L->r_d, M, ldp}, M, L->r_d, L->ff,
+                                           ST_DOWN_U, w, s);
   }
-  if (h_f16) {
-    SVD_CHECK(output_map<CfgDU>(&out, w.t, L->r_d, M, L->rp_d));
-    return launch_gemm<CfgDU>(a, a, b, b, out, M, L->r_d, L->ff, ST_DOWN_U, w, nullptr, 0, s);
-  }
-  SVD_CHECK(output_map<CfgDUbf>(&out, w.t, L->r_d, M, L->rp_d));
-  return launch_gemm<CfgDUbf>(a, a, b, b, out, M, L->r_d, L->ff, ST_DOWN_U, w, nullptr, 0, s);
+  const Output to{w.t, L->r_d, M, L->rp_d};
+  if (h_f16) return gemm_stage<CfgDU, CfgDU1>(ha, ha, ud, ud, to, M, L->r_d, L->ff, ST_DOWN_U, w, s);
+  return gemm_stage<CfgDUbf, CfgDUbf1>(ha, ha, ud, ud, to, M, L->r_d, L->ff, ST_DOWN_U, w, s);
 }
 
 // Stage 4: T . v_down (+ residual) -> y (bf16)
 static int run_down_v(const svdmlp_layout* L, const uint8_t* packed, int M, void* y, int64_t ldy,
                       const void* residual, int64_t ld_res, const Workspace& w, cudaStream_t s) {
-  CUtensorMap a, b, out;
-  SVD_CHECK(operand_map(&a, w.t, true, L->r_d, M, L->rp_d, 128));
-  SVD_CHECK(operand_map(&b, packed + L->off_vd, true, L->r_d, L->d, L->rp_d, CfgDV::BN));
-  SVD_CHECK(output_map<CfgDV>(&out, y, L->d, M, ldy));
+  const Operand ta{w.t, true, L->r_d, M, L->rp_d};
+  const Operand vd{packed + L->off_vd, true, L->r_d, L->d, L->rp_d};
+  const Output yo{y, L->d, M, ldy};
   if (residual)
-    return launch_gemm<CfgDVres>(a, a, b, b, out, M, L->d, L->r_d, ST_DOWN_V, w, static_cast<const bf16*>(residual),
-                                 ld_res, s);
-  return launch_gemm<CfgDV>(a, a, b, b, out, M, L->d, L->r_d, ST_DOWN_V, w, nullptr, 0, s);
+    return gemm_stage<CfgDVres, CfgDVres1>(ta, ta, vd, vd, yo, M, L->d, L->r_d, ST_DOWN_V, w, s, residual, ld_res);
+  return gemm_stage<CfgDV, CfgDV1>(ta, ta, vd, vd, yo, M, L->d, L->r_d, ST_DOWN_V, w, s);
+}
+
+// Dense SwiGLU: H = silu(X.w_g) * (X.w_u) (fp16), y = H.w_d (+ residual).
+static int run_dense(const svdmlp_layout* L, const uint8_t* packed, const void* x, int64_t ldx, int M, void* y,
+                     int64_t ldy, const void* residual, int64_t ld_res, const Workspace& w, cudaStream_t s) {
+  const Operand xa{x, false, L->d, M, ldx};
+  const Operand bg{packed + L->off_vg, false, L->d, L->ff, L->ld_d};
+  const Operand bu{packed + L->off_vu, false, L->d, L->ff, L->ld_d};
+  SVD_CHECK(gemm_stage<CfgDenseGU, CfgDenseGU1>(xa, xa, bg, bu, Output{w.h, L->ff, M, L->ld_ff}, M, L->ff, L->d,
+                                                ST_DENSE_GU, w, s));
+  const Operand ha{w.h, true, L->ff, M, L->ld_ff};
+  const Operand bd{packed + L->off_ud, true, L->ff, L->d, L->ld_ff};
+  const Output yo{y, L->d, M, ldy};
+  if (residual)
+    return gemm_stage<CfgDVres, CfgDVres1>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s, residual, ld_res);
+  return gemm_stage<CfgDV, CfgDV1>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s);
 }
 
 // Output target: the caller's buffer when TMA-legal, else workspace staging.
@@ -779,25 +882,11 @@ int svdmlp_dense_forward(const svdmlp_layout* L, const void* packed, const void*
   const void* xa;
   int64_t ldxa;
   SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
-  CUtensorMap a, b_g, b_u, hmap;
-  SVD_CHECK(operand_map(&a, xa, false, L->d, M, ldxa, 128));
-  SVD_CHECK(operand_map(&b_g, P + L->off_vg, false, L->d, L->ff, L->ld_d, CfgDenseGU::BN));
-  SVD_CHECK(operand_map(&b_u, P + L->off_vu, false, L->d, L->ff, L->ld_d, CfgDenseGU::BN));
-  SVD_CHECK(output_map<CfgDenseGU>(&hmap, w.h, L->ff, M, L->ld_ff));
-  SVD_CHECK(launch_gemm<CfgDenseGU>(a, a, b_g, b_u, hmap, M, L->ff, L->d, ST_DENSE_GU, w, nullptr, 0, s));
   const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
   const void* res = nullptr;
   int64_t ldr = 0;
   if (residual) SVD_CHECK(stage_in(residual, ld_res, M, L->d, w.xs, L->ld_d, &res, &ldr, s));
-  CUtensorMap ha, bd, out;
-  SVD_CHECK(operand_map(&ha, w.h, true, L->ff, M, L->ld_ff, 128));
-  SVD_CHECK(operand_map(&bd, P + L->off_ud, true, L->ff, L->d, L->ld_ff, CfgDV::BN));
-  SVD_CHECK(output_map<CfgDV>(&out, yt.ptr, L->d, M, yt.ld));
-  if (res)
-    SVD_CHECK(launch_gemm<CfgDVres>(ha, ha, bd, bd, out, M, L->d, L->ff, ST_DENSE_D, w,
-                                    static_cast<const bf16*>(res), ldr, s));
-  else
-    SVD_CHECK(launch_gemm<CfgDV>(ha, ha, bd, bd, out, M, L->d, L->ff, ST_DENSE_D, w, nullptr, 0, s));
+  SVD_CHECK(run_dense(L, P, xa, ldxa, M, yt.ptr, yt.ld, res, ldr, w, s));
   return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
 }
 
@@ -857,9 +946,11 @@ int svdmlp_down_finish(const svdmlp_layout* L, const void* packed, const float* 
 
 int64_t svdmlp_gemm_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return SVDMLP_ERR_INVALID_VALUE;
-  const Plan pl = plan_gemm(M, N, K, CfgGemm::BN, planning_sms(), g_split_override[ST_GEMM]);
-  return kCtlBytes + round_up(static_cast<int64_t>(pl.m_tiles) * pl.n_tiles * 4, 256) +
-         round_up(partial_bytes(pl, CfgGemm::BN, 1), 256);
+  const int sms = planning_sms();
+  const Plan pl = M >= kPairMinM ? plan_for<CfgGemm>(M, N, K, sms, 0)
+                                 : plan_for<CfgGemm1>(M, N, K, sms, g_split_override[ST_GEMM]);
+  const int64_t part = M >= kPairMinM ? 0 : partial_bytes(pl, CfgGemm1::BN, 1);
+  return kCtlBytes + round_up(cdiv(M, 128) * cdiv(N, 128) * 4, 256) + round_up(part, 256);
 }
 
 int svdmlp_gemm(const void* a, int64_t lda, const void* bt, int64_t ldb, void* c, int64_t ldc, int M, int N, int K,
@@ -867,22 +958,20 @@ int svdmlp_gemm(const void* a, int64_t lda, const void* bt, int64_t ldb, void* c
   if (!a || !bt || !c || M <= 0 || N <= 0 || K <= 0 || lda < K || ldb < K || ldc < N) return SVDMLP_ERR_INVALID_VALUE;
   if (!aligned16(a, lda) || !aligned16(bt, ldb) || !aligned16(c, ldc)) return SVDMLP_ERR_ALIGNMENT;
   if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return SVDMLP_ERR_INVALID_VALUE;
-  const int sms = planning_sms();
-  const Plan pl = plan_gemm(M, N, K, CfgGemm::BN, sms, g_split_override[ST_GEMM]);
-  const int64_t cnt = round_up(static_cast<int64_t>(pl.m_tiles) * pl.n_tiles * 4, 256);
-  if (ws_bytes < svdmlp_gemm_workspace_bytes(M, N, K)) return SVDMLP_ERR_WORKSPACE;
+  const int64_t need = svdmlp_gemm_workspace_bytes(M, N, K);
+  if (ws_bytes < need) return SVDMLP_ERR_WORKSPACE;
+  const int64_t cnt = round_up(static_cast<int64_t>(cdiv(M, 128)) * cdiv(N, 128) * 4, 256);
+  if (ws_bytes < kCtlBytes + cnt) return SVDMLP_ERR_WORKSPACE;
   Workspace w{};
   uint8_t* p = static_cast<uint8_t*>(ws);
   w.err = reinterpret_cast<int*>(p);
   w.counters = reinterpret_cast<int*>(p + kCtlBytes);
   w.partials = reinterpret_cast<float*>(p + kCtlBytes + cnt);
   w.partial_cap = ws_bytes - kCtlBytes - cnt;
-  CUtensorMap am, bm, cm;
-  SVD_CHECK(operand_map(&am, a, false, K, M, lda, 128));
-  SVD_CHECK(operand_map(&bm, bt, false, K, N, ldb, CfgGemm::BN));
-  SVD_CHECK(output_map<CfgGemm>(&cm, c, N, M, ldc));
-  return launch_gemm<CfgGemm>(am, am, bm, bm, cm, M, N, K, ST_GEMM, w, nullptr, 0,
-                              static_cast<cudaStream_t>(stream));
+  const Operand ao{a, false, K, M, lda};
+  const Operand bo{bt, false, K, N, ldb};
+  return gemm_stage<CfgGemm, CfgGemm1>(ao, ao, bo, bo, Output{c, N, M, ldc}, M, N, K, ST_GEMM, w,
+                                       static_cast<cudaStream_t>(stream));
 }
 
 int svdmlp_rmsnorm(const void* x, int64_t ldx, const void* w, void* y, int64_t ldy, int M, int n, float eps,
@@ -904,6 +993,41 @@ int svdmlp_debug_wait_timeout(void* ws, int64_t ws_bytes, int64_t limit_ns, void
   return SVDMLP_OK;
 }
 
+int svdmlp_stage_timing(int enable) {
+  std::lock_guard<std::mutex> lock(g_timing_mu);
+  if (enable && g_timed.empty()) {
+    g_timed.resize(4096);
+    for (auto& t : g_timed) {
+      SVD_CUDA(cudaEventCreate(&t.start));
+      SVD_CUDA(cudaEventCreate(&t.stop));
+    }
+  }
+  g_timing = enable != 0;
+  g_timed_used = 0;
+  return SVDMLP_OK;
+}
+
+int svdmlp_stage_times(double* ms_out, int64_t* counts_out, int n) {
+  if (!ms_out || !counts_out || n <= 0) return SVDMLP_ERR_INVALID_VALUE;
+  std::lock_guard<std::mutex> lock(g_timing_mu);
+  for (int i = 0; i < n; ++i) {
+    ms_out[i] = 0.0;
+    counts_out[i] = 0;
+  }
+  for (size_t i = 0; i < g_timed_used; ++i) {
+    SVD_CUDA(cudaEventSynchronize(g_timed[i].stop));
+    float ms = 0.f;
+    SVD_CUDA(cudaEventElapsedTime(&ms, g_timed[i].start, g_timed[i].stop));
+    const int st = g_timed[i].stage;
+    if (st >= 0 && st < n) {
+      ms_out[st] += ms;
+      counts_out[st] += 1;
+    }
+  }
+  g_timed_used = 0;
+  return SVDMLP_OK;
+}
+
 int svdmlp_set_split_override(int stage, int splits) {
   if (stage < 0 || stage >= 8 || splits < 0 || splits > 64) return SVDMLP_ERR_INVALID_VALUE;
   g_split_override[stage] = splits;
@@ -913,7 +1037,9 @@ int svdmlp_set_split_override(int stage, int splits) {
 int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
   if (!out6 || M <= 0 || N <= 0 || K <= 0 || stage < 0 || stage >= 8) return SVDMLP_ERR_INVALID_VALUE;
   const int bn = (stage == ST_GATEUP || stage == ST_DENSE_GU) ? 128 : 256;
-  const Plan p = plan_gemm(M, N, K, bn, planning_sms(), g_split_override[stage]);
+  const int nb = (stage == ST_GATEUP || stage == ST_DENSE_GU) ? 2 : 1;
+  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, N, K, bn, planning_sms())
+                                : plan_gemm(M, N, K, bn, nb, planning_sms(), g_split_override[stage]);
   out6[0] = p.m_tiles;
   out6[1] = p.n_tiles;
   out6[2] = p.k_blocks;

@@ -81,6 +81,8 @@ SIGNATURES = {
     "svdmlp_debug_wait_timeout": (c_int, [V, I64, I64, V]),
     "svdmlp_set_split_override": (c_int, [c_int, c_int]),
     "svdmlp_plan_info": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_int)]),
+    "svdmlp_stage_timing": (c_int, [c_int]),
+    "svdmlp_stage_times": (c_int, [POINTER(ctypes.c_double), POINTER(c_int64), c_int]),
     "svdmlp_launch_count": (c_int64, []),
 }
 
