@@ -1,0 +1,109 @@
+"""The C-ABI library loads and exports every symbol include/svdmlp.h
+declares; host-side argument checks return the documented status codes.
+No compute call reaches a GPU here."""
+from __future__ import annotations
+
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+ROOT = pathlib.Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "svdmlp.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from svdflash_b200 import _build, _lib
+    if _build.is_stale():
+        _build.build()
+    return _lib.load()
+
+
+def declared_functions():
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(svdmlp_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_every_declared_symbol_is_exported(lib):
+    names = declared_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, missing
+
+
+def test_binding_matches_header(lib):
+    from svdflash_b200 import _lib
+    assert set(_lib.SIGNATURES) == set(declared_functions())
+
+
+def test_layout_sizes(lib):
+    from svdflash_b200 import _lib
+    L = _lib.Layout()
+    assert lib.svdmlp_layout_init(ctypes.byref(L), 4096, 14336, 2867, 2867) == 0
+    assert (L.rp_gu, L.rp_d, L.ld_d, L.ld_ff, L.ud_f16) == (2872, 2872, 4096, 14336, 1)
+    # w1 [2*rp, d] + vg, vu [ff, rp] + ud [rp, ff] + vd [d, rp], 2 bytes each, 256-aligned pieces
+    expect = 2 * 2 * 2872 * 4096 + 2 * 2 * 14336 * 2872 + 2 * 2872 * 14336 + 2 * 4096 * 2872
+    assert L.packed_bytes == pytest.approx(expect, abs=5 * 256)
+    for off in (L.off_w1, L.off_vg, L.off_vu, L.off_ud, L.off_vd):
+        assert off % 256 == 0
+    assert lib.svdmlp_workspace_bytes(ctypes.byref(L), 1024) > 0
+    D = _lib.Layout()
+    assert lib.svdmlp_dense_layout_init(ctypes.byref(D), 129, 137) == 0
+    assert (D.ld_d, D.ld_ff, D.kind) == (136, 144, _lib.KIND_DENSE)
+    X = _lib.Layout()
+    assert lib.svdmlp_layout_init(ctypes.byref(X), 513, 1025, 0, 513) == 0
+    assert X.ud_f16 == 0 and X.r_gu == 0
+
+
+@pytest.mark.parametrize("args", [(0, 10, 4, 4), (10, -1, 4, 4), (10, 10, -1, 4), (10, 10, 0, 0)])
+def test_layout_rejects_bad_sizes(lib, args):
+    from svdflash_b200 import _lib
+    L = _lib.Layout()
+    assert lib.svdmlp_layout_init(ctypes.byref(L), *args) == _lib.ERR_INVALID_VALUE
+
+
+def test_entry_points_reject_bad_arguments(lib):
+    from svdflash_b200 import _lib
+    L = _lib.Layout()
+    assert lib.svdmlp_layout_init(ctypes.byref(L), 64, 96, 40, 40) == 0
+    # null pointers / non-positive M fail before any device work
+    assert lib.svdmlp_forward(ctypes.byref(L), None, None, 64, 8, None, 64, None, 0, None, 0, None) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_gate_up(ctypes.byref(L), 1, 1, 64, 0, 1, 96, 1, 1 << 20, None) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_xuv(ctypes.byref(L), 1, 1, 10, 4, 1, 64, 1, 1 << 20, None) == _lib.ERR_INVALID_VALUE  # ld_h < ff
+    assert lib.svdmlp_workspace_init(None, 0, None) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_gemm(None, 8, None, 8, None, 8, 4, 4, 4, None, 0, None) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_set_split_override(9, 1) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_rmsnorm(None, 8, None, None, 8, 1, 8, 1e-5, None) == _lib.ERR_INVALID_VALUE
+    # misaligned output of the fp32 partial
+    assert lib.svdmlp_forward_partial(ctypes.byref(L), 1, 1, 64, 4, 2, 40, 256, 1 << 20, None) == _lib.ERR_ALIGNMENT
+
+
+def test_status_strings(lib):
+    from svdflash_b200 import _lib
+    for code in range(0, -10, -1):
+        assert lib.svdmlp_status_string(code)
+    assert b"positive" in lib.svdmlp_status_string(_lib.ERR_INVALID_VALUE)
+    assert b"SMEM/TMEM budget" in lib.svdmlp_status_string(_lib.ERR_BUDGET)
+
+
+def test_plan_info_is_deterministic(lib):
+    out = (ctypes.c_int * 6)()
+    assert lib.svdmlp_plan_info(1, 1024, 14336, 2867, out) == 0
+    assert list(out)[:3] == [4, 112, 45]          # 256-row CTA-pair tiles, BN=128, 64-wide k-blocks
+    assert out[3] == 1
+    assert lib.svdmlp_plan_info(1, 1, 14336, 2867, out) == 0
+    assert out[0] == 1 and out[3] >= 1 and out[4] == out[1] * out[3]
+
+
+def test_status_mapping_to_exceptions():
+    from svdflash_b200 import _lib
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ERR_SHAPE_MISMATCH)
+    with pytest.raises(TypeError):
+        _lib.check(_lib.ERR_DTYPE)
+    with pytest.raises(_lib.SvdMlpError):
+        _lib.check(_lib.ERR_DEVICE_TIMEOUT)
+    _lib.check(_lib.OK)

@@ -1,0 +1,117 @@
+"""GPU tests of the model hook, the launcher-name API, the block stack (eager
+and CUDA graph) and the single-GPU tensor-parallel path, against the oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import svdmlp_oracle as orc
+from helpers import assert_close, to_dev, to_np
+
+pytestmark = pytest.mark.gpu
+
+
+def test_svd_module_3d_input_and_linear_order(cuda_device):
+    from svdflash_b200.models import SvdLlamaMLP
+    b, s, h, r, i = 2, 70, 256, 96, 512
+    x, f = orc.make_inputs(31, b * s, h, i, r)
+    fd = [to_dev(a, cuda_device) for a in f]
+    mod = SvdLlamaMLP(*fd)
+    y = mod(to_dev(x, cuda_device).reshape(b, s, h))
+    assert tuple(y.shape) == (b, s, h)
+    ref = orc.svd_mlp(x, *f)
+    assert_close(to_np(y).reshape(b * s, h), ref, what="module")
+    # torch.nn.Linear order: *_v_proj [r, in] (first factor^T), *_u_proj [out, r]
+    mod2 = SvdLlamaMLP.from_torch_linear_factors(fd[0].t(), fd[1].t(), fd[2].t(), fd[3].t(), fd[4].t(), fd[5].t())
+    y2 = mod2(to_dev(x, cuda_device))
+    torch.testing.assert_close(y2, y.reshape(b * s, h), rtol=0, atol=0)
+
+
+def test_launcher_names(cuda_device):
+    from svdflash_b200.kernels import launchers
+    s, h, r, i = 40, 128, 64, 256
+    x, f = orc.make_inputs(32, s, h, i, r)
+    ug, vg, uu, vu, ud, vd = [to_dev(a, cuda_device) for a in f]
+    xd = to_dev(x, cuda_device)
+    y = launchers.svd_mlp_with_fused_kernel(xd, uu, vu, ug, vg, ud, vd)   # up-before-gate order
+    assert_close(to_np(y), orc.svd_mlp(x, *f), what="svd_mlp_with_fused_kernel")
+    ht = launchers.fused_mlp_up_T(xd, ug, vg, uu, vu)
+    assert tuple(ht.shape) == (i, s)
+    y2 = launchers.fused_three_mm_XTUV(ht, ud, vd)
+    hb = orc.bf16_round(orc.fused_gate_up(x, *f[:4]))
+    assert_close(to_np(y2), orc.fused_xuv(hb, f[4], f[5]), what="XTUV")
+    y3 = launchers.nki_mm(xd, uu.t(), vu.t(), ug.t(), vg.t(), ud.t(), vd.t())
+    assert_close(to_np(y3), orc.svd_mlp(x, *f), what="nki_mm")
+    wg, wu, wd = orc.make_dense(33, h, i)
+    yd = launchers.nki_baseline(xd, to_dev(wu, cuda_device).t(), to_dev(wg, cuda_device).t(), to_dev(wd, cuda_device).t())
+    assert_close(to_np(yd), orc.dense_mlp(x, wg, wu, wd), what="nki_baseline")
+
+
+def test_block_stack_eager_and_graph(cuda_device):
+    from svdflash_b200.models import MlpBlockStack, SvdLlamaMLP
+    m, h, r, i, layers = 200, 256, 72, 512, 3
+    rng = np.random.default_rng(40)
+    x = orc.bf16_round(rng.standard_normal((m, h), dtype=np.float32))
+    facs, norms = [], []
+    for l in range(layers):
+        _, f = orc.make_inputs(41 + l, 1, h, i, r)
+        facs.append(f)
+        norms.append(orc.bf16_round(1 + 0.02 * rng.standard_normal(h, dtype=np.float32)))
+    stack = MlpBlockStack([SvdLlamaMLP(*[to_dev(a, cuda_device) for a in f]) for f in facs],
+                          [to_dev(w, cuda_device) for w in norms], eps=1e-5)
+    ref = x
+    for f, w in zip(facs, norms):
+        ref = orc.mlp_block(ref, w, f, eps=1e-5)
+    y = stack(to_dev(x, cuda_device))
+    assert_close(to_np(y), ref, rel=1e-2, max_abs_rms=4e-2, what="stack eager (bf16 residual stream)")
+    stack.capture(m, h, cuda_device)
+    yg = stack.replay(to_dev(x, cuda_device))
+    torch.cuda.synchronize()
+    torch.testing.assert_close(yg, y, rtol=0, atol=0)
+
+
+def test_tensor_parallel_single_rank(cuda_device):
+    from svdflash_b200.tp import TensorParallelSvdMlp
+    m, h, r, i = 150, 256, 100, 512
+    x, f = orc.make_inputs(50, m, h, i, r)
+    tp = TensorParallelSvdMlp(*[to_dev(a, cuda_device) for a in f], rank=0, world=1)
+    y = tp(to_dev(x, cuda_device))
+    assert_close(to_np(y), orc.svd_mlp(x, *f), what="tp world=1")
+
+
+def test_tensor_parallel_shards_summed_on_one_gpu(cuda_device):
+    """Two ff-shards run on one GPU; their fp32 partials summed on the host side
+    of the exchange reproduce the full layer (the all-reduce's arithmetic)."""
+    from svdflash_b200.kernels import ops
+    from svdflash_b200.tp import TensorParallelSvdMlp
+    m, h, r, i = 64, 256, 100, 512
+    x, f = orc.make_inputs(51, m, h, i, r)
+    fd = [to_dev(a, cuda_device) for a in f]
+    xd = to_dev(x, cuda_device)
+    parts = []
+    shards = [TensorParallelSvdMlp(*fd, rank=p, world=2) for p in range(2)]
+    for sh in shards:
+        buf = sh._partial_buffer(m, cuda_device).clone()
+        ops.forward_partial_packed(sh.layer, xd, buf[:, :sh.r_d])
+        parts.append(buf)
+    total = parts[0] + parts[1]
+    y = ops.down_finish_packed(shards[0].layer, total[:, :r])
+    assert_close(to_np(y), orc.svd_mlp(x, *f), what="tp 2 shards on one gpu")
+    for p, sh in enumerate(shards):
+        want = orc.shard_partial(x, orc.shard_factors(f, p, 2))
+        got = to_np(parts[p][:, :r])
+        assert orc.error_metrics(got, want)["rel_fro"] < 5e-3
+
+
+def test_decode_sizes_split_k(cuda_device):
+    """M <= 128 runs the one-CTA split-K kernels (config 2 regime, small dims)."""
+    from svdflash_b200.kernels import ops
+    h, r, i = 1024, 764, 3584
+    _, f = orc.make_inputs(60, 1, h, i, r)
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f])
+    for m in (1, 8, 32, 128):
+        x = orc.bf16_round(np.random.default_rng(m).standard_normal((m, h), dtype=np.float32))
+        y = ops.svd_mlp_packed(layer, to_dev(x, cuda_device))
+        assert_close(to_np(y), orc.svd_mlp(x, *f), what=f"decode m={m}")
+    ops.check_device_status(cuda_device)
