@@ -192,6 +192,33 @@ int svdmlp_down_finish(const svdmlp_layout* layout, const void* packed, const fl
                        int64_t ld_partial, int m, void* y, int64_t ld_y, const void* residual,
                        int64_t ld_residual, void* workspace, int64_t workspace_bytes, void* stream);
 
+/*
+ * XUV down operator, y[M, d] = (h . u_down) . v_down, that allocates nothing
+ * and takes no workspace.  It has no counterpart in the reference.
+ *
+ * For callers that cannot allocate device memory: plugins hosted by a runtime
+ * that owns every device allocation and passes the plugin only its input and
+ * output buffers, and code that runs where cudaMalloc is not allowed.  The
+ * caller passes h and y (16-byte aligned, leading dimensions multiples of 8
+ * elements, else SVDMLP_ERR_ALIGNMENT); the scratch lives in a file-scope
+ * device array of 8 MiB inside the library, which every GPU that loads the
+ * library holds until the process exits.
+ *
+ * Limit: 256 + 4*ceil(M/128)*ceil(max(r_d, d)/128) (rounded up to 256) +
+ * 2*M*rp_d (rounded up to 256) + [full layers, ud_f16 = 1] 2*M*ld_ff (rounded
+ * up to 256) bytes must fit in 8 MiB; larger M is rejected with
+ * SVDMLP_ERR_WORKSPACE before any work is enqueued.  Split-K partials use the
+ * rest of the array when they fit; otherwise the GEMMs run unsplit.
+ *
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress, with that device current), so that first call should
+ * come before any stream capture.  Every call shares the one array and clears
+ * its error word and counters at the start; calls that overlap on the GPU
+ * (different streams, or different host threads on one device) race on it.
+ */
+int svdmlp_xuv_noalloc(const svdmlp_layout* layout, const void* packed, const void* h, int64_t ld_h, int m,
+                       void* y, int64_t ld_y, void* stream);
+
 /* --------------------------------------------------------- building blocks */
 /*
  * c[M, N] = a[M, K] . b[K, N] given b pre-transposed as bt[N, K] (K-major):

@@ -254,6 +254,9 @@ struct Workspace {
   bf16* ys;   // [M, ld_d] staging for unaligned y
   float* partials;
   int64_t partial_cap;
+  // When the split-K partials of a plan do not fit in partial_cap: false
+  // fails the call with SVDMLP_ERR_WORKSPACE, true runs the GEMM unsplit.
+  bool unsplit_if_short = false;
 };
 
 static constexpr int64_t kCtlBytes = 256;
@@ -347,7 +350,9 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
       done_mask |= 1ull << cur;
     }
   }
-  const Plan pl = plan_for<Cfg>(M, N, K, dev->sms, g_split_override[stage]);
+  Plan pl = plan_for<Cfg>(M, N, K, dev->sms, g_split_override[stage]);
+  if (partial_bytes(pl, Cfg::BN, Cfg::NB) > w.partial_cap && w.unsplit_if_short)
+    pl = plan_for<Cfg>(M, N, K, dev->sms, 1);
   GemmParams p{};
   p.M = M;
   p.N = N;
@@ -1032,6 +1037,76 @@ int svdmlp_set_split_override(int stage, int splits) {
   if (stage < 0 || stage >= 8 || splits < 0 || splits > 64) return SVDMLP_ERR_INVALID_VALUE;
   g_split_override[stage] = splits;
   return SVDMLP_OK;
+}
+
+// ----------------------------------------------------------------------------
+// XUV down operator with library-owned scratch, for callers that cannot
+// allocate device memory: plugins hosted by a runtime that owns every device
+// allocation and hands the plugin only its input and output buffers, and code
+// that runs where cudaMalloc is not allowed.  The scratch (control block,
+// split-K counters, the rank-r intermediate, the fp16 copy of H and, when they
+// fit, split-K partials) lives in this file-scope device array, one copy per
+// GPU that loads the library, kept until the process exits.
+// ----------------------------------------------------------------------------
+static constexpr int64_t kStaticScratchBytes = 8LL << 20;  // 8 MiB
+static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBytes];
+static std::mutex g_static_mu;
+static void* g_static_scratch_dev[64] = {};
+
+// Device address of g_static_scratch on the current device.  The host-side
+// name is only a stand-in; the address must come from cudaGetSymbolAddress,
+// called once per device with that device current.
+static int static_scratch_address(void** out) {
+  int dev = 0;
+  SVD_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return SVDMLP_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_static_mu);
+  if (!g_static_scratch_dev[dev]) {
+    void* p = nullptr;
+    SVD_CUDA(cudaGetSymbolAddress(&p, g_static_scratch));
+    if (!p) return SVDMLP_ERR_CUDA;
+    g_static_scratch_dev[dev] = p;
+  }
+  *out = g_static_scratch_dev[dev];
+  return SVDMLP_OK;
+}
+
+int svdmlp_xuv_noalloc(const svdmlp_layout* L, const void* packed, const void* h, int64_t ldh, int M, void* y,
+                       int64_t ldy, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_d <= 0 || !packed || !h || !y || M <= 0 || ldh < L->ff || ldy < L->d)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if (!aligned16(h, ldh) || !aligned16(y, ldy)) return SVDMLP_ERR_ALIGNMENT;
+  const int64_t cnt = round_up(cdiv(M, 128) * cdiv(std::max(L->r_d, L->d), 128) * 4, 256);
+  const int64_t t_bytes = round_up(static_cast<int64_t>(M) * L->rp_d * 2, 256);
+  const int64_t h_bytes = L->ud_f16 ? round_up(static_cast<int64_t>(M) * L->ld_ff * 2, 256) : 0;
+  const int64_t need = kCtlBytes + cnt + t_bytes + h_bytes;
+  if (need > kStaticScratchBytes) return SVDMLP_ERR_WORKSPACE;
+  void* base = nullptr;
+  SVD_CHECK(static_scratch_address(&base));
+  uint8_t* p = static_cast<uint8_t*>(base);
+  Workspace w{};
+  w.err = reinterpret_cast<int*>(p);
+  w.counters = reinterpret_cast<int*>(p + kCtlBytes);
+  w.t = reinterpret_cast<__half*>(p + kCtlBytes + cnt);
+  w.h = reinterpret_cast<__half*>(p + kCtlBytes + cnt + t_bytes);
+  w.partials = reinterpret_cast<float*>(p + need);
+  w.partial_cap = kStaticScratchBytes - need;
+  w.unsplit_if_short = true;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: the error word and the
+  // split-K counters must start at zero.
+  SVD_CUDA(cudaMemsetAsync(p, 0, static_cast<size_t>(kCtlBytes + cnt), s));
+  const void* ha = h;
+  int64_t ldha = ldh;
+  if (L->ud_f16) {
+    SVD_CHECK(launch_convert<bf16, __half>(static_cast<const bf16*>(h), ldh, w.h, L->ld_ff, M, L->ff, s));
+    ha = w.h;
+    ldha = L->ld_ff;
+  }
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  SVD_CHECK(run_down_u(L, P, ha, ldha, L->ud_f16 != 0, M, nullptr, 0, w, s));
+  return run_down_v(L, P, M, y, ldy, nullptr, 0, w, s);
 }
 
 int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
