@@ -347,8 +347,14 @@ def main():
             stage_us[nm] = 1e3 * ms_arr[i] / cnt_arr[i]
     r_loc = r
     ff_loc = ff // world
+    rp = (r + 7) // 8 * 8
     stage_flops = {"xu": 4.0 * m * d * r_loc, "gate_up": 4.0 * m * r_loc * ff_loc, "down_u": 2.0 * m * ff_loc * r_loc,
                    "down_v": 2.0 * m * r_loc * d}
+    # minimum HBM bytes per launch: the stage's weights once + its activations in and out
+    stage_bytes = {"xu": 2.0 * 2 * rp * d + 2.0 * m * d + 2.0 * m * 2 * rp,
+                   "gate_up": 2.0 * 2 * ff_loc * rp + 2.0 * m * 2 * rp + 2.0 * m * ff_loc,
+                   "down_u": 2.0 * rp * ff_loc + 2.0 * m * ff_loc + (4.0 if world > 1 else 2.0) * m * rp,
+                   "down_v": 2.0 * d * rp + 2.0 * m * rp + 2.0 * m * d}
 
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -359,18 +365,27 @@ def main():
     peaks, peak_src = load_peaks()
     dominant = max(stage_us, key=stage_us.get) if stage_us else None
     roofline = None
+    hbm_bound = m <= 128   # decode: intensity ~ M FLOP/B, far below the ridge
     if dominant:
-        achieved = stage_flops[dominant] / (stage_us[dominant] * 1e-6) / 1e12
-        peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
         traffic = None
         tfile = ROOT / "profiles" / "traffic_per_launch.json"
         if tfile.exists():
-            traffic = json.loads(tfile.read_text()).get(f"{args.workload}/{dominant}")
-        roofline = {"bound": "tensor", "kernel": f"{dominant} ({'dual SwiGLU' if dominant == 'gate_up' else 'plain'} tcgen05 GEMM)",
-                    "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-                    "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long run)",
-                    "traffic": traffic,
-                    "algorithmic_flops_per_launch": stage_flops[dominant]}
+            traffic = json.loads(tfile.read_text()).get(f"{args.workload}/n{world}/{dominant}")
+        kname = f"{dominant} ({'dual SwiGLU' if dominant == 'gate_up' else 'plain'} tcgen05 GEMM)"
+        if hbm_bound:
+            achieved = stage_bytes[dominant] / (stage_us[dominant] * 1e-6) / 1e9
+            peak = float(peaks["hbm_gbs"])
+            roofline = {"bound": "hbm", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                        "frac": achieved / peak, "peak_source": f"{peak_src} hbm_gbs (copy bandwidth)",
+                        "traffic": traffic, "algorithmic_bytes_per_launch": stage_bytes[dominant]}
+        else:
+            achieved = stage_flops[dominant] / (stage_us[dominant] * 1e-6) / 1e12
+            peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+            roofline = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                        "frac": achieved / peak,
+                        "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long run)",
+                        "traffic": traffic, "algorithmic_flops_per_launch": stage_flops[dominant]}
+    layer_bytes = sum(stage_bytes.values())
     tokens_per_s = m / (ms_per_step * 1e-3)
     line = {
         "metric": METRIC,
@@ -391,6 +406,7 @@ def main():
         "us_per_layer": ms_per_step * 1e3,
         "tflops": flops_layer / (ms_per_step * 1e-3) / 1e12,
         "stage_us": stage_us,
+        "hbm_gbs_layer": layer_bytes / (ms_per_step * 1e-3) / 1e9,
         "roofline": roofline,
         "e2e": {"value": m / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": m * d * 2,
                 "d2h_bytes_per_step": m * d * 2, "ms_per_step": e2e_ms},

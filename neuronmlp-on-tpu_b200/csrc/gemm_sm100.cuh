@@ -12,12 +12,15 @@
 // tensor-core rate, which keeps the layer well inside the max-abs error bound
 // that bf16 intermediates overshoot.
 //
-// Roles (192 threads per CTA, one CTA per SM):
-//   warps 0-3  epilogue: TMEM -> registers -> (math) -> swizzled smem -> TMA store
-//   warp  4    TMA producer: STAGES-deep smem ring of 128B-swizzled K-major tiles
-//   warp  5    TMEM allocator + single-thread tcgen05.mma issuer
-// Accumulators are double-buffered in TMEM so the epilogue of one tile
-// overlaps the main loop of the next.
+// Roles (one CTA per SM):
+//   warps 0..E-1  epilogue (E = 4 or 8): TMEM -> registers -> (math) ->
+//                 swizzled smem -> TMA store
+//   warp  E       TMA producer: STAGES-deep smem ring of 128B-swizzled K-major tiles
+//   warp  E+1     TMEM allocator + single-thread tcgen05.mma issuer
+// Accumulators are double-buffered in TMEM when two fit in its 512 columns,
+// so that the epilogue of one tile overlaps the main loop of the next; wider
+// tiles use one buffer that the epilogue releases as soon as its TMEM reads
+// have returned.
 //
 // CTAS == 2 (a cluster of two CTAs on two SMs): a tile is 256 x BN; each CTA
 // loads its own 128 rows of A and half (BN/2 rows) of B, and the even CTA
@@ -71,10 +74,17 @@ struct GemmParams {
   long long ld_residual;
 };
 
-template <int BN_, int NB_, bool SHARED_A_, int STAGES_, int EPI_, bool IN_F16_, int OUT_, int CTAS_ = 1>
+template <int BN_, int NB_, bool SHARED_A_, int STAGES_, int EPI_, bool IN_F16_, int OUT_, int CTAS_ = 1,
+          int EPI_WARPS_ = 4>
 struct GemmCfg {
   static constexpr int BM = 128, BK = 64;  // rows per CTA, K per stage
   static constexpr int BN = BN_, NB = NB_, STAGES = STAGES_, EPI = EPI_, OUT = OUT_, CTAS = CTAS_;
+  // Epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter,
+  // each taking every other 32-column chunk).  Warps EPI_WARPS and
+  // EPI_WARPS + 1 are the TMA producer and the MMA issuer.
+  static constexpr int EPI_WARPS = EPI_WARPS_;
+  static constexpr int THREADS = 32 * (EPI_WARPS + 2);
+  static constexpr int PRODUCER_WARP = EPI_WARPS, MMA_WARP = EPI_WARPS + 1;
   static constexpr bool IN_F16 = IN_F16_;
   static constexpr bool SHARED_A = SHARED_A_;
   static constexpr int NA = (NB == 2 && !SHARED_A) ? 2 : 1;
@@ -85,6 +95,7 @@ struct GemmCfg {
   static_assert(B_ROWS % 8 == 0, "B half-tile must hold whole 8-row core-matrix groups");
   static_assert(NB == 1 || NB == 2, "one or two accumulators per tile");
   static_assert(NB == 1 || EPI == EPI_SWIGLU, "dual GEMMs use the SwiGLU epilogue");
+  static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "four or eight epilogue warps");
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
   static constexpr int STAGE_BYTES = NA * A_BYTES + NB * B_BYTES;  // per CTA
@@ -93,7 +104,10 @@ struct GemmCfg {
   static constexpr int STG_BYTES = 32 * 32 * OUT_ELT;  // one 32x32 output box per warp buffer
   static constexpr int BSTRIDE = BN <= 128 ? 128 : 256;  // TMEM columns between the two branches
   static constexpr int ACC_STRIDE = NB * BSTRIDE;        // TMEM columns per accumulator buffer
-  static_assert(2 * ACC_STRIDE <= 512, "double-buffered accumulators must fit in 512 TMEM columns");
+  // Two accumulator buffers when they fit in 512 TMEM columns (the epilogue
+  // of one tile overlaps the next tile's main loop); one otherwise.
+  static constexpr int ACC_BUFS = 2 * ACC_STRIDE <= 512 ? 2 : 1;
+  static_assert(ACC_BUFS * ACC_STRIDE <= 512, "accumulators must fit in 512 TMEM columns");
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t IDESC = make_idesc_16bit(TILE_M, BN, IN_F16);
 
@@ -102,7 +116,7 @@ struct GemmCfg {
   static constexpr int OFF_B = OFF_A2 + (NA == 2 ? STAGES * A_BYTES : 0);
   static constexpr int OFF_B2 = OFF_B + STAGES * B_BYTES;
   static constexpr int OFF_STG = OFF_B2 + (NB == 2 ? STAGES * B_BYTES : 0);
-  static constexpr int OFF_BAR = OFF_STG + 4 * 2 * STG_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + EPI_WARPS * 2 * STG_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 5;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;  // + slack for 1024-byte alignment
@@ -240,7 +254,7 @@ SVD_DEV void issue_stage_loads(const CUtensorMap* tm_a, const CUtensorMap* tm_a2
 }
 
 template <class Cfg>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(Cfg::THREADS, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a2,
                       const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b2,
                       const __grid_constant__ CUtensorMap tm_out, const GemmParams p) {
@@ -272,7 +286,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4 * Cfg::CTAS);
+      mbar_init(&acc_empty[b], Cfg::EPI_WARPS * Cfg::CTAS);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -280,14 +294,14 @@ __global__ void __launch_bounds__(192, 1)
     *epi_abort = 0;
     fence_mbarrier_init();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == Cfg::PRODUCER_WARP && lane == 0) {
     prefetch_tensormap(&tm_a);
     if (Cfg::NA == 2) prefetch_tensormap(&tm_a2);
     prefetch_tensormap(&tm_b);
     if (Cfg::NB == 2) prefetch_tensormap(&tm_b2);
     prefetch_tensormap(&tm_out);
   }
-  if (warp == 5) {
+  if (warp == Cfg::MMA_WARP) {
     if constexpr (PAIR) {
       tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
       tmem_relinquish_pair();
@@ -303,7 +317,7 @@ __global__ void __launch_bounds__(192, 1)
   const uint32_t tmem_base = *tmem_slot;
   const WaitCtx ctx{abort_flag, p.err, p.timeout_ns};
 
-  if (warp == 4) {
+  if (warp == Cfg::PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       grid_dependency_wait();  // inputs of this launch come from the previous one
@@ -343,15 +357,15 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == Cfg::MMA_WARP) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0 && leader) {
       int it = 0, acc_it = 0;
       bool ok = true;
       for (int u = unit0; u < p.num_units && ok; u += unit_step) {
         const UnitCoord c = decode_unit(p, u);
-        const int b = acc_it & 1;
-        const uint32_t aph = static_cast<uint32_t>(acc_it >> 1) & 1u;
+        const int b = acc_it % Cfg::ACC_BUFS;
+        const uint32_t aph = static_cast<uint32_t>(acc_it / Cfg::ACC_BUFS) & 1u;
         if (!mbar_wait(&acc_empty[b], aph ^ 1u, ctx, SITE_MMA_ACC_EMPTY)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
@@ -397,21 +411,25 @@ __global__ void __launch_bounds__(192, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp;  // TMEM lane quarter == rows [32q, 32q + 32) of this CTA's rows
-    uint8_t* stg_warp = smem + Cfg::OFF_STG + q * 2 * Cfg::STG_BYTES;
+    const int q = warp & 3;          // TMEM lane quarter == rows [32q, 32q + 32) of this CTA's rows
+    const int half = warp >> 2;      // with eight epilogue warps: which chunks this warp takes
+    constexpr int CH_STEP = Cfg::EPI_WARPS / 4;
+    constexpr int NCH = Cfg::BN / 32;
+    uint8_t* stg_warp = smem + Cfg::OFF_STG + warp * 2 * Cfg::STG_BYTES;
     const uint32_t acc_empty_leader0 = PAIR ? mapa_shared(smem_addr(&acc_empty[0]), 0) : 0u;
+    constexpr int EPI_THREADS = 32 * Cfg::EPI_WARPS;
     int stg_buf = 0;
     int acc_it = 0;
     for (int u = unit0; u < p.num_units; u += unit_step) {
       const UnitCoord c = decode_unit(p, u);
-      const int b = acc_it & 1;
-      const uint32_t aph = static_cast<uint32_t>(acc_it >> 1) & 1u;
+      const int b = acc_it % Cfg::ACC_BUFS;
+      const uint32_t aph = static_cast<uint32_t>(acc_it / Cfg::ACC_BUFS) & 1u;
       bool ok = mbar_wait(&acc_full[b], aph, ctx, SITE_EPI_ACC_FULL);
       ok = __all_sync(0xffffffffu, ok);
-      // The four epilogue warps take the same decision, so that none of them
-      // is left alone at a named barrier below.
+      // The epilogue warps take the same decision, so that none of them is
+      // left alone at a named barrier below.
       if (!ok && lane == 0) *epi_abort = 1;
-      named_barrier_sync(2, 128);
+      named_barrier_sync(2, EPI_THREADS);
       if (*epi_abort) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
@@ -421,16 +439,16 @@ __global__ void __launch_bounds__(192, 1)
       const int n0 = c.n_t * Cfg::BN;
       const int y_box = row_base + q * 32;
 
-      if (p.splits == 1) {
+      if (Cfg::CTAS == 2 || p.splits == 1) {
 #pragma unroll 1
-        for (int ch = 0; ch < Cfg::BN / 32; ++ch) {
+        for (int ch = half; ch < NCH; ch += CH_STEP) {
           uint32_t rg[32];
           uint32_t ru[32];
           tmem_ld_x32(tacc + ch * 32, rg);
           if constexpr (Cfg::NB == 2) tmem_ld_x32(tacc + Cfg::BSTRIDE + ch * 32, ru);
           tmem_ld_wait();
-          if (ch == Cfg::BN / 32 - 1) {
-            // Every TMEM read of this buffer has returned: release it early.
+          if (ch + CH_STEP >= NCH) {
+            // This warp's TMEM reads of the buffer have all returned: release it.
             tc_fence_before();
             __syncwarp();
             if (lane == 0) {
@@ -447,12 +465,12 @@ __global__ void __launch_bounds__(192, 1)
           epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
           store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
         }
-      } else {
+      } else if constexpr (Cfg::CTAS == 1) {
         // Pass 1: publish this split's fp32 partial tile (valid rows only).
         float* slot = p.partials + static_cast<size_t>(c.tile * p.splits + c.ks) * Cfg::NB * (Cfg::BM * Cfg::BN);
         const bool row_ok = grow < p.M;
 #pragma unroll 1
-        for (int ch = 0; ch < Cfg::BN / 32; ++ch) {
+        for (int ch = half; ch < NCH; ch += CH_STEP) {
 #pragma unroll
           for (int br = 0; br < Cfg::NB; ++br) {
             uint32_t r[32];
@@ -472,17 +490,17 @@ __global__ void __launch_bounds__(192, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(&acc_empty[b]);  // TMEM no longer needed for this unit
         __threadfence();
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, EPI_THREADS);
         if (threadIdx.x == 0) {
           const int old = atomicAdd(&p.counters[c.tile], 1);
           *fix_flag = (old == p.splits - 1) ? 1 : 0;
         }
-        named_barrier_sync(1, 128);
+        named_barrier_sync(1, EPI_THREADS);
         if (*fix_flag) {
           __threadfence();
           const float* base = p.partials + static_cast<size_t>(c.tile * p.splits) * Cfg::NB * (Cfg::BM * Cfg::BN);
 #pragma unroll 1
-          for (int ch = 0; ch < Cfg::BN / 32; ++ch) {
+          for (int ch = half; ch < NCH; ch += CH_STEP) {
             float v[32], w[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -515,6 +533,7 @@ __global__ void __launch_bounds__(192, 1)
             epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
             store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
           }
+          named_barrier_sync(1, EPI_THREADS);
           if (threadIdx.x == 0) p.counters[c.tile] = 0;
         }
       }
@@ -526,7 +545,7 @@ __global__ void __launch_bounds__(192, 1)
 
   __syncthreads();
   if constexpr (PAIR) cluster_sync();  // the peer's MMAs and arrivals are done
-  if (warp == 5) {
+  if (warp == Cfg::MMA_WARP) {
     tc_fence_after();
     if constexpr (PAIR) tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
     else tmem_dealloc(tmem_base, Cfg::TMEM_COLS);

@@ -216,18 +216,46 @@ static int64_t partial_bytes(const Plan& p, int BN, int NB) {
 }
 
 // ------------------------------------------------------------ kernel configs
+// Tile choices of the prefill kernels (compile-time; the defaults are the
+// tuned values, other values serve tile sweeps).
+// Dual gate/up tile: 256 x 224 per branch (one TMEM buffer of 2 x 256
+// columns) moves 68.6 bytes of operands per MMA cycle per SM against 96 for
+// 256 x 128 (double-buffered); L2-to-SM bandwidth (~11-12 TB/s) bounds these
+// kernels, so the wider tile wins (measured 166 vs 199 us at config 1).
+#ifndef SVDMLP_GU_BN
+#define SVDMLP_GU_BN 224      // per-branch N of the dual gate/up tile
+#endif
+#ifndef SVDMLP_GU_STAGES
+#define SVDMLP_GU_STAGES 3
+#endif
+#ifndef SVDMLP_GU_EPI_WARPS
+#define SVDMLP_GU_EPI_WARPS 8
+#endif
+#ifndef SVDMLP_DENSE_GU_STAGES
+#define SVDMLP_DENSE_GU_STAGES 4
+#endif
+#ifndef SVDMLP_PLAIN_STAGES
+#define SVDMLP_PLAIN_STAGES 6
+#endif
+#ifndef SVDMLP_PLAIN_EPI_WARPS
+#define SVDMLP_PLAIN_EPI_WARPS 4
+#endif
+constexpr int kGuBn = SVDMLP_GU_BN, kGuSt = SVDMLP_GU_STAGES, kGuEw = SVDMLP_GU_EPI_WARPS;
+constexpr int kDgSt = SVDMLP_DENSE_GU_STAGES;
+constexpr int kPlSt = SVDMLP_PLAIN_STAGES, kPlEw = SVDMLP_PLAIN_EPI_WARPS;
+
 // Prefill (M > 128): CTA pairs, 256-row tiles.
-//                          BN  NB shared STG epilogue   fp16-in out       CTAs
-using CfgXU     = GemmCfg<256, 1, false, 6, EPI_PLAIN,  false, OUT_F16,  2>;  // X.[u_g|u_u] -> XU (fp16)
-using CfgGU     = GemmCfg<128, 2, false, 4, EPI_SWIGLU, true,  OUT_F16,  2>;  // XU.v -> H (fp16, internal)
-using CfgGUbf   = GemmCfg<128, 2, false, 4, EPI_SWIGLU, true,  OUT_BF16, 2>;  // XU.v -> H (bf16, to the caller)
-using CfgDU     = GemmCfg<256, 1, false, 6, EPI_PLAIN,  true,  OUT_F16,  2>;  // H.u_down -> T (fp16)
-using CfgDUbf   = GemmCfg<256, 1, false, 6, EPI_PLAIN,  false, OUT_F16,  2>;  // bf16 H.u_down (down-only layout)
-using CfgDUf32  = GemmCfg<256, 1, false, 6, EPI_PLAIN,  true,  OUT_F32,  2>;  // H.u_down -> fp32 partial (TP)
-using CfgDV     = GemmCfg<256, 1, false, 6, EPI_PLAIN,  true,  OUT_BF16, 2>;  // T.v_down -> y
-using CfgDVres  = GemmCfg<256, 1, false, 6, EPI_RESID,  true,  OUT_BF16, 2>;  // T.v_down + residual -> y
-using CfgDenseGU = GemmCfg<128, 2, true, 6, EPI_SWIGLU, false, OUT_F16,  2>;  // X.[w_g|w_u] -> H (fp16)
-using CfgGemm   = GemmCfg<256, 1, false, 6, EPI_PLAIN,  false, OUT_BF16, 2>;  // plain bf16 GEMM
+//                          BN     NB shared STG    epilogue   fp16-in out       CTAs epi-warps
+using CfgXU     = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  false, OUT_F16,  2, kPlEw>;  // X.[u_g|u_u] -> XU
+using CfgGU     = GemmCfg<kGuBn, 2, false, kGuSt, EPI_SWIGLU, true,  OUT_F16,  2, kGuEw>;  // XU.v -> H (internal)
+using CfgGUbf   = GemmCfg<kGuBn, 2, false, kGuSt, EPI_SWIGLU, true,  OUT_BF16, 2, kGuEw>;  // XU.v -> H (to caller)
+using CfgDU     = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_F16,  2, kPlEw>;  // H.u_down -> T
+using CfgDUbf   = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  false, OUT_F16,  2, kPlEw>;  // bf16 H.u_down
+using CfgDUf32  = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_F32,  2, kPlEw>;  // H.u_down -> fp32 (TP)
+using CfgDV     = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_BF16, 2, kPlEw>;  // T.v_down -> y
+using CfgDVres  = GemmCfg<256,   1, false, kPlSt, EPI_RESID,  true,  OUT_BF16, 2, kPlEw>;  // + residual
+using CfgDenseGU = GemmCfg<kGuBn, 2, true, kDgSt, EPI_SWIGLU, false, OUT_F16,  2, kGuEw>;  // X.[w_g|w_u] -> H
+using CfgGemm   = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  false, OUT_BF16, 2, kPlEw>;  // plain bf16 GEMM
 // Decode (M <= 128): one CTA per tile, split-K across the SMs.
 using CfgXU1     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_F16>;
 using CfgGU1     = GemmCfg<128, 2, false, 3, EPI_SWIGLU, true,  OUT_F16>;
@@ -373,7 +401,7 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(Cfg::THREADS);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
@@ -1111,10 +1139,10 @@ int svdmlp_xuv_noalloc(const svdmlp_layout* L, const void* packed, const void* h
 
 int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
   if (!out6 || M <= 0 || N <= 0 || K <= 0 || stage < 0 || stage >= 8) return SVDMLP_ERR_INVALID_VALUE;
-  const int bn = (stage == ST_GATEUP || stage == ST_DENSE_GU) ? 128 : 256;
-  const int nb = (stage == ST_GATEUP || stage == ST_DENSE_GU) ? 2 : 1;
-  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, N, K, bn, planning_sms())
-                                : plan_gemm(M, N, K, bn, nb, planning_sms(), g_split_override[stage]);
+  const bool dual = stage == ST_GATEUP || stage == ST_DENSE_GU;
+  const int nb = dual ? 2 : 1;
+  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, N, K, dual ? CfgGU::BN : 256, planning_sms())
+                                : plan_gemm(M, N, K, dual ? CfgGU1::BN : 256, nb, planning_sms(), g_split_override[stage]);
   out6[0] = p.m_tiles;
   out6[1] = p.n_tiles;
   out6[2] = p.k_blocks;

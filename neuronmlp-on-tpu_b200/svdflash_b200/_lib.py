@@ -92,7 +92,12 @@ _lib = None
 
 
 def lib_path():
-    return _build.LIB_PATH
+    """The shared library to load: $SVDMLP_LIBRARY (another build of the same
+    sources, e.g. a tile sweep) or the in-tree build."""
+    import os
+    import pathlib
+    env = os.environ.get("SVDMLP_LIBRARY")
+    return pathlib.Path(env) if env else _build.LIB_PATH
 
 
 def load() -> ctypes.CDLL:
@@ -100,7 +105,7 @@ def load() -> ctypes.CDLL:
     global _lib
     with _lock:
         if _lib is None:
-            path = _build.LIB_PATH
+            path = lib_path()
             if not path.exists():
                 raise RuntimeError(
                     f"libsvdmlp.so not found at {path}; build it with __graft_entry__.build() "

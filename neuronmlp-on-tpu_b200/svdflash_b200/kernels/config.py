@@ -26,7 +26,7 @@ for _m in MODELS.values():
 # Tile shapes of the B200 kernels (rows x K-block x N) and hardware budgets.
 BLOCK_M = 128          # tcgen05 MMA M (one TMEM lane per row)
 BLOCK_K = 64           # one 128-byte swizzle row of 16-bit elements
-GATE_UP_BLOCK_N = 128  # per branch; two accumulators (gate, up) per tile
+GATE_UP_BLOCK_N = 224  # per branch (prefill); two accumulators (gate, up) per tile
 DOWN_BLOCK_N = 256
 SMEM_BUDGET_BYTES = 232448   # 227 KB opt-in dynamic shared memory per CTA
 TMEM_COLUMNS = 512           # 128 lanes x 512 x 32-bit per SM
@@ -81,10 +81,19 @@ def _stage_smem(bn: int, nb: int, shared_a: bool, stages: int, out_bytes: int) -
     return stages * (na * a + nb * b) + staging + bars + 1024
 
 
+def _pair_stage_smem(bn: int, nb: int, shared_a: bool, stages: int, out_bytes: int, epi_warps: int) -> int:
+    a = BLOCK_M * BLOCK_K * 2
+    b = (bn // 2) * BLOCK_K * 2
+    na = 1 if (nb == 1 or shared_a) else 2
+    staging = epi_warps * 2 * 32 * 32 * out_bytes
+    bars = (2 * stages + 5) * 8 + 64
+    return stages * (na * a + nb * b) + staging + bars + 1024
+
+
 def smem_bytes_gate_up(blocks: GateUpBlocks | None = None, r_pad: int = 0, hidden: int = 0) -> int:
-    """Shared memory of the gate/up kernels (the larger of its two stages)."""
+    """Shared memory of the gate/up kernels (the larger of its two GEMM stages)."""
     del blocks, r_pad, hidden
-    return max(_stage_smem(256, 1, False, 4, 2), _stage_smem(128, 2, False, 3, 2))
+    return max(_pair_stage_smem(256, 1, False, 6, 2, 4), _pair_stage_smem(GATE_UP_BLOCK_N, 2, False, 3, 2, 8))
 
 
 def smem_bytes_xuv(intermediate: int = 0, r_pad: int = 0, hidden: int = 0) -> int:
@@ -97,7 +106,7 @@ def smem_bytes_gate_up_down_u(blocks=None, r_g: int = 0, r_d: int = 0, hidden: i
 
 
 def tmem_columns_gate_up() -> int:
-    return 2 * 2 * GATE_UP_BLOCK_N   # two branches, double-buffered
+    return 2 * 256   # two branches of up to 256 columns, one buffer
 
 
 def fits_smem(nbytes: int) -> bool:
