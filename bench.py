@@ -341,7 +341,7 @@ def main():
     lib.svdmlp_stage_times(ms_arr, cnt_arr, 8)
     lib.svdmlp_stage_timing(0)
     stage_us = {}
-    names = {0: "xu", 1: "gate_up", 2: "down_u", 3: "down_v"}
+    names = {0: "xu", 1: "gate_up", 2: "down_u", 3: "down_v", 7: "layer_decode"}
     for i, nm in names.items():
         if cnt_arr[i]:
             stage_us[nm] = 1e3 * ms_arr[i] / cnt_arr[i]
@@ -350,11 +350,13 @@ def main():
     rp = (r + 7) // 8 * 8
     stage_flops = {"xu": 4.0 * m * d * r_loc, "gate_up": 4.0 * m * r_loc * ff_loc, "down_u": 2.0 * m * ff_loc * r_loc,
                    "down_v": 2.0 * m * r_loc * d}
+    stage_flops["layer_decode"] = sum(stage_flops.values())
     # minimum HBM bytes per launch: the stage's weights once + its activations in and out
     stage_bytes = {"xu": 2.0 * 2 * rp * d + 2.0 * m * d + 2.0 * m * 2 * rp,
                    "gate_up": 2.0 * 2 * ff_loc * rp + 2.0 * m * 2 * rp + 2.0 * m * ff_loc,
                    "down_u": 2.0 * rp * ff_loc + 2.0 * m * ff_loc + (4.0 if world > 1 else 2.0) * m * rp,
                    "down_v": 2.0 * d * rp + 2.0 * m * rp + 2.0 * m * d}
+    stage_bytes["layer_decode"] = sum(stage_bytes.values())
 
     if world > 1:
         dist.barrier(device_ids=[local])
@@ -371,7 +373,8 @@ def main():
         tfile = ROOT / "profiles" / "traffic_per_launch.json"
         if tfile.exists():
             traffic = json.loads(tfile.read_text()).get(f"{args.workload}/n{world}/{dominant}")
-        kname = f"{dominant} ({'dual SwiGLU' if dominant == 'gate_up' else 'plain'} tcgen05 GEMM)"
+        kname = {"gate_up": "gate_up (dual SwiGLU tcgen05 GEMM)",
+                 "layer_decode": "layer_decode (whole-layer tcgen05 decode kernel)"}.get(dominant, f"{dominant} (tcgen05 GEMM)")
         if hbm_bound:
             achieved = stage_bytes[dominant] / (stage_us[dominant] * 1e-6) / 1e9
             peak = float(peaks["hbm_gbs"])
@@ -385,7 +388,7 @@ def main():
                         "frac": achieved / peak,
                         "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long run)",
                         "traffic": traffic, "algorithmic_flops_per_launch": stage_flops[dominant]}
-    layer_bytes = sum(stage_bytes.values())
+    layer_bytes = stage_bytes["layer_decode"]
     tokens_per_s = m / (ms_per_step * 1e-3)
     line = {
         "metric": METRIC,

@@ -260,6 +260,17 @@ int svdmlp_debug_wait_timeout(void* workspace, int64_t workspace_bytes, int64_t 
  * svdmlp_plan_info writes {m_tiles, n_tiles, k_blocks, splits, units, grid}.
  */
 int svdmlp_set_split_override(int stage, int splits);
+
+/* svdmlp_forward runs layers of M <= 64 tokens as one whole-layer decode
+ * kernel (1, the default) or as four per-stage kernels (0). */
+int svdmlp_set_layer_decode(int enable);
+
+/* Timeline of the whole-layer decode kernel (tracing; NULL turns it off).
+ * Each launch writes, per CTA, 64 pairs of uint64 (tag | (unit + 1) << 8,
+ * globaltimer ns): tags 1 start, 2 unit claimed, 3/4 dependency wait
+ * begin/end, 5 unit epilogue done, 6 exit.  `buffer` is a device buffer of at
+ * least 2 * SMs * 64 * 16 bytes, zeroed by the caller. */
+int svdmlp_set_trace_buffer(void* buffer, int64_t bytes);
 int svdmlp_plan_info(int stage, int m, int n, int k, int* out6);
 
 /*

@@ -59,6 +59,7 @@ enum ErrSite : int {
   SITE_DRAIN_LOADS = 5,
   SITE_DRAIN_MMA = 6,
   SITE_PROBE = 7,
+  SITE_DEPENDENCY = 8,
 };
 
 struct GemmParams {

@@ -1,0 +1,527 @@
+// Whole-layer decode kernel (M <= 64 tokens) for sm_100a: the four GEMM
+// stages of one SVD MLP layer in one persistent, cooperative launch.
+//
+//   stage 0  XU = X . [u_g|u_u]                 (bf16 -> fp16)
+//   stage 1  H  = silu(XU_g . v_g) * (XU_u . v_u)   (fp16, dual)
+//   stage 2  T  = H . u_down                    (fp16)
+//   stage 3  y  = T . v_down (+ residual)       (bf16)
+//
+// At decode sizes every stage streams its factor matrix from HBM once; the
+// work is the weight bytes.  Running the stages as separate kernels pays a
+// launch, a pipeline ramp and a split-K hand-off per stage.  Here all units
+// of all stages form one list that the co-resident CTAs claim in order, and
+// a stage's units wait (bounded) on a per-stage "tiles done" counter before
+// they load their activation tiles.  The weight tiles never depend on an
+// earlier stage, so the producer fetches them before it waits: the weight
+// stream runs on across stage boundaries.
+//
+// Each unit is a 128-row panel of a stage's weight (the MMA M) over a K range
+// (split-K), times the tokens (the MMA N, TOK = 16 or 64, zero-filled beyond
+// M).  Units are claimed dynamically: the producer takes the next unit index
+// from a global counter and passes it to the MMA and epilogue warps through a
+// small shared-memory queue, so busy and idle CTAs even out at every stage
+// boundary; since units are claimed in order, a unit only ever waits on units
+// that running CTAs have already claimed.
+// A shared-memory slot holds two weight tiles and two token tiles: the
+// two branches (gate, up) of one k-block for the dual stage, or two
+// consecutive k-blocks for the other stages.  The split of a tile that
+// finishes last sums the fp32 partials in split order (deterministic), runs
+// the epilogue and bumps the stage's done counter.  The last CTA to leave
+// resets the counters.
+//
+// Roles: warps 0-3 epilogue, warp 4 TMA producer, warp 5 TMEM allocator and
+// MMA issuer.  Every wait is bounded (ptx.cuh).
+#pragma once
+
+#include "gemv_sm100.cuh"
+
+namespace svdmlp {
+
+struct alignas(64) DecStage {
+  CUtensorMap x, x2, w, w2;  // token operand(s) [M, K] and weight(s) [N, K], K-major
+  void* out;
+  long long ld_out;
+  float* partials;   // [tiles][splits][nb][128][TOK] fp32
+  int* tile_counters;
+  int N, K, n_tiles, k_blocks, splits, kb_per_split, units, unit_base;
+  int nb;            // 1, or 2 for the dual SwiGLU stage
+  int in_f16;        // operand type: fp16 (1) or bf16 (0)
+  int epi;           // EPI_PLAIN, EPI_SWIGLU or EPI_RESID
+  int out_kind;      // OUT_BF16, OUT_F16 or OUT_F32
+};
+
+struct LayerDecParams {
+  DecStage st[4];
+  int num_stages, M, total_units;
+  int* done;        // [4] tiles completed per stage in this launch
+  int* exit_count;  // CTAs that have left
+  int* next_unit;   // unit claim counter
+  int* err;
+  unsigned long long timeout_ns;
+  const __nv_bfloat16* residual;
+  long long ld_residual;
+  // Optional timeline (null: off): per CTA kTraceEvents pairs of
+  // (tag | unit << 8, globaltimer ns).
+  unsigned long long* trace;
+};
+
+// Trace tags of the whole-layer decode kernel.
+enum TraceTag : unsigned { TR_START = 1, TR_CLAIM = 2, TR_DEP_BEGIN = 3, TR_DEP_END = 4, TR_UNIT_DONE = 5, TR_END = 6 };
+constexpr int kTraceEvents = 64;
+
+SVD_DEV void trace_event(const LayerDecParams& p, int& n, unsigned tag, int unit) {
+  if (p.trace == nullptr || n >= kTraceEvents) return;
+  unsigned long long* e = p.trace + (static_cast<size_t>(blockIdx.x) * kTraceEvents + n) * 2;
+  e[0] = static_cast<unsigned long long>(tag) | (static_cast<unsigned long long>(unit + 1) << 8);
+  e[1] = global_timer_ns();
+  ++n;
+}
+
+template <int TOK_, int STAGES_>
+struct LayerDecCfg {
+  static constexpr int BM = 128, BK = 64, TOK = TOK_, STAGES = STAGES_;
+  static constexpr int W_BYTES = BM * BK * 2;
+  static constexpr int X_BYTES = TOK * BK * 2;
+  static constexpr int SLOT_BYTES = 2 * W_BYTES + 2 * X_BYTES;
+  static constexpr int ACC_BUFS = 2;
+  static constexpr int ACC_STRIDE = 2 * TOK;
+  static constexpr uint32_t TMEM_COLS = ACC_BUFS * ACC_STRIDE <= 64 ? 64 : ACC_BUFS * ACC_STRIDE <= 128 ? 128 : 256;
+  static constexpr int OFF_W = 0;                        // [slot][2] weight tiles
+  static constexpr int OFF_X = STAGES * 2 * W_BYTES;     // [slot][2] token tiles
+  static constexpr int OFF_BAR = OFF_X + STAGES * 2 * X_BYTES;
+  static constexpr int QUEUE = 4;  // claimed units in flight per CTA
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1 + 2 * QUEUE;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = OFF_MISC + 64 + 4 * QUEUE + 1024;
+  static_assert(X_BYTES % 1024 == 0, "token tiles stay 1024-byte aligned");
+  static_assert(SMEM_BYTES <= 113 * 1024, "two CTAs per SM");
+  static_assert(TOK == 16 || TOK == 64, "16 or 64 tokens per tile");
+};
+
+struct LdUnit {
+  int s, n_t, ks, kb0, kb1;
+};
+
+SVD_DEV LdUnit layer_dec_unit(const LayerDecParams& p, int u) {
+  int s = 0;
+  while (s + 1 < p.num_stages && u >= p.st[s + 1].unit_base) ++s;
+  const DecStage& st = p.st[s];
+  const int local = u - st.unit_base;
+  LdUnit c;
+  c.s = s;
+  c.ks = local % st.splits;
+  c.n_t = local / st.splits;
+  c.kb0 = c.ks * st.kb_per_split;
+  c.kb1 = min(c.kb0 + st.kb_per_split, st.k_blocks);
+  return c;
+}
+
+// Shared-memory slots a unit occupies: one per k-block for the dual stage
+// (two branches), one per pair of k-blocks otherwise.
+SVD_DEV int unit_slots(const LayerDecParams& p, const LdUnit& c) {
+  const int nk = c.kb1 - c.kb0;
+  return p.st[c.s].nb == 2 ? nk : (nk + 1) / 2;
+}
+
+template <int TOK>
+SVD_DEV void ld_store_chunk(const LayerDecParams& p, const DecStage& st, int f, int t0, const float (&v)[16]) {
+  if (f >= st.N) return;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int t = t0 + j;
+    if (t < p.M) {
+      float x = v[j];
+      if (st.epi == EPI_RESID) x += __bfloat162float(p.residual[static_cast<long long>(t) * p.ld_residual + f]);
+      const long long off = static_cast<long long>(t) * st.ld_out + f;
+      if (st.out_kind == OUT_F32) static_cast<float*>(st.out)[off] = x;
+      else if (st.out_kind == OUT_F16)
+        static_cast<__half*>(st.out)[off] = __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f));
+      else static_cast<__nv_bfloat16*>(st.out)[off] = __float2bfloat16(x);
+    }
+  }
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant__ LayerDecParams p) {
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr int TOK = Cfg::TOK;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::OFF_BAR);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + Cfg::ACC_BUFS;
+  uint64_t* drain = acc_empty + Cfg::ACC_BUFS;
+  uint64_t* q_full = drain + 1;            // [QUEUE] producer -> MMA, epilogue
+  uint64_t* q_empty = q_full + Cfg::QUEUE; // [QUEUE] MMA + 4 epilogue warps -> producer
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* fix_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
+  volatile int* epi_abort = reinterpret_cast<volatile int*>(tmem_slot + 3);
+  volatile int* unit_q = reinterpret_cast<volatile int*>(smem + Cfg::OFF_MISC + 64);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < Cfg::ACC_BUFS; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    mbar_init(drain, 1);
+    for (int i = 0; i < Cfg::QUEUE; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 5);
+    }
+    *abort_flag = 0;
+    *fix_flag = 0;
+    *epi_abort = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 4 && lane == 0) {
+    for (int s = 0; s < p.num_stages; ++s) {
+      prefetch_tensormap(&p.st[s].x);
+      prefetch_tensormap(&p.st[s].w);
+      if (p.st[s].nb == 2) {
+        prefetch_tensormap(&p.st[s].x2);
+        prefetch_tensormap(&p.st[s].w2);
+      }
+    }
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const WaitCtx ctx{abort_flag, p.err, p.timeout_ns};
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      // k-blocks of slot i of unit c: dual -> kb0 + i (both branches);
+      // otherwise kb0 + 2i and kb0 + 2i + 1 (the second may not exist).
+      auto slot_w = [&](const LdUnit& c, int i, int sl) {
+        const DecStage& st = p.st[c.s];
+        uint8_t* w0 = smem + Cfg::OFF_W + (sl * 2) * Cfg::W_BYTES;
+        uint8_t* w1 = w0 + Cfg::W_BYTES;
+        const int row = c.n_t * Cfg::BM;
+        if (st.nb == 2) {
+          tma_load_2d(&st.w, &full[sl], w0, (c.kb0 + i) * Cfg::BK, row);
+          tma_load_2d(&st.w2, &full[sl], w1, (c.kb0 + i) * Cfg::BK, row);
+        } else {
+          tma_load_2d(&st.w, &full[sl], w0, (c.kb0 + 2 * i) * Cfg::BK, row);
+          if (c.kb0 + 2 * i + 1 < c.kb1) tma_load_2d(&st.w, &full[sl], w1, (c.kb0 + 2 * i + 1) * Cfg::BK, row);
+        }
+      };
+      auto slot_x = [&](const LdUnit& c, int i, int sl) {
+        const DecStage& st = p.st[c.s];
+        uint8_t* x0 = smem + Cfg::OFF_X + (sl * 2) * Cfg::X_BYTES;
+        uint8_t* x1 = x0 + Cfg::X_BYTES;
+        if (st.nb == 2) {
+          tma_load_2d(&st.x, &full[sl], x0, (c.kb0 + i) * Cfg::BK, 0);
+          tma_load_2d(&st.x2, &full[sl], x1, (c.kb0 + i) * Cfg::BK, 0);
+        } else {
+          tma_load_2d(&st.x, &full[sl], x0, (c.kb0 + 2 * i) * Cfg::BK, 0);
+          if (c.kb0 + 2 * i + 1 < c.kb1) tma_load_2d(&st.x, &full[sl], x1, (c.kb0 + 2 * i + 1) * Cfg::BK, 0);
+        }
+      };
+      auto slot_bytes = [&](const LdUnit& c, int i) -> uint32_t {
+        const bool two = p.st[c.s].nb == 2 || c.kb0 + 2 * i + 1 < c.kb1;
+        return (two ? 2u : 1u) * (Cfg::W_BYTES + Cfg::X_BYTES);
+      };
+      int it = 0;  // slot index over the whole run
+      bool ok = true;
+      int ready_stage = 0;  // stages whose inputs are known complete (stage 0 always)
+      int ntr = 0;          // producer trace events (slots [0, 40))
+      trace_event(p, ntr, TR_START, -1);
+      for (int qi = 0; ok; ++qi) {
+        // claim the next unit and hand it to the MMA and epilogue warps
+        const int qs = qi % Cfg::QUEUE;
+        if (!mbar_wait(&q_empty[qs], (static_cast<uint32_t>(qi / Cfg::QUEUE) & 1u) ^ 1u, ctx, SITE_PRODUCER_EMPTY)) {
+          ok = false;
+          unit_q[qs] = -1;
+          mbar_arrive(&q_full[qs]);
+          break;
+        }
+        const int u = atomicAdd(p.next_unit, 1);
+        unit_q[qs] = u < p.total_units ? u : -1;
+        mbar_arrive(&q_full[qs]);  // release: the unit id is visible to the waiters
+        if (u >= p.total_units) break;
+        if (ntr < 40) trace_event(p, ntr, TR_CLAIM, u);
+        const LdUnit c = layer_dec_unit(p, u);
+        const int ns = unit_slots(p, c);
+        int i = 0;
+        if (c.s > ready_stage) {
+          // Weights first: as many slots as the ring frees up, then wait for
+          // the previous stage, then the token tiles of those slots.
+          int pre = 0;
+          for (; pre < min(ns, STAGES); ++pre) {
+            const int sl = (it + pre) % STAGES;
+            const uint32_t ph = static_cast<uint32_t>((it + pre) / STAGES) & 1u;
+            if (!mbar_wait(&empty[sl], ph ^ 1u, ctx, SITE_PRODUCER_EMPTY)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&full[sl], slot_bytes(c, pre));
+            slot_w(c, pre, sl);
+          }
+          if (!ok) break;
+          if (ntr < 40) trace_event(p, ntr, TR_DEP_BEGIN, u);
+          if (!wait_counter_geq(&p.done[c.s - 1], p.st[c.s - 1].n_tiles, ctx, SITE_DEPENDENCY)) {
+            // Complete the slots already announced with their token tiles so
+            // the barrier phases stay consistent, then stop.
+            ok = false;
+          }
+          if (ntr < 40) trace_event(p, ntr, TR_DEP_END, u);
+          fence_proxy_async_global();
+          for (int j = 0; j < pre; ++j) slot_x(c, j, (it + j) % STAGES);
+          it += pre;
+          i = pre;
+          ready_stage = c.s;
+          if (!ok) break;
+        }
+        for (; i < ns; ++i, ++it) {
+          const int sl = it % STAGES;
+          const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+          if (!mbar_wait(&empty[sl], ph ^ 1u, ctx, SITE_PRODUCER_EMPTY)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[sl], slot_bytes(c, i));
+          slot_w(c, i, sl);
+          slot_x(c, i, sl);
+        }
+      }
+      for (int s = 0; s < STAGES; ++s) {
+        if (it > s) {
+          const int last = s + ((it - 1 - s) / STAGES) * STAGES;
+          mbar_wait(&full[s], static_cast<uint32_t>(last / STAGES) & 1u, ctx, SITE_DRAIN_LOADS, false);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc_bf = make_idesc_16bit(Cfg::BM, TOK, false);
+      const uint32_t idesc_h = make_idesc_16bit(Cfg::BM, TOK, true);
+      int it = 0, acc_it = 0;
+      bool ok = true;
+      for (int qi = 0; ok; ++qi) {
+        const int qs = qi % Cfg::QUEUE;
+        if (!mbar_wait(&q_full[qs], static_cast<uint32_t>(qi / Cfg::QUEUE) & 1u, ctx, SITE_MMA_FULL)) break;
+        const int u = unit_q[qs];
+        mbar_arrive(&q_empty[qs]);
+        if (u < 0) break;
+        const LdUnit c = layer_dec_unit(p, u);
+        const DecStage& st = p.st[c.s];
+        const uint32_t idesc = st.in_f16 ? idesc_h : idesc_bf;
+        const int ns = unit_slots(p, c);
+        const int b = acc_it % Cfg::ACC_BUFS;
+        const uint32_t aph = static_cast<uint32_t>(acc_it / Cfg::ACC_BUFS) & 1u;
+        if (!mbar_wait(&acc_empty[b], aph ^ 1u, ctx, SITE_MMA_ACC_EMPTY)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
+        for (int i = 0; i < ns; ++i, ++it) {
+          const int sl = it % STAGES;
+          const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+          if (!mbar_wait(&full[sl], ph, ctx, SITE_MMA_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t w0 = smem_addr(smem + Cfg::OFF_W + (sl * 2) * Cfg::W_BYTES);
+          const uint32_t x0 = smem_addr(smem + Cfg::OFF_X + (sl * 2) * Cfg::X_BYTES);
+          const bool dual = st.nb == 2;
+          const bool second = dual || c.kb0 + 2 * i + 1 < c.kb1;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            if (h == 1 && !second) break;
+            const uint32_t wa = w0 + h * Cfg::W_BYTES, xa = x0 + h * Cfg::X_BYTES;
+            const uint32_t dd = dual ? d + h * TOK : d;
+#pragma unroll
+            for (int k = 0; k < Cfg::BK / 16; ++k) {
+              const bool first = i == 0 && k == 0 && (dual || h == 0);
+              umma_f16kind(dd, make_sw128_desc(wa + k * 32), make_sw128_desc(xa + k * 32), idesc, first ? 0u : 1u);
+            }
+          }
+          umma_commit(&empty[sl]);
+        }
+        if (!ok) break;
+        umma_commit(&acc_full[b]);
+        ++acc_it;
+      }
+      umma_commit(drain);
+      mbar_wait(drain, 0, ctx, SITE_DRAIN_MMA, false);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp;
+    int acc_it = 0;
+    int ntr = 40;  // epilogue trace events (slots [40, 64))
+    for (int qi = 0;; ++qi) {
+      const int qs = qi % Cfg::QUEUE;
+      bool qok = mbar_wait(&q_full[qs], static_cast<uint32_t>(qi / Cfg::QUEUE) & 1u, ctx, SITE_EPI_ACC_FULL);
+      qok = __all_sync(0xffffffffu, qok);
+      // The four warps take the same decision (a timed-out wait in any of
+      // them stops all), so that none is left alone at a named barrier.
+      if (!qok && lane == 0) *epi_abort = 1;
+      named_barrier_sync(2, 128);
+      if (*epi_abort) break;
+      const int u = unit_q[qs];  // the same entry for all four warps
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&q_empty[qs]);
+      if (u < 0) break;
+      const LdUnit c = layer_dec_unit(p, u);
+      const DecStage& st = p.st[c.s];
+      const int b = acc_it % Cfg::ACC_BUFS;
+      const uint32_t aph = static_cast<uint32_t>(acc_it / Cfg::ACC_BUFS) & 1u;
+      bool ok = mbar_wait(&acc_full[b], aph, ctx, SITE_EPI_ACC_FULL);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok && lane == 0) *epi_abort = 1;
+      named_barrier_sync(2, 128);
+      if (*epi_abort) break;
+      tc_fence_after();
+      const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
+      const int row = q * 32 + static_cast<int>(lane);
+      const int f = c.n_t * Cfg::BM + row;
+      const int tv = min(p.M, TOK);
+      const bool dual = st.nb == 2;
+      constexpr int NCH = TOK / 16;
+      const size_t tile_slot = static_cast<size_t>(c.n_t) * st.splits;
+      float* slot = st.partials + ((tile_slot + c.ks) * 2) * (Cfg::BM * TOK) + static_cast<size_t>(row) * TOK;
+#pragma unroll
+      for (int ch = 0; ch < NCH; ++ch) {
+        uint32_t rg[16], ru[16];
+        tmem_ld_x16(tacc + ch * 16, rg);
+        tmem_ld_x16(tacc + TOK + ch * 16, ru);  // unused columns for one-branch stages
+        tmem_ld_wait();
+        if (ch == NCH - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[b]);
+        }
+        if (16 * ch >= tv) continue;
+        float v[16], w[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          v[j] = __uint_as_float(rg[j]);
+          w[j] = __uint_as_float(ru[j]);
+        }
+        if (st.splits == 1) {
+          if (dual) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] = silu_mul(v[j], w[j]);
+          }
+          ld_store_chunk<TOK>(p, st, f, 16 * ch, v);
+        } else {
+#pragma unroll
+          for (int j4 = 0; j4 < 4; ++j4) {
+            __stcg(reinterpret_cast<float4*>(slot + 16 * ch) + j4,
+                   make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]));
+            if (dual)
+              __stcg(reinterpret_cast<float4*>(slot + Cfg::BM * TOK + 16 * ch) + j4,
+                     make_float4(w[4 * j4], w[4 * j4 + 1], w[4 * j4 + 2], w[4 * j4 + 3]));
+          }
+        }
+      }
+      bool finished = st.splits == 1;  // this unit completed its tile
+      if (st.splits > 1) {
+        // Every thread's partial stores, then one acq_rel increment: the
+        // barrier orders the stores before it and the release is cumulative.
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 0) {
+          const int old = atom_add_acq_rel_gpu(&st.tile_counters[c.n_t], 1);
+          *fix_flag = (old == st.splits - 1) ? 1 : 0;
+        }
+        named_barrier_sync(1, 128);
+        if (*fix_flag) {
+          const float* base = st.partials + (tile_slot * 2) * (Cfg::BM * TOK) + static_cast<size_t>(row) * TOK;
+#pragma unroll
+          for (int ch = 0; ch < NCH; ++ch) {
+            if (16 * ch >= tv) continue;
+            float v[16], w[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              v[j] = 0.f;
+              w[j] = 0.f;
+            }
+#pragma unroll 1
+            for (int s0 = 0; s0 < st.splits; s0 += 4) {
+              float4 g4[4][4], u4[4][4];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const bool have = s0 + j < st.splits;
+                const float* src = base + static_cast<size_t>((s0 + j) * 2) * (Cfg::BM * TOK) + 16 * ch;
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                  g4[j][j4] = have ? __ldcg(reinterpret_cast<const float4*>(src) + j4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                  u4[j][j4] = have && dual ? __ldcg(reinterpret_cast<const float4*>(src + Cfg::BM * TOK) + j4)
+                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+#pragma unroll
+                for (int j4 = 0; j4 < 4; ++j4) {
+                  v[4 * j4] += g4[j][j4].x;
+                  v[4 * j4 + 1] += g4[j][j4].y;
+                  v[4 * j4 + 2] += g4[j][j4].z;
+                  v[4 * j4 + 3] += g4[j][j4].w;
+                  w[4 * j4] += u4[j][j4].x;
+                  w[4 * j4 + 1] += u4[j][j4].y;
+                  w[4 * j4 + 2] += u4[j][j4].z;
+                  w[4 * j4 + 3] += u4[j][j4].w;
+                }
+              }
+            }
+            if (dual) {
+#pragma unroll
+              for (int j = 0; j < 16; ++j) v[j] = silu_mul(v[j], w[j]);
+            }
+            ld_store_chunk<TOK>(p, st, f, 16 * ch, v);
+          }
+          finished = true;
+          named_barrier_sync(1, 128);
+          if (threadIdx.x == 0) st.tile_counters[c.n_t] = 0;
+        }
+      }
+      if (finished) {
+        // Publish the tile: every thread's stores, then one release increment.
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 0) red_add_release_gpu(&p.done[c.s], 1);
+      }
+      if (threadIdx.x == 0 && ntr < kTraceEvents - 1) trace_event(p, ntr, TR_UNIT_DONE, u);
+      ++acc_it;
+    }
+  }
+
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (threadIdx.x == 0) {
+    int ntr = kTraceEvents - 1;
+    trace_event(p, ntr, TR_END, -1);
+    // The last CTA to leave re-arms the counters for the next launch.
+    __threadfence();
+    const int e = atomicAdd(p.exit_count, 1);
+    if (e == static_cast<int>(gridDim.x) - 1) {
+      for (int s = 0; s < 4; ++s) atomicExch(&p.done[s], 0);
+      atomicExch(p.next_unit, 0);
+      atomicExch(p.exit_count, 0);
+      __threadfence();
+    }
+  }
+}
+
+}  // namespace svdmlp

@@ -291,6 +291,50 @@ SVD_DEV void umma_commit_pair(uint64_t* bar) {
                : "memory");
 }
 
+// ------------------------------------------------ cross-CTA dependency counters
+SVD_DEV int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Atomic add with acquire-release semantics at GPU scope; returns the old
+// value.  Release is cumulative: writes that happen before it in this CTA
+// (ordered by a barrier) are published with it.
+SVD_DEV int atom_add_acq_rel_gpu(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
+// Fire-and-forget add with release semantics at GPU scope.
+SVD_DEV void red_add_release_gpu(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's earlier generic-proxy view of global memory before its
+// later async-proxy (TMA) accesses.
+SVD_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// Waits until *ctr >= target (bounded like mbar_wait; the counter is written
+// by other CTAs of the same grid, all of which are co-resident).
+SVD_DEV bool wait_counter_geq(const int* ctr, int target, const WaitCtx& ctx, int site) {
+  if (ld_acquire_gpu(ctr) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_gpu(ctr) >= target) return true;
+    __nanosleep(32);
+    if ((i & 15u) == 0u) {
+      if (*ctx.abort_flag) return false;
+      if (global_timer_ns() - t0 > ctx.limit_ns) {
+        *ctx.abort_flag = 1;
+        atomicCAS(ctx.err, 0, site);
+        return false;
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------- misc
 SVD_DEV void named_barrier_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -18,6 +18,8 @@
 
 #include "../../include/svdmlp.h"
 #include "gemm_sm100.cuh"
+#include "gemv_sm100.cuh"
+#include "layer_decode_sm100.cuh"
 
 using bf16 = __nv_bfloat16;
 
@@ -28,6 +30,8 @@ static thread_local int g_last_cuda_error = 0;
 static std::atomic<int64_t> g_launches{0};
 static int g_split_override[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 static unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s: far above any legal wait
+static bool g_layer_decode_enabled = true;  // whole-layer decode kernel for M <= 64
+static unsigned long long* g_trace = nullptr;  // whole-layer decode timeline (diagnostics)
 
 // Optional per-stage event timing (a diagnostics pass; off by default).
 struct TimedLaunch {
@@ -209,6 +213,90 @@ static Plan plan_for(int M, int N, int K, int sms, int forced_splits) {
 // with split-K stream the weights across all SMs.
 static constexpr int kPairMinM = 129;
 
+// Split choice for a weight-streaming (decode) stage, from a model fitted to
+// B200 measurements of these kernels: a CTA streams about 60 GB/s (its
+// in-flight weight bytes over ~1.6 us of memory latency), the GPU about
+// 7 TB/s; every extra unit a CTA runs in a stage costs about one latency, and
+// split-K adds a ~4 us chain to the stage (partial stores, the arrival
+// atomic, the last split's reads and stores), plus a memory round trip per
+// four splits per 16 tokens.
+static constexpr double kHbmBytesPerUs = 7.0e6;
+static constexpr double kCtaBytesPerUs = 6.0e4;
+static Plan plan_stream(int M, int tok, int N, int K, int nb, int slots, int forced_splits) {
+  Plan p{};
+  p.m_tiles = 1;
+  p.n_tiles = static_cast<int>(cdiv(N, 128));
+  p.k_blocks = static_cast<int>(cdiv(K, 64));
+  const int tv16 = static_cast<int>(cdiv(std::min(M, tok), 16));
+  const double total = static_cast<double>(p.n_tiles) * p.k_blocks * 16384.0 * nb;
+  int best_s = 1;
+  if (forced_splits > 0) {
+    best_s = std::min(forced_splits, p.k_blocks);
+  } else {
+    double best = 1e30;
+    for (int s = 1; s <= 24; ++s) {
+      const int kbs = static_cast<int>(cdiv(p.k_blocks, s));
+      if (s > 1 && kbs < 2) break;
+      const int s_eff = static_cast<int>(cdiv(p.k_blocks, kbs));
+      if (s > 1 && s_eff != s) continue;
+      const int64_t units = static_cast<int64_t>(p.n_tiles) * s_eff;
+      const double rounds = static_cast<double>(cdiv(units, slots));
+      const double busiest = rounds * kbs * 16384.0 * nb;
+      double us = std::max(total / kHbmBytesPerUs, busiest / kCtaBytesPerUs) + 1.5 * rounds;
+      if (s_eff > 1) us += 4.0 + 1.0 * static_cast<double>(cdiv(s_eff, 4) - 1) * tv16;
+      if (us < best * 0.97) {
+        best = us;
+        best_s = s_eff;
+      }
+    }
+  }
+  p.kb_per_split = static_cast<int>(cdiv(p.k_blocks, best_s));
+  p.splits = static_cast<int>(cdiv(p.k_blocks, p.kb_per_split));
+  p.units = p.n_tiles * p.splits;
+  p.grid = std::min(p.units, slots);
+  return p;
+}
+
+// Decode plans of the per-stage streaming kernels: 128-row weight panels
+// split along K over the CTA slots (two per SM where the footprint allows).
+template <class Cfg>
+static Plan plan_dec(int M, int N, int K, int sms, int forced_splits) {
+#ifndef SVDMLP_DEC_CTAS_PER_SM
+#define SVDMLP_DEC_CTAS_PER_SM 2
+#endif
+  const int slots = (Cfg::TWO_PER_SM ? SVDMLP_DEC_CTAS_PER_SM : 1) * sms;
+  return plan_stream(M, Cfg::TOK, N, K, Cfg::NB, slots, forced_splits);
+}
+
+// One stage of the whole-layer decode kernel (all stages share `slots` CTAs).
+static Plan plan_layer_stage(int M, int tok, int N, int K, int nb, int slots, int forced_splits) {
+  Plan p = plan_stream(M, tok, N, K, nb, slots, forced_splits);
+  p.grid = slots;
+  return p;
+}
+
+static constexpr int kLayerDecodeMaxM = 64;
+
+// Partial bytes of the whole-layer decode kernel (all four stages at once).
+static int64_t layer_decode_partials(const svdmlp_layout* L, int M, int sms) {
+  const int tok = M <= 16 ? 16 : 64;
+  const int slots = 2 * sms;
+  const int shapes[4][3] = {{2 * L->rp_gu, L->d, 1}, {L->ff, L->r_gu, 2}, {L->r_d, L->ff, 1}, {L->d, L->r_d, 1}};
+  int64_t total = 0;
+  for (int st = 0; st < 4; ++st) {
+    const Plan pl =
+        plan_layer_stage(M, tok, shapes[st][0], shapes[st][1], shapes[st][2], slots, g_split_override[st]);
+    if (pl.splits > 1) total += round_up(static_cast<int64_t>(pl.units) * 2 * 128 * tok * 4, 256);
+  }
+  return total;
+}
+
+template <class Cfg>
+static int64_t dec_partial_bytes(const Plan& p) {
+  if (p.splits <= 1) return 0;
+  return static_cast<int64_t>(p.units) * Cfg::NB * Cfg::BM * Cfg::TOK * 4;
+}
+
 // Bytes of split-K partials a plan needs (NB accumulators of BM x BN fp32).
 static int64_t partial_bytes(const Plan& p, int BN, int NB) {
   if (p.splits <= 1) return 0;
@@ -267,8 +355,28 @@ using CfgDV1     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_BF16>;
 using CfgDVres1  = GemmCfg<256, 1, false, 4, EPI_RESID,  true,  OUT_BF16>;
 using CfgDenseGU1 = GemmCfg<128, 2, true, 4, EPI_SWIGLU, false, OUT_F16>;
 using CfgGemm1   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_BF16>;
+// Decode (M <= 128): swapped-operand weight-streaming kernels (gemv_sm100.cuh),
+// one set per token tile TOK (the MMA N).  TOK <= 64 sets stay within 113 KB
+// of shared memory and 256 TMEM columns so that two CTAs share an SM.
+template <int TOK>
+struct DecSet {
+  static constexpr int PST = TOK == 16 ? 5 : TOK == 64 ? 4 : 3;  // stages, one-branch kernels
+  static constexpr int DST = TOK == 16 ? 3 : TOK == 64 ? 2 : 3;  // stages, dual kernels
+  using XU = DecCfg<TOK, 1, PST, EPI_PLAIN, false, OUT_F16>;
+  using GU = DecCfg<TOK, 2, DST, EPI_SWIGLU, true, OUT_F16>;
+  using DU = DecCfg<TOK, 1, PST, EPI_PLAIN, true, OUT_F16>;
+  using DUf32 = DecCfg<TOK, 1, PST, EPI_PLAIN, true, OUT_F32>;
+  using DV = DecCfg<TOK, 1, PST, EPI_PLAIN, true, OUT_BF16>;
+  using DVres = DecCfg<TOK, 1, PST, EPI_RESID, true, OUT_BF16>;
+};
+using Dec16 = DecSet<16>;
+using Dec64 = DecSet<64>;
+using Dec128 = DecSet<128>;
 
-enum Stage : int { ST_XU = 0, ST_GATEUP = 1, ST_DOWN_U = 2, ST_DOWN_V = 3, ST_DENSE_GU = 4, ST_DENSE_D = 5, ST_GEMM = 6 };
+enum Stage : int {
+  ST_XU = 0, ST_GATEUP = 1, ST_DOWN_U = 2, ST_DOWN_V = 3, ST_DENSE_GU = 4, ST_DENSE_D = 5, ST_GEMM = 6,
+  ST_LAYER_DECODE = 7  // timing id of the whole-layer decode kernel
+};
 
 // Workspace carving.  The control block holds the error word (int 0) and the
 // split-K counters; the rest holds the intermediates.
@@ -288,10 +396,11 @@ struct Workspace {
 };
 
 static constexpr int64_t kCtlBytes = 256;
-static int64_t counters_bytes(const svdmlp_layout* L, int max_m) {
-  const int64_t widest = std::max<int64_t>({2LL * L->rp_gu, L->ff, L->rp_d, L->d, 1});
-  return round_up(cdiv(max_m, 128) * cdiv(widest, 32) * 4, 256);
-}
+// Split-K arrival counters: a fixed 1 MiB region (262144 tiles) right after
+// the control block, so that every entry point and layout carves it at the
+// same place and svdmlp_workspace_init zeroes exactly it.
+static constexpr int64_t kCounterBytes = 1 << 20;
+static int64_t counters_bytes(const svdmlp_layout*, int) { return kCounterBytes; }
 
 template <class Cfg>
 static int64_t stage_partials(int M, int N, int K, int sms, int stage) {
@@ -299,8 +408,26 @@ static int64_t stage_partials(int M, int N, int K, int sms, int stage) {
   return Cfg::CTAS == 1 ? partial_bytes(p, Cfg::BN, Cfg::NB) : 0;
 }
 
+template <class Set>
+static int64_t dec_set_partials(const svdmlp_layout* L, int M, int sms) {
+  int64_t b = 0;
+  if (L->r_gu > 0) {
+    b = std::max(b, dec_partial_bytes<typename Set::XU>(
+                        plan_dec<typename Set::XU>(M, 2 * L->rp_gu, L->d, sms, g_split_override[ST_XU])));
+    b = std::max(b, dec_partial_bytes<typename Set::GU>(
+                        plan_dec<typename Set::GU>(M, L->ff, L->r_gu, sms, g_split_override[ST_GATEUP])));
+  }
+  if (L->r_d > 0) {
+    b = std::max(b, dec_partial_bytes<typename Set::DU>(
+                        plan_dec<typename Set::DU>(M, L->r_d, L->ff, sms, g_split_override[ST_DOWN_U])));
+    b = std::max(b, dec_partial_bytes<typename Set::DV>(
+                        plan_dec<typename Set::DV>(M, L->d, L->r_d, sms, g_split_override[ST_DOWN_V])));
+  }
+  return b;
+}
+
 // Largest split-K partial buffer any M <= max_m can ask for (split-K runs
-// only in the one-CTA kernels, i.e. for M <= 128).
+// only in the one-CTA and decode kernels, i.e. for M <= 128).
 static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
   const int M = std::min(max_m, kPairMinM - 1);
   int64_t best = 0;
@@ -316,6 +443,20 @@ static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
   } else {
     best = std::max(best, stage_partials<CfgDenseGU1>(M, L->ff, L->d, sms, ST_DENSE_GU));
     best = std::max(best, stage_partials<CfgDV1>(M, L->d, L->ff, sms, ST_DENSE_D));
+  }
+  if (L->kind == SVDMLP_KIND_SVD && L->r_gu > 0 && L->r_d > 0) {
+    for (int m : {1, 16, 17, 64}) {
+      if (m > max_m) break;
+      best = std::max(best, layer_decode_partials(L, m, sms));
+    }
+  }
+  if (L->kind == SVDMLP_KIND_SVD) {
+    for (int m : {1, 16, 17, 64, 65, 128}) {
+      if (m > max_m) break;
+      if (m <= 16) best = std::max(best, dec_set_partials<Dec16>(L, m, sms));
+      else if (m <= 64) best = std::max(best, dec_set_partials<Dec64>(L, m, sms));
+      else best = std::max(best, dec_set_partials<Dec128>(L, m, sms));
+    }
   }
   return round_up(best, 256);
 }
@@ -423,6 +564,71 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   }
   if (tl) SVD_CUDA(cudaEventRecord(tl->start, stream));
   SVD_CUDA(cudaLaunchKernelEx(&cfg, gemm_sm100_kernel<Cfg>, a, a2, b, b2, out, p));
+  if (tl) SVD_CUDA(cudaEventRecord(tl->stop, stream));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return SVDMLP_OK;
+}
+
+template <class Cfg>
+static int launch_gemv(const CUtensorMap& x, const CUtensorMap& x2, const CUtensorMap& wm, const CUtensorMap& wm2,
+                       void* out, int64_t ld_out, int M, int N, int K, int stage, const Workspace& w,
+                       const bf16* residual, int64_t ld_res, cudaStream_t stream) {
+  DeviceInfo* dev = nullptr;
+  SVD_CHECK(device_info(&dev));
+  static std::mutex mu;
+  {
+    int cur = 0;
+    SVD_CUDA(cudaGetDevice(&cur));
+    static uint64_t done_mask = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!(done_mask & (1ull << cur))) {
+      SVD_CUDA(cudaFuncSetAttribute(gemv_sm100_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg::SMEM_BYTES));
+      SVD_CUDA(cudaFuncSetAttribute(gemv_sm100_kernel<Cfg>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+      done_mask |= 1ull << cur;
+    }
+  }
+  Plan pl = plan_dec<Cfg>(M, N, K, dev->sms, g_split_override[stage]);
+  if (dec_partial_bytes<Cfg>(pl) > w.partial_cap) {
+    if (!w.unsplit_if_short) return SVDMLP_ERR_WORKSPACE;
+    pl = plan_dec<Cfg>(M, N, K, dev->sms, 1);
+  }
+  GemmParams p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.m_tiles = 1;
+  p.n_tiles = pl.n_tiles;
+  p.k_blocks = pl.k_blocks;
+  p.splits = pl.splits;
+  p.kb_per_split = pl.kb_per_split;
+  p.num_units = pl.units;
+  p.partials = w.partials;
+  p.counters = w.counters;
+  p.err = w.err;
+  p.timeout_ns = g_wait_limit_ns;
+  p.residual = residual;
+  p.ld_residual = ld_res;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TimedLaunch* tl = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_timing_mu);
+    if (g_timing && g_timed_used < g_timed.size()) {
+      tl = &g_timed[g_timed_used++];
+      tl->stage = stage;
+    }
+  }
+  if (tl) SVD_CUDA(cudaEventRecord(tl->start, stream));
+  SVD_CUDA(cudaLaunchKernelEx(&cfg, gemv_sm100_kernel<Cfg>, x, x2, wm, wm2, out, static_cast<long long>(ld_out), p));
   if (tl) SVD_CUDA(cudaEventRecord(tl->stop, stream));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return SVDMLP_OK;
@@ -604,6 +810,39 @@ static int gemm_stage(const Operand& a, const Operand& a2, const Operand& b, con
   return gemm_cfg<COne>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
 }
 
+template <class Cfg>
+static int gemv_cfg(const Operand& x, const Operand& x2, const Operand& wt, const Operand& wt2, const Output& o, int M,
+                    int N, int K, int stage, const Workspace& w, const void* residual, int64_t ld_res,
+                    cudaStream_t s) {
+  CUtensorMap mx, mx2, mw, mw2;
+  SVD_CHECK(operand_map(&mx, x.ptr, x.f16, x.k, x.rows, x.ld, Cfg::TOK));
+  SVD_CHECK(operand_map(&mx2, x2.ptr, x2.f16, x2.k, x2.rows, x2.ld, Cfg::TOK));
+  SVD_CHECK(operand_map(&mw, wt.ptr, wt.f16, wt.k, wt.rows, wt.ld, Cfg::BM));
+  SVD_CHECK(operand_map(&mw2, wt2.ptr, wt2.f16, wt2.k, wt2.rows, wt2.ld, Cfg::BM));
+  const int64_t elt = Cfg::OUT == OUT_F32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(o.ptr) % elt) != 0) return SVDMLP_ERR_ALIGNMENT;
+  return launch_gemv<Cfg>(mx, mx2, mw, mw2, o.ptr, o.ld, M, N, K, stage, w, static_cast<const bf16*>(residual), ld_res,
+                          s);
+}
+
+// Like gemm_stage, with the swapped-operand streaming kernels for M <= 128:
+// `Pick` maps a DecSet to the stage's config.
+template <class CPair, template <class> class Pick>
+static int gemm_stage_dec(const Operand& a, const Operand& a2, const Operand& b, const Operand& b2, const Output& o,
+                          int M, int N, int K, int stage, const Workspace& w, cudaStream_t s,
+                          const void* residual = nullptr, int64_t ld_res = 0) {
+  if (M >= kPairMinM) return gemm_cfg<CPair>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
+  if (M <= 16) return gemv_cfg<Pick<Dec16>>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
+  if (M <= 64) return gemv_cfg<Pick<Dec64>>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
+  return gemv_cfg<Pick<Dec128>>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
+}
+template <class S> using PickXU = typename S::XU;
+template <class S> using PickGU = typename S::GU;
+template <class S> using PickDU = typename S::DU;
+template <class S> using PickDUf32 = typename S::DUf32;
+template <class S> using PickDV = typename S::DV;
+template <class S> using PickDVres = typename S::DVres;
+
 // Stage 1 + 2: h = silu(X.u_g.v_g) * (X.u_u.v_u); `h_bf16` selects the
 // caller-facing bf16 output instead of the internal fp16 H.
 static int run_gate_up(const svdmlp_layout* L, const uint8_t* packed, const void* x, int64_t ldx, int M, void* h,
@@ -611,15 +850,15 @@ static int run_gate_up(const svdmlp_layout* L, const uint8_t* packed, const void
   const int64_t n1 = 2LL * L->rp_gu;
   const Operand xa{x, false, L->d, M, ldx};
   const Operand w1{packed + L->off_w1, false, L->d, n1, L->ld_d};
-  SVD_CHECK(gemm_stage<CfgXU, CfgXU1>(xa, xa, w1, w1, Output{w.xu, n1, M, n1}, M, static_cast<int>(n1), L->d, ST_XU,
-                                      w, s));
+  SVD_CHECK(gemm_stage_dec<CfgXU, PickXU>(xa, xa, w1, w1, Output{w.xu, n1, M, n1}, M, static_cast<int>(n1), L->d,
+                                          ST_XU, w, s));
   const Operand ag{w.xu, true, L->r_gu, M, n1};
   const Operand au{w.xu + L->rp_gu, true, L->r_gu, M, n1};
   const Operand bg{packed + L->off_vg, true, L->r_gu, L->ff, L->rp_gu};
   const Operand bu{packed + L->off_vu, true, L->r_gu, L->ff, L->rp_gu};
   const Output ho{h, L->ff, M, ldh};
   if (h_bf16) return gemm_stage<CfgGUbf, CfgGUbf1>(ag, au, bg, bu, ho, M, L->ff, L->r_gu, ST_GATEUP, w, s);
-  return gemm_stage<CfgGU, CfgGU1>(ag, au, bg, bu, ho, M, L->ff, L->r_gu, ST_GATEUP, w, s);
+  return gemm_stage_dec<CfgGU, PickGU>(ag, au, bg, bu, ho, M, L->ff, L->r_gu, ST_GATEUP, w, s);
 }
 
 // Stage 3: H . u_down -> T (fp16, workspace) or an fp32 partial.  `h_f16`
@@ -630,11 +869,11 @@ static int run_down_u(const svdmlp_layout* L, const uint8_t* packed, const void*
   const Operand ud{packed + L->off_ud, h_f16, L->ff, L->r_d, L->ld_ff};
   if (partial) {
     if (!h_f16) return SVDMLP_ERR_DTYPE;
-    return gemm_stage<CfgDUf32, CfgDUf321>(ha, ha, ud, ud, Output{partial, L->r_d, M, ldp}, M, L->r_d, L->ff,
-                                           ST_DOWN_U, w, s);
+    return gemm_stage_dec<CfgDUf32, PickDUf32>(ha, ha, ud, ud, Output{partial, L->r_d, M, ldp}, M, L->r_d, L->ff,
+                                               ST_DOWN_U, w, s);
   }
   const Output to{w.t, L->r_d, M, L->rp_d};
-  if (h_f16) return gemm_stage<CfgDU, CfgDU1>(ha, ha, ud, ud, to, M, L->r_d, L->ff, ST_DOWN_U, w, s);
+  if (h_f16) return gemm_stage_dec<CfgDU, PickDU>(ha, ha, ud, ud, to, M, L->r_d, L->ff, ST_DOWN_U, w, s);
   return gemm_stage<CfgDUbf, CfgDUbf1>(ha, ha, ud, ud, to, M, L->r_d, L->ff, ST_DOWN_U, w, s);
 }
 
@@ -645,8 +884,9 @@ static int run_down_v(const svdmlp_layout* L, const uint8_t* packed, int M, void
   const Operand vd{packed + L->off_vd, true, L->r_d, L->d, L->rp_d};
   const Output yo{y, L->d, M, ldy};
   if (residual)
-    return gemm_stage<CfgDVres, CfgDVres1>(ta, ta, vd, vd, yo, M, L->d, L->r_d, ST_DOWN_V, w, s, residual, ld_res);
-  return gemm_stage<CfgDV, CfgDV1>(ta, ta, vd, vd, yo, M, L->d, L->r_d, ST_DOWN_V, w, s);
+    return gemm_stage_dec<CfgDVres, PickDVres>(ta, ta, vd, vd, yo, M, L->d, L->r_d, ST_DOWN_V, w, s, residual,
+                                               ld_res);
+  return gemm_stage_dec<CfgDV, PickDV>(ta, ta, vd, vd, yo, M, L->d, L->r_d, ST_DOWN_V, w, s);
 }
 
 // Dense SwiGLU: H = silu(X.w_g) * (X.w_u) (fp16), y = H.w_d (+ residual).
@@ -663,6 +903,139 @@ static int run_dense(const svdmlp_layout* L, const uint8_t* packed, const void* 
   if (residual)
     return gemm_stage<CfgDVres, CfgDVres1>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s, residual, ld_res);
   return gemm_stage<CfgDV, CfgDV1>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s);
+}
+
+// The whole layer for M <= 64 in one cooperative launch (layer_decode_sm100.cuh).
+template <int TOK, int STAGES>
+static int launch_layer_decode(LayerDecParams& prm, cudaStream_t s, int sms) {
+  using Cfg = LayerDecCfg<TOK, STAGES>;
+  static std::mutex mu;
+  {
+    int cur = 0;
+    SVD_CUDA(cudaGetDevice(&cur));
+    static uint64_t done_mask = 0;
+    std::lock_guard<std::mutex> lock(mu);
+    if (!(done_mask & (1ull << cur))) {
+      SVD_CUDA(cudaFuncSetAttribute(layer_decode_kernel<Cfg>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    Cfg::SMEM_BYTES));
+      // all of the unified L1/shared storage as shared memory: two CTAs per SM
+      SVD_CUDA(cudaFuncSetAttribute(layer_decode_kernel<Cfg>, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+      done_mask |= 1ull << cur;
+    }
+  }
+  // A cooperative grid must fit on the device at once.
+  int per_sm = 0;
+  SVD_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, layer_decode_kernel<Cfg>, 192, Cfg::SMEM_BYTES));
+  if (per_sm < 1) return SVDMLP_ERR_BUDGET;
+  const int grid = std::min(prm.total_units, std::min(per_sm, 2) * sms);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: they wait on one another
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  TimedLaunch* tl = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_timing_mu);
+    if (g_timing && g_timed_used < g_timed.size()) {
+      tl = &g_timed[g_timed_used++];
+      tl->stage = ST_LAYER_DECODE;
+    }
+  }
+  if (tl) SVD_CUDA(cudaEventRecord(tl->start, s));
+  SVD_CUDA(cudaLaunchKernelEx(&cfg, layer_decode_kernel<Cfg>, prm));
+  if (tl) SVD_CUDA(cudaEventRecord(tl->stop, s));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return SVDMLP_OK;
+}
+
+static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void* x, int64_t ldx, int M, void* y,
+                            int64_t ldy, const void* residual, int64_t ld_res, const Workspace& w, cudaStream_t s) {
+  DeviceInfo* dev = nullptr;
+  SVD_CHECK(device_info(&dev));
+  const int tok = M <= 16 ? 16 : 64;
+  const int slots = 2 * dev->sms;  // the planning grid; the launch checks that it fits
+  LayerDecParams prm;
+  std::memset(&prm, 0, sizeof(prm));
+#ifndef SVDMLP_LAYER_DECODE_STAGES
+#define SVDMLP_LAYER_DECODE_STAGES 4
+#endif
+  prm.num_stages = SVDMLP_LAYER_DECODE_STAGES;  // fewer only in stage-timing builds
+  prm.M = M;
+  prm.err = w.err;
+  prm.timeout_ns = g_wait_limit_ns;
+  prm.residual = static_cast<const bf16*>(residual);
+  prm.ld_residual = ld_res;
+  prm.done = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(w.err) + 64);
+  prm.exit_count = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(w.err) + 96);
+  prm.next_unit = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(w.err) + 128);
+  prm.trace = g_trace;
+  const int64_t n1 = 2LL * L->rp_gu;
+  // stage operands: token tiles (box TOK rows) and weight panels (box 128 rows)
+  struct Spec {
+    const void *x, *x2;
+    bool xf16;
+    int64_t xk, xld;
+    const void *w, *w2;
+    int64_t wrows, wld;
+    void* out;
+    int64_t ld_out;
+    int nb, epi, out_kind;
+  } spec[4] = {
+      {x, x, false, L->d, ldx, P + L->off_w1, P + L->off_w1, n1, L->ld_d, w.xu, n1, 1, EPI_PLAIN, OUT_F16},
+      {w.xu, w.xu + L->rp_gu, true, L->r_gu, n1, P + L->off_vg, P + L->off_vu, L->ff, L->rp_gu, w.h, L->ld_ff, 2,
+       EPI_SWIGLU, OUT_F16},
+      {w.h, w.h, true, L->ff, L->ld_ff, P + L->off_ud, P + L->off_ud, L->r_d, L->ld_ff, w.t, L->rp_d, 1, EPI_PLAIN,
+       OUT_F16},
+      {w.t, w.t, true, L->r_d, L->rp_d, P + L->off_vd, P + L->off_vd, L->d, L->rp_d, y, ldy, 1,
+       residual ? EPI_RESID : EPI_PLAIN, OUT_BF16},
+  };
+  float* part = w.partials;
+  int64_t part_left = w.partial_cap;
+  int base = 0;
+  for (int st = 0; st < 4; ++st) {
+    DecStage& d = prm.st[st];
+    const Spec& sp = spec[st];
+    SVD_CHECK(operand_map(&d.x, sp.x, sp.xf16, sp.xk, M, sp.xld, tok));
+    SVD_CHECK(operand_map(&d.x2, sp.x2, sp.xf16, sp.xk, M, sp.xld, tok));
+    SVD_CHECK(operand_map(&d.w, sp.w, sp.xf16, sp.xk, sp.wrows, sp.wld, 128));
+    SVD_CHECK(operand_map(&d.w2, sp.w2, sp.xf16, sp.xk, sp.wrows, sp.wld, 128));
+    const int N = static_cast<int>(st == 0 ? n1 : sp.wrows);
+    const int K = static_cast<int>(sp.xk);
+    Plan pl = plan_layer_stage(M, tok, N, K, sp.nb, slots, g_split_override[st]);
+    int64_t pb = pl.splits > 1 ? round_up(static_cast<int64_t>(pl.units) * 2 * 128 * tok * 4, 256) : 0;
+    if (pb > part_left) {
+      if (!w.unsplit_if_short) return SVDMLP_ERR_WORKSPACE;
+      pl = plan_layer_stage(M, tok, N, K, sp.nb, slots, 1);
+      pb = 0;
+    }
+    d.out = sp.out;
+    d.ld_out = sp.ld_out;
+    d.partials = part;
+    d.tile_counters = w.counters + st * 65536;
+    d.N = N;
+    d.K = K;
+    d.n_tiles = pl.n_tiles;
+    d.k_blocks = pl.k_blocks;
+    d.splits = pl.splits;
+    d.kb_per_split = pl.kb_per_split;
+    d.units = pl.units;
+    d.unit_base = base;
+    d.nb = sp.nb;
+    d.in_f16 = sp.xf16 ? 1 : 0;
+    d.epi = sp.epi;
+    d.out_kind = sp.out_kind;
+    base += pl.units;
+    part += pb / 4;
+    part_left -= pb;
+  }
+  prm.total_units = prm.st[prm.num_stages - 1].unit_base + prm.st[prm.num_stages - 1].units;
+  if (tok == 16) return launch_layer_decode<16, 3>(prm, s, dev->sms);
+  return launch_layer_decode<64, 2>(prm, s, dev->sms);
 }
 
 // Output target: the caller's buffer when TMA-legal, else workspace staging.
@@ -812,7 +1185,7 @@ int64_t svdmlp_workspace_bytes(const svdmlp_layout* L, int max_m) {
 int svdmlp_workspace_init(void* ws, int64_t ws_bytes, void* stream) {
   if (!ws || ws_bytes < kCtlBytes) return SVDMLP_ERR_INVALID_VALUE;
   // The control block and the split-K counters sit at the front.
-  const int64_t n = std::min<int64_t>(ws_bytes, kCtlBytes + (4 << 20));
+  const int64_t n = std::min<int64_t>(ws_bytes, kCtlBytes + kCounterBytes);
   SVD_CUDA(cudaMemsetAsync(ws, 0, static_cast<size_t>(n), static_cast<cudaStream_t>(stream)));
   return SVDMLP_OK;
 }
@@ -890,6 +1263,11 @@ int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, in
   const void* xa;
   int64_t ldxa;
   SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
+  if (M <= kLayerDecodeMaxM && g_layer_decode_enabled) {
+    // Decode sizes: the whole layer in one launch; its stores need no TMA
+    // alignment, and the residual is read in place (it must not alias y).
+    return run_layer_decode(L, P, xa, ldxa, M, y, ldy, residual, ld_res, w, s);
+  }
   SVD_CHECK(run_gate_up(L, P, xa, ldxa, M, w.h, L->ld_ff, false, w, s));
   SVD_CHECK(run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, 0, w, s));
   const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
@@ -983,7 +1361,7 @@ int64_t svdmlp_gemm_workspace_bytes(int M, int N, int K) {
   const Plan pl = M >= kPairMinM ? plan_for<CfgGemm>(M, N, K, sms, 0)
                                  : plan_for<CfgGemm1>(M, N, K, sms, g_split_override[ST_GEMM]);
   const int64_t part = M >= kPairMinM ? 0 : partial_bytes(pl, CfgGemm1::BN, 1);
-  return kCtlBytes + round_up(cdiv(M, 128) * cdiv(N, 128) * 4, 256) + round_up(part, 256);
+  return kCtlBytes + kCounterBytes + round_up(part, 256);
 }
 
 int svdmlp_gemm(const void* a, int64_t lda, const void* bt, int64_t ldb, void* c, int64_t ldc, int M, int N, int K,
@@ -993,8 +1371,7 @@ int svdmlp_gemm(const void* a, int64_t lda, const void* bt, int64_t ldb, void* c
   if (!ws || (reinterpret_cast<uintptr_t>(ws) & 255u) != 0) return SVDMLP_ERR_INVALID_VALUE;
   const int64_t need = svdmlp_gemm_workspace_bytes(M, N, K);
   if (ws_bytes < need) return SVDMLP_ERR_WORKSPACE;
-  const int64_t cnt = round_up(static_cast<int64_t>(cdiv(M, 128)) * cdiv(N, 128) * 4, 256);
-  if (ws_bytes < kCtlBytes + cnt) return SVDMLP_ERR_WORKSPACE;
+  const int64_t cnt = kCounterBytes;
   Workspace w{};
   uint8_t* p = static_cast<uint8_t*>(ws);
   w.err = reinterpret_cast<int*>(p);
@@ -1058,6 +1435,18 @@ int svdmlp_stage_times(double* ms_out, int64_t* counts_out, int n) {
     }
   }
   g_timed_used = 0;
+  return SVDMLP_OK;
+}
+
+int svdmlp_set_trace_buffer(void* buffer, int64_t bytes) {
+  // 296 CTAs x 64 events x 16 bytes is the largest timeline one launch writes
+  if (buffer && bytes < 2 * 148 * 64 * 16) return SVDMLP_ERR_INVALID_VALUE;
+  g_trace = static_cast<unsigned long long*>(buffer);
+  return SVDMLP_OK;
+}
+
+int svdmlp_set_layer_decode(int enable) {
+  g_layer_decode_enabled = enable != 0;
   return SVDMLP_OK;
 }
 
@@ -1141,8 +1530,10 @@ int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
   if (!out6 || M <= 0 || N <= 0 || K <= 0 || stage < 0 || stage >= 8) return SVDMLP_ERR_INVALID_VALUE;
   const bool dual = stage == ST_GATEUP || stage == ST_DENSE_GU;
   const int nb = dual ? 2 : 1;
+  const int tok = M <= 16 ? 16 : M <= 64 ? 64 : 128;
   const Plan p = M >= kPairMinM ? plan_gemm_pair(M, N, K, dual ? CfgGU::BN : 256, planning_sms())
-                                : plan_gemm(M, N, K, dual ? CfgGU1::BN : 256, nb, planning_sms(), g_split_override[stage]);
+                                : plan_stream(M, tok, N, K, nb, (tok <= 64 ? 2 : 1) * planning_sms(),
+                                              g_split_override[stage]);
   out6[0] = p.m_tiles;
   out6[1] = p.n_tiles;
   out6[2] = p.k_blocks;

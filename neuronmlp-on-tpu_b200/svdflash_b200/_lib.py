@@ -81,6 +81,8 @@ SIGNATURES = {
     "svdmlp_rmsnorm": (c_int, [V, I64, V, V, I64, c_int, c_int, c_float, V]),
     "svdmlp_debug_wait_timeout": (c_int, [V, I64, I64, V]),
     "svdmlp_set_split_override": (c_int, [c_int, c_int]),
+    "svdmlp_set_layer_decode": (c_int, [c_int]),
+    "svdmlp_set_trace_buffer": (c_int, [V, I64]),
     "svdmlp_plan_info": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_int)]),
     "svdmlp_stage_timing": (c_int, [c_int]),
     "svdmlp_stage_times": (c_int, [POINTER(ctypes.c_double), POINTER(c_int64), c_int]),

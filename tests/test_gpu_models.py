@@ -115,3 +115,35 @@ def test_decode_sizes_split_k(cuda_device):
         y = ops.svd_mlp_packed(layer, to_dev(x, cuda_device))
         assert_close(to_np(y), orc.svd_mlp(x, *f), what=f"decode m={m}")
     ops.check_device_status(cuda_device)
+
+
+@pytest.mark.parametrize("m", [1, 5, 16, 17, 64])
+def test_whole_layer_decode_kernel(cuda_device, m):
+    """M <= 64 runs the one-launch whole-layer decode kernel; it matches the
+    oracle and the four per-stage kernels, with and without a residual."""
+    from svdflash_b200 import _lib
+    from svdflash_b200.kernels import ops
+    lib = _lib.load()
+    h, r, i = 4096, 2867, 14336
+    x, f = orc.make_inputs(90 + m, m, h, i, r)
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f])
+    xd = to_dev(x, cuda_device)
+    res = orc.bf16_round(np.random.default_rng(m).standard_normal((m, h), dtype=np.float32))
+    rd = to_dev(res, cuda_device)
+    try:
+        lib.svdmlp_set_layer_decode(1)
+        y1 = ops.svd_mlp_packed(layer, xd)
+        y1r = ops.svd_mlp_packed(layer, xd, residual=rd)
+        y1b = ops.svd_mlp_packed(layer, xd)
+        lib.svdmlp_set_layer_decode(0)
+        y0 = ops.svd_mlp_packed(layer, xd)
+    finally:
+        lib.svdmlp_set_layer_decode(1)
+    torch.cuda.synchronize()
+    ops.check_device_status(cuda_device)
+    ref = orc.svd_mlp(x, *f)
+    assert_close(to_np(y1), ref, what=f"layer decode m={m}")
+    assert_close(to_np(y1r), res + ref, what=f"layer decode + residual m={m}")
+    assert torch.equal(y1, y1b), "repeated launches differ"
+    from helpers import assert_close_bf16_output
+    assert_close_bf16_output(to_np(y1), to_np(y0), what=f"layer decode vs per-stage m={m}")
