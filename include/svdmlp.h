@@ -62,15 +62,19 @@ int svdmlp_last_cuda_error(void);
  *
  * SVD kind (ranks r_gu for gate and up, r_d for down; a rank of 0 leaves that
  * half out, so a down-only layout serves xuv_matmul and a gate/up-only layout
- * serves fused_gate_up):
- *   w1 [2*rp_gu, ld_d]  bf16  rows [0,r_gu) = u_gate^T, rows [rp_gu, rp_gu+r_gu) = u_up^T
- *   vg [ff, rp_gu]      fp16  v_gate^T
- *   vu [ff, rp_gu]      fp16  v_up^T
- *   ud [rp_d, ld_ff]    fp16  u_down^T  (bf16 when r_gu == 0, see ud_f16)
- *   vd [d, rp_d]        fp16  v_down^T
+ * serves fused_gate_up), each a K-major matrix [N rows, K]:
+ *   w1 [2*rp_gu, d]    bf16  rows [0,r_gu) = u_gate^T, rows [rp_gu, rp_gu+r_gu) = u_up^T
+ *   vg [ff, r_gu]      fp16  v_gate^T
+ *   vu [ff, r_gu]      fp16  v_up^T
+ *   ud [r_d, ff]       fp16  u_down^T  (bf16 when r_gu == 0, see ud_f16)
+ *   vd [d, r_d]        fp16  v_down^T
  * Dense kind:
- *   vg [ff, ld_d] bf16 w_gate^T,  vu [ff, ld_d] bf16 w_up^T,  ud [d, ld_ff] fp16 w_down^T
- * Pads are zero.  rp_* and ld_* are multiples of 8 elements (16 bytes).
+ *   vg [ff, d] bf16 w_gate^T,  vu [ff, d] bf16 w_up^T,  ud [d, ff] fp16 w_down^T
+ * Every matrix is stored tile-major: tiles of 16 rows x 64 columns, 2 KB
+ * each, ordered [row group][column block], row-major inside a tile; N is
+ * padded to 16 and K to 64 with zeros.  rp_gu is a multiple of 16; rp_d and
+ * the ld_* (leading dimensions of the activations X, H and T in the
+ * workspace) are multiples of 8 elements (16 bytes).
  *
  * Precision: inputs and outputs are bf16.  The intermediates X.u (rank r),
  * H (ff) and H.u_down (rank r) are kept in fp16 (saturating at +-65504), so

@@ -76,8 +76,11 @@ struct GemmParams {
 };
 
 template <int BN_, int NB_, bool SHARED_A_, int STAGES_, int EPI_, bool IN_F16_, int OUT_, int CTAS_ = 1,
-          int EPI_WARPS_ = 4>
+          int EPI_WARPS_ = 4, bool B_TILED_ = true>
 struct GemmCfg {
+  // B (the weight operand) in the packed tile-major layout (4-D tensor map,
+  // 2 KB contiguous tiles) or row-major (2-D tensor map).
+  static constexpr bool B_TILED = B_TILED_;
   static constexpr int BM = 128, BK = 64;  // rows per CTA, K per stage
   static constexpr int BN = BN_, NB = NB_, STAGES = STAGES_, EPI = EPI_, OUT = OUT_, CTAS = CTAS_;
   // Epilogue warps: 4 (one per TMEM lane quarter) or 8 (two per quarter,
@@ -94,6 +97,7 @@ struct GemmCfg {
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "BN must be a multiple of 32 in [32, 256]");
   static_assert(CTAS == 1 || CTAS == 2, "one CTA or a CTA pair per tile");
   static_assert(B_ROWS % 8 == 0, "B half-tile must hold whole 8-row core-matrix groups");
+  static_assert(!B_TILED || B_ROWS % 16 == 0, "tiled B loads whole 16-row groups");
   static_assert(NB == 1 || NB == 2, "one or two accumulators per tile");
   static_assert(NB == 1 || EPI == EPI_SWIGLU, "dual GEMMs use the SwiGLU epilogue");
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "four or eight epilogue warps");
@@ -241,16 +245,27 @@ SVD_DEV void issue_stage_loads(const CUtensorMap* tm_a, const CUtensorMap* tm_a2
   uint8_t* a2 = smem + Cfg::OFF_A2 + s * Cfg::A_BYTES;
   uint8_t* b = smem + Cfg::OFF_B + s * Cfg::B_BYTES;
   uint8_t* b2 = smem + Cfg::OFF_B2 + s * Cfg::B_BYTES;
+  const int kb = kx / Cfg::BK, grp = b_row / 16;
   if constexpr (Cfg::CTAS == 1) {
     tma_load_2d(tm_a, full_local, a, kx, a_row);
     if constexpr (Cfg::NA == 2) tma_load_2d(tm_a2, full_local, a2, kx, a_row);
-    tma_load_2d(tm_b, full_local, b, kx, b_row);
-    if constexpr (Cfg::NB == 2) tma_load_2d(tm_b2, full_local, b2, kx, b_row);
+    if constexpr (Cfg::B_TILED) {
+      tma_load_4d(tm_b, full_local, b, kb, grp);
+      if constexpr (Cfg::NB == 2) tma_load_4d(tm_b2, full_local, b2, kb, grp);
+    } else {
+      tma_load_2d(tm_b, full_local, b, kx, b_row);
+      if constexpr (Cfg::NB == 2) tma_load_2d(tm_b2, full_local, b2, kx, b_row);
+    }
   } else {
     tma_load_2d_pair(tm_a, full_leader, a, kx, a_row);
     if constexpr (Cfg::NA == 2) tma_load_2d_pair(tm_a2, full_leader, a2, kx, a_row);
-    tma_load_2d_pair(tm_b, full_leader, b, kx, b_row);
-    if constexpr (Cfg::NB == 2) tma_load_2d_pair(tm_b2, full_leader, b2, kx, b_row);
+    if constexpr (Cfg::B_TILED) {
+      tma_load_4d_pair(tm_b, full_leader, b, kb, grp);
+      if constexpr (Cfg::NB == 2) tma_load_4d_pair(tm_b2, full_leader, b2, kb, grp);
+    } else {
+      tma_load_2d_pair(tm_b, full_leader, b, kx, b_row);
+      if constexpr (Cfg::NB == 2) tma_load_2d_pair(tm_b2, full_leader, b2, kx, b_row);
+    }
   }
 }
 

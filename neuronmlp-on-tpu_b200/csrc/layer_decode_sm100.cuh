@@ -38,7 +38,7 @@
 namespace svdmlp {
 
 struct alignas(64) DecStage {
-  CUtensorMap x, x2, w, w2;  // token operand(s) [M, K] and weight(s) [N, K], K-major
+  CUtensorMap x, x2, w, w2;  // token operand(s) [M, K] (2-D) and packed tiled weight(s) [N, K] (4-D)
   void* out;
   long long ld_out;
   float* partials;   // [tiles][splits][nb][128][TOK] fp32
@@ -211,13 +211,14 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         const DecStage& st = p.st[c.s];
         uint8_t* w0 = smem + Cfg::OFF_W + (sl * 2) * Cfg::W_BYTES;
         uint8_t* w1 = w0 + Cfg::W_BYTES;
-        const int row = c.n_t * Cfg::BM;
+        // weights: packed tile-major layout, 4-D loads at (k-block, 16-row group)
+        const int grp = c.n_t * Cfg::BM / 16;
         if (st.nb == 2) {
-          tma_load_2d(&st.w, &full[sl], w0, (c.kb0 + i) * Cfg::BK, row);
-          tma_load_2d(&st.w2, &full[sl], w1, (c.kb0 + i) * Cfg::BK, row);
+          tma_load_4d(&st.w, &full[sl], w0, c.kb0 + i, grp);
+          tma_load_4d(&st.w2, &full[sl], w1, c.kb0 + i, grp);
         } else {
-          tma_load_2d(&st.w, &full[sl], w0, (c.kb0 + 2 * i) * Cfg::BK, row);
-          if (c.kb0 + 2 * i + 1 < c.kb1) tma_load_2d(&st.w, &full[sl], w1, (c.kb0 + 2 * i + 1) * Cfg::BK, row);
+          tma_load_4d(&st.w, &full[sl], w0, c.kb0 + 2 * i, grp);
+          if (c.kb0 + 2 * i + 1 < c.kb1) tma_load_4d(&st.w, &full[sl], w1, c.kb0 + 2 * i + 1, grp);
         }
       };
       auto slot_x = [&](const LdUnit& c, int i, int sl) {

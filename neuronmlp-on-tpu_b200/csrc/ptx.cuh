@@ -106,6 +106,16 @@ SVD_DEV void tma_load_2d(const CUtensorMap* map, uint64_t* bar, void* dst, int x
       : "memory");
 }
 
+// 4-D tile load: the packed weight layout [16-row group][k-block][16][64]
+// (see tiled_weight_map in svdmlp.cu); coordinates (0, 0, k-block, group).
+SVD_DEV void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* dst, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %3, %4, %5}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(0), "r"(c2), "r"(c3)
+      : "memory");
+}
+
 SVD_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
@@ -248,6 +258,14 @@ SVD_DEV void tma_load_2d_pair(const CUtensorMap* map, uint32_t bar_cluster, void
       "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_addr(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+      : "memory");
+}
+
+SVD_DEV void tma_load_4d_pair(const CUtensorMap* map, uint32_t bar_cluster, void* dst, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %3, %4, %5}], [%2];" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(0), "r"(c2), "r"(c3)
       : "memory");
 }
 

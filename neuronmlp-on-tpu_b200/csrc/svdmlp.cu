@@ -145,6 +145,32 @@ static int output_map(CUtensorMap* m, const void* base, int64_t n, int64_t rows,
                   dt == DT::F32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
 }
 
+// Packed weights are stored tile-major: [16-row group][64-column k-block]
+// tiles of 16 x 64 elements, each tile 2 KB contiguous and row-major inside.
+// A 4-D tensor map (64, 16, k-blocks, groups) reads a box of `box_rows` rows
+// (a multiple of 16) of one k-block as box_rows/16 contiguous 2 KB runs and
+// lays it out in shared memory exactly as a 2-D [box_rows x 64] box would,
+// with the 128-byte swizzle.  Rows beyond N and columns beyond K are zero in
+// the packed buffer.
+static int64_t tiled_bytes(int64_t n, int64_t k) { return round_up(n, 16) * round_up(k, 64) * 2; }
+
+static int tiled_map(CUtensorMap* map, const void* base, bool f16, int64_t n, int64_t k, int box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return cuda_fail(cudaErrorInitializationError);
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0 || box_rows % 16 != 0 || box_rows > 256)
+    return SVDMLP_ERR_ALIGNMENT;
+  const int64_t kb = cdiv(k, 64), groups = cdiv(n, 16);
+  cuuint64_t dims[4] = {64, 16, static_cast<cuuint64_t>(kb), static_cast<cuuint64_t>(groups)};
+  cuuint64_t strides[3] = {128, 2048, static_cast<cuuint64_t>(kb * 2048)};
+  cuuint32_t box[4] = {64, 16, 1, static_cast<cuuint32_t>(box_rows / 16)};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4,
+                  const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return SVDMLP_ERR_ALIGNMENT;
+  return SVDMLP_OK;
+}
+
 // ------------------------------------------------------------------ planner
 struct Plan {
   int m_tiles, n_tiles, k_blocks, splits, kb_per_split, units, grid;
@@ -343,7 +369,7 @@ using CfgDUf32  = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_F32,  2
 using CfgDV     = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_BF16, 2, kPlEw>;  // T.v_down -> y
 using CfgDVres  = GemmCfg<256,   1, false, kPlSt, EPI_RESID,  true,  OUT_BF16, 2, kPlEw>;  // + residual
 using CfgDenseGU = GemmCfg<kGuBn, 2, true, kDgSt, EPI_SWIGLU, false, OUT_F16,  2, kGuEw>;  // X.[w_g|w_u] -> H
-using CfgGemm   = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  false, OUT_BF16, 2, kPlEw>;  // plain bf16 GEMM
+using CfgGemm   = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  false, OUT_BF16, 2, kPlEw, false>;  // row-major B
 // Decode (M <= 128): one CTA per tile, split-K across the SMs.
 using CfgXU1     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_F16>;
 using CfgGU1     = GemmCfg<128, 2, false, 3, EPI_SWIGLU, true,  OUT_F16>;
@@ -354,7 +380,7 @@ using CfgDUf321  = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_F32>;
 using CfgDV1     = GemmCfg<256, 1, false, 4, EPI_PLAIN,  true,  OUT_BF16>;
 using CfgDVres1  = GemmCfg<256, 1, false, 4, EPI_RESID,  true,  OUT_BF16>;
 using CfgDenseGU1 = GemmCfg<128, 2, true, 4, EPI_SWIGLU, false, OUT_F16>;
-using CfgGemm1   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_BF16>;
+using CfgGemm1   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_BF16, 1, 4, false>;
 // Decode (M <= 128): swapped-operand weight-streaming kernels (gemv_sm100.cuh),
 // one set per token tile TOK (the MMA N).  TOK <= 64 sets stay within 113 KB
 // of shared memory and 256 TMEM columns so that two CTAs share an SM.
@@ -660,6 +686,32 @@ __global__ void transpose_pack_kernel(const bf16* __restrict__ src, long long ld
   }
 }
 
+// Packs src [rows, cols] (row-major bf16) transposed into rows [row0,
+// row0 + cols) of a tiled K-major matrix with K = rows: element (n, k) of the
+// destination is src[k][n - row0], stored at tile (n / 16, k / 64), offset
+// (n % 16) * 64 + k % 64.  `kb_count` is the number of 64-column k-blocks of
+// the destination; destination columns k >= rows are written as zero.
+template <typename TO>
+__global__ void tiled_pack_kernel(const bf16* __restrict__ src, long long ld_src, int rows, int cols,
+                                  TO* __restrict__ dst, int row0, int kb_count) {
+  __shared__ float tile[32][33];
+  const int k0 = blockIdx.x * 32;  // destination column (k) == source row
+  const int n0 = blockIdx.y * 32;  // destination row offset within [0, cols)
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    const int k = k0 + y, n = n0 + threadIdx.x;
+    tile[y][threadIdx.x] = (k < rows && n < cols) ? __bfloat162float(src[static_cast<long long>(k) * ld_src + n]) : 0.f;
+  }
+  __syncthreads();
+  for (int y = threadIdx.y; y < 32; y += blockDim.y) {
+    const int n = n0 + y, k = k0 + threadIdx.x;
+    if (n < cols && k < kb_count * 64) {
+      const int gn = row0 + n;
+      const long long off = (static_cast<long long>(gn / 16) * kb_count + k / 64) * 1024 + (gn % 16) * 64 + (k % 64);
+      dst[off] = from_float<TO>(tile[threadIdx.x][y]);
+    }
+  }
+}
+
 // 2-D element-wise conversion with leading dimensions (fp32 -> fp16, bf16 -> fp16).
 template <typename TI, typename TO>
 __global__ void convert_kernel(const TI* __restrict__ src, long long ld_src, TO* __restrict__ dst, long long ld_dst,
@@ -721,6 +773,19 @@ static int launch_convert(const TI* src, int64_t ld_src, TO* dst, int64_t ld_dst
   const int64_t total = static_cast<int64_t>(rows) * cols;
   const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cdiv(total, 256), 148 * 16)));
   convert_kernel<TI, TO><<<blocks, 256, 0, s>>>(src, ld_src, dst, ld_dst, rows, cols);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+template <typename TO>
+static int launch_tiled_pack(const void* src, int64_t ld_src, int rows, int cols, void* dst, int row0, int64_t k,
+                             cudaStream_t s) {
+  if (!src || !dst || rows <= 0 || cols <= 0 || ld_src < cols || row0 % 16 != 0) return SVDMLP_ERR_INVALID_VALUE;
+  const int kb = static_cast<int>(cdiv(k, 64));
+  dim3 grid(static_cast<unsigned>(cdiv(static_cast<int64_t>(kb) * 64, 32)), static_cast<unsigned>(cdiv(cols, 32)));
+  tiled_pack_kernel<TO><<<grid, dim3(32, 8), 0, s>>>(static_cast<const bf16*>(src), ld_src, rows, cols,
+                                                     static_cast<TO*>(dst), row0, kb);
   SVD_CUDA(cudaGetLastError());
   g_launches.fetch_add(1);
   return SVDMLP_OK;
@@ -794,8 +859,13 @@ static int gemm_cfg(const Operand& a, const Operand& a2, const Operand& b, const
   CUtensorMap ma, ma2, mb, mb2, mo;
   SVD_CHECK(operand_map(&ma, a.ptr, a.f16, a.k, a.rows, a.ld, Cfg::BM));
   SVD_CHECK(operand_map(&ma2, a2.ptr, a2.f16, a2.k, a2.rows, a2.ld, Cfg::BM));
-  SVD_CHECK(operand_map(&mb, b.ptr, b.f16, b.k, b.rows, b.ld, Cfg::B_ROWS));
-  SVD_CHECK(operand_map(&mb2, b2.ptr, b2.f16, b2.k, b2.rows, b2.ld, Cfg::B_ROWS));
+  if constexpr (Cfg::B_TILED) {
+    SVD_CHECK(tiled_map(&mb, b.ptr, b.f16, b.rows, b.k, Cfg::B_ROWS));
+    SVD_CHECK(tiled_map(&mb2, b2.ptr, b2.f16, b2.rows, b2.k, Cfg::B_ROWS));
+  } else {
+    SVD_CHECK(operand_map(&mb, b.ptr, b.f16, b.k, b.rows, b.ld, Cfg::B_ROWS));
+    SVD_CHECK(operand_map(&mb2, b2.ptr, b2.f16, b2.k, b2.rows, b2.ld, Cfg::B_ROWS));
+  }
   SVD_CHECK(output_map<Cfg>(&mo, o.ptr, o.n, o.rows, o.ld));
   return launch_gemm<Cfg>(ma, ma2, mb, mb2, mo, M, N, K, stage, w, static_cast<const bf16*>(residual), ld_res, s);
 }
@@ -817,8 +887,8 @@ static int gemv_cfg(const Operand& x, const Operand& x2, const Operand& wt, cons
   CUtensorMap mx, mx2, mw, mw2;
   SVD_CHECK(operand_map(&mx, x.ptr, x.f16, x.k, x.rows, x.ld, Cfg::TOK));
   SVD_CHECK(operand_map(&mx2, x2.ptr, x2.f16, x2.k, x2.rows, x2.ld, Cfg::TOK));
-  SVD_CHECK(operand_map(&mw, wt.ptr, wt.f16, wt.k, wt.rows, wt.ld, Cfg::BM));
-  SVD_CHECK(operand_map(&mw2, wt2.ptr, wt2.f16, wt2.k, wt2.rows, wt2.ld, Cfg::BM));
+  SVD_CHECK(tiled_map(&mw, wt.ptr, wt.f16, wt.rows, wt.k, Cfg::BM));
+  SVD_CHECK(tiled_map(&mw2, wt2.ptr, wt2.f16, wt2.rows, wt2.k, Cfg::BM));
   const int64_t elt = Cfg::OUT == OUT_F32 ? 4 : 2;
   if ((reinterpret_cast<uintptr_t>(o.ptr) % elt) != 0) return SVDMLP_ERR_ALIGNMENT;
   return launch_gemv<Cfg>(mx, mx2, mw, mw2, o.ptr, o.ld, M, N, K, stage, w, static_cast<const bf16*>(residual), ld_res,
@@ -1002,8 +1072,8 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
     const Spec& sp = spec[st];
     SVD_CHECK(operand_map(&d.x, sp.x, sp.xf16, sp.xk, M, sp.xld, tok));
     SVD_CHECK(operand_map(&d.x2, sp.x2, sp.xf16, sp.xk, M, sp.xld, tok));
-    SVD_CHECK(operand_map(&d.w, sp.w, sp.xf16, sp.xk, sp.wrows, sp.wld, 128));
-    SVD_CHECK(operand_map(&d.w2, sp.w2, sp.xf16, sp.xk, sp.wrows, sp.wld, 128));
+    SVD_CHECK(tiled_map(&d.w, sp.w, sp.xf16, sp.wrows, sp.xk, 128));
+    SVD_CHECK(tiled_map(&d.w2, sp.w2, sp.xf16, sp.wrows, sp.xk, 128));
     const int N = static_cast<int>(st == 0 ? n1 : sp.wrows);
     const int K = static_cast<int>(sp.xk);
     Plan pl = plan_layer_stage(M, tok, N, K, sp.nb, slots, g_split_override[st]);
@@ -1083,7 +1153,7 @@ int svdmlp_layout_init(svdmlp_layout* L, int d, int ff, int r_gu, int r_d) {
   L->ff = ff;
   L->r_gu = r_gu;
   L->r_d = r_d;
-  L->rp_gu = static_cast<int32_t>(round_up(r_gu, 8));
+  L->rp_gu = static_cast<int32_t>(round_up(r_gu, 16));  // the up half of w1 starts on a 16-row group
   L->rp_d = static_cast<int32_t>(round_up(r_d, 8));
   L->ld_d = static_cast<int32_t>(round_up(d, 8));
   L->ld_ff = static_cast<int32_t>(round_up(ff, 8));
@@ -1094,11 +1164,11 @@ int svdmlp_layout_init(svdmlp_layout* L, int d, int ff, int r_gu, int r_d) {
     off += round_up(bytes, 256);
     return o;
   };
-  L->off_w1 = take(2LL * L->rp_gu * L->ld_d * 2);
-  L->off_vg = take(static_cast<int64_t>(ff) * L->rp_gu * 2);
-  L->off_vu = take(static_cast<int64_t>(ff) * L->rp_gu * 2);
-  L->off_ud = take(static_cast<int64_t>(L->rp_d) * L->ld_ff * 2);
-  L->off_vd = take(static_cast<int64_t>(d) * L->rp_d * 2);
+  L->off_w1 = take(tiled_bytes(2LL * L->rp_gu, d));  // [2*rp_gu, d]
+  L->off_vg = take(tiled_bytes(ff, r_gu));            // [ff, r_gu]
+  L->off_vu = take(tiled_bytes(ff, r_gu));
+  L->off_ud = take(tiled_bytes(r_d, ff));             // [r_d, ff]
+  L->off_vd = take(tiled_bytes(d, r_d));              // [d, r_d]
   L->packed_bytes = off;
   return SVDMLP_OK;
 }
@@ -1118,9 +1188,9 @@ int svdmlp_dense_layout_init(svdmlp_layout* L, int d, int ff) {
     off += round_up(bytes, 256);
     return o;
   };
-  L->off_vg = take(static_cast<int64_t>(ff) * L->ld_d * 2);
-  L->off_vu = take(static_cast<int64_t>(ff) * L->ld_d * 2);
-  L->off_ud = take(static_cast<int64_t>(d) * L->ld_ff * 2);
+  L->off_vg = take(tiled_bytes(ff, d));  // [ff, d]
+  L->off_vu = take(tiled_bytes(ff, d));
+  L->off_ud = take(tiled_bytes(d, ff));  // [d, ff]
   L->packed_bytes = off;
   return SVDMLP_OK;
 }
@@ -1142,23 +1212,21 @@ int svdmlp_pack(const svdmlp_layout* L, const void* u_gate, int64_t ld_ug, const
   SVD_CUDA(cudaMemsetAsync(P, 0, static_cast<size_t>(L->packed_bytes), s));
   if (L->r_gu > 0) {
     if (!u_gate || !v_gate || !u_up || !v_up) return SVDMLP_ERR_INVALID_VALUE;
-    bf16* w1 = reinterpret_cast<bf16*>(P + L->off_w1);
-    // u [d, r] -> rows of w1 = u^T (bf16: it multiplies the bf16 input X)
-    SVD_CHECK(launch_transpose<bf16>(u_gate, ld_ug, L->d, L->r_gu, w1, L->ld_d, L->rp_gu, L->d, s));
-    SVD_CHECK(launch_transpose<bf16>(u_up, ld_uu, L->d, L->r_gu, w1 + static_cast<int64_t>(L->rp_gu) * L->ld_d,
-                                     L->ld_d, L->rp_gu, L->d, s));
-    // v [r, ff] -> v^T [ff, rp] (fp16: it multiplies the fp16 XU)
-    SVD_CHECK(launch_transpose<__half>(v_gate, ld_vg, L->r_gu, L->ff, P + L->off_vg, L->rp_gu, L->ff, L->rp_gu, s));
-    SVD_CHECK(launch_transpose<__half>(v_up, ld_vu, L->r_gu, L->ff, P + L->off_vu, L->rp_gu, L->ff, L->rp_gu, s));
+    // w1 [2*rp_gu, d] (bf16: it multiplies the bf16 input X): u_gate^T, then u_up^T
+    SVD_CHECK(launch_tiled_pack<bf16>(u_gate, ld_ug, L->d, L->r_gu, P + L->off_w1, 0, L->d, s));
+    SVD_CHECK(launch_tiled_pack<bf16>(u_up, ld_uu, L->d, L->r_gu, P + L->off_w1, L->rp_gu, L->d, s));
+    // v [r, ff] -> v^T [ff, r] (fp16: it multiplies the fp16 XU)
+    SVD_CHECK(launch_tiled_pack<__half>(v_gate, ld_vg, L->r_gu, L->ff, P + L->off_vg, 0, L->r_gu, s));
+    SVD_CHECK(launch_tiled_pack<__half>(v_up, ld_vu, L->r_gu, L->ff, P + L->off_vu, 0, L->r_gu, s));
   }
   if (L->r_d > 0) {
     if (!u_down || !v_down) return SVDMLP_ERR_INVALID_VALUE;
-    // u_down [ff, r_d] -> [rp_d, ld_ff];  v_down [r_d, d] -> [d, rp_d]
+    // u_down [ff, r_d] -> [r_d, ff];  v_down [r_d, d] -> [d, r_d]
     if (L->ud_f16)
-      SVD_CHECK(launch_transpose<__half>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, L->ld_ff, L->rp_d, L->ff, s));
+      SVD_CHECK(launch_tiled_pack<__half>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, 0, L->ff, s));
     else
-      SVD_CHECK(launch_transpose<bf16>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, L->ld_ff, L->rp_d, L->ff, s));
-    SVD_CHECK(launch_transpose<__half>(v_down, ld_vd, L->r_d, L->d, P + L->off_vd, L->rp_d, L->d, L->rp_d, s));
+      SVD_CHECK(launch_tiled_pack<bf16>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, 0, L->ff, s));
+    SVD_CHECK(launch_tiled_pack<__half>(v_down, ld_vd, L->r_d, L->d, P + L->off_vd, 0, L->r_d, s));
   }
   return SVDMLP_OK;
 }
@@ -1171,9 +1239,9 @@ int svdmlp_dense_pack(const svdmlp_layout* L, const void* w_gate, int64_t ld_wg,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* P = static_cast<uint8_t*>(packed);
   SVD_CUDA(cudaMemsetAsync(P, 0, static_cast<size_t>(L->packed_bytes), s));
-  SVD_CHECK(launch_transpose<bf16>(w_gate, ld_wg, L->d, L->ff, P + L->off_vg, L->ld_d, L->ff, L->d, s));
-  SVD_CHECK(launch_transpose<bf16>(w_up, ld_wu, L->d, L->ff, P + L->off_vu, L->ld_d, L->ff, L->d, s));
-  SVD_CHECK(launch_transpose<__half>(w_down, ld_wd, L->ff, L->d, P + L->off_ud, L->ld_ff, L->d, L->ff, s));
+  SVD_CHECK(launch_tiled_pack<bf16>(w_gate, ld_wg, L->d, L->ff, P + L->off_vg, 0, L->d, s));
+  SVD_CHECK(launch_tiled_pack<bf16>(w_up, ld_wu, L->d, L->ff, P + L->off_vu, 0, L->d, s));
+  SVD_CHECK(launch_tiled_pack<__half>(w_down, ld_wd, L->ff, L->d, P + L->off_ud, 0, L->ff, s));
   return SVDMLP_OK;
 }
 

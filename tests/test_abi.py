@@ -43,9 +43,12 @@ def test_layout_sizes(lib):
     from svdflash_b200 import _lib
     L = _lib.Layout()
     assert lib.svdmlp_layout_init(ctypes.byref(L), 4096, 14336, 2867, 2867) == 0
-    assert (L.rp_gu, L.rp_d, L.ld_d, L.ld_ff, L.ud_f16) == (2872, 2872, 4096, 14336, 1)
-    # w1 [2*rp, d] + vg, vu [ff, rp] + ud [rp, ff] + vd [d, rp], 2 bytes each, 256-aligned pieces
-    expect = 2 * 2 * 2872 * 4096 + 2 * 2 * 14336 * 2872 + 2 * 2872 * 14336 + 2 * 4096 * 2872
+    assert (L.rp_gu, L.rp_d, L.ld_d, L.ld_ff, L.ud_f16) == (2880, 2872, 4096, 14336, 1)
+
+    def tiled(n, k):  # 16-row x 64-column tiles, 2 bytes per element
+        return -(-n // 16) * 16 * (-(-k // 64) * 64) * 2
+    # w1 [2*rp_gu, d] + vg, vu [ff, r] + ud [r, ff] + vd [d, r]
+    expect = tiled(2 * 2880, 4096) + 2 * tiled(14336, 2867) + tiled(2867, 14336) + tiled(4096, 2867)
     assert L.packed_bytes == pytest.approx(expect, abs=5 * 256)
     for off in (L.off_w1, L.off_vg, L.off_vu, L.off_ud, L.off_vd):
         assert off % 256 == 0
