@@ -265,9 +265,18 @@ int svdmlp_debug_wait_timeout(void* workspace, int64_t workspace_bytes, int64_t 
  */
 int svdmlp_set_split_override(int stage, int splits);
 
-/* svdmlp_forward runs layers of M <= 64 tokens as one whole-layer decode
- * kernel (1, the default) or as four per-stage kernels (0). */
-int svdmlp_set_layer_decode(int enable);
+/* svdmlp_forward runs layers of M <= max_m tokens as one whole-layer decode
+ * kernel and larger ones as four per-stage kernels.  max_m = 0 turns the
+ * whole-layer kernel off, a negative value restores the default (16, the
+ * measured crossover on B200); at most 64. */
+int svdmlp_set_layer_decode(int max_m);
+
+/* L2 prefetch window of the whole-layer decode kernel's weight stream, in
+ * shared-memory slots (two 16 KB weight tiles each): `ahead_slots` beyond the
+ * slot being loaded while a unit streams, `wait_slots` beyond the slots
+ * already loaded while a unit waits for the previous stage.  0 turns a window
+ * off; both are at most 64. */
+int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots);
 
 /* Timeline of the whole-layer decode kernel (tracing; NULL turns it off).
  * Each launch writes, per CTA, 64 pairs of uint64 (tag | (unit + 1) << 8,

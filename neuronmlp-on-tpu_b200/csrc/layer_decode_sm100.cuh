@@ -1,5 +1,5 @@
 // Whole-layer decode kernel (M <= 64 tokens) for sm_100a: the four GEMM
-// stages of one SVD MLP layer in one persistent, cooperative launch.
+// stages of one SVD MLP layer in one persistent launch.
 //
 //   stage 0  XU = X . [u_g|u_u]                 (bf16 -> fp16)
 //   stage 1  H  = silu(XU_g . v_g) * (XU_u . v_u)   (fp16, dual)
@@ -9,7 +9,7 @@
 // At decode sizes every stage streams its factor matrix from HBM once; the
 // work is the weight bytes.  Running the stages as separate kernels pays a
 // launch, a pipeline ramp and a split-K hand-off per stage.  Here all units
-// of all stages form one list that the co-resident CTAs claim in order, and
+// of all stages form one list that the running CTAs claim in order, and
 // a stage's units wait (bounded) on a per-stage "tiles done" counter before
 // they load their activation tiles.  The weight tiles never depend on an
 // earlier stage, so the producer fetches them before it waits: the weight
@@ -58,6 +58,11 @@ struct LayerDecParams {
   int* next_unit;   // unit claim counter
   int* err;
   unsigned long long timeout_ns;
+  // L2 prefetch window of the weight stream, in slots: while streaming, the
+  // producer keeps the next `pf_ahead` slots of its unit requested from HBM
+  // into L2; while a unit waits on the previous stage it requests up to
+  // `pf_wait` slots beyond those it has already loaded to shared memory.
+  int pf_ahead, pf_wait;
   const __nv_bfloat16* residual;
   long long ld_residual;
   // Optional timeline (null: off): per CTA kTraceEvents pairs of
@@ -94,7 +99,7 @@ struct LayerDecCfg {
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 4 * QUEUE + 1024;
   static_assert(X_BYTES % 1024 == 0, "token tiles stay 1024-byte aligned");
-  static_assert(SMEM_BYTES <= 113 * 1024, "two CTAs per SM");
+  static_assert(SMEM_BYTES <= 227 * 1024, "fits one CTA's shared memory");
   static_assert(TOK == 16 || TOK == 64, "16 or 64 tokens per tile");
 };
 
@@ -233,6 +238,17 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
           if (c.kb0 + 2 * i + 1 < c.kb1) tma_load_2d(&st.x, &full[sl], x1, (c.kb0 + 2 * i + 1) * Cfg::BK, 0);
         }
       };
+      auto slot_pf = [&](const LdUnit& c, int i) {
+        const DecStage& st = p.st[c.s];
+        const int grp = c.n_t * Cfg::BM / 16;
+        if (st.nb == 2) {
+          tma_prefetch_4d(&st.w, c.kb0 + i, grp);
+          tma_prefetch_4d(&st.w2, c.kb0 + i, grp);
+        } else {
+          tma_prefetch_4d(&st.w, c.kb0 + 2 * i, grp);
+          if (c.kb0 + 2 * i + 1 < c.kb1) tma_prefetch_4d(&st.w, c.kb0 + 2 * i + 1, grp);
+        }
+      };
       auto slot_bytes = [&](const LdUnit& c, int i) -> uint32_t {
         const bool two = p.st[c.s].nb == 2 || c.kb0 + 2 * i + 1 < c.kb1;
         return (two ? 2u : 1u) * (Cfg::W_BYTES + Cfg::X_BYTES);
@@ -259,6 +275,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         const LdUnit c = layer_dec_unit(p, u);
         const int ns = unit_slots(p, c);
         int i = 0;
+        int pf = 0;  // slots of this unit requested so far (to L2 or shared memory)
         if (c.s > ready_stage) {
           // Weights first: as many slots as the ring frees up, then wait for
           // the previous stage, then the token tiles of those slots.
@@ -274,6 +291,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
             slot_w(c, pre, sl);
           }
           if (!ok) break;
+          for (pf = pre; pf < min(ns, pre + p.pf_wait); ++pf) slot_pf(c, pf);
           if (ntr < 40) trace_event(p, ntr, TR_DEP_BEGIN, u);
           if (!wait_counter_geq(&p.done[c.s - 1], p.st[c.s - 1].n_tiles, ctx, SITE_DEPENDENCY)) {
             // Complete the slots already announced with their token tiles so
@@ -291,6 +309,8 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         for (; i < ns; ++i, ++it) {
           const int sl = it % STAGES;
           const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+          if (pf < i + 1) pf = i + 1;
+          for (; pf < min(ns, i + 1 + p.pf_ahead); ++pf) slot_pf(c, pf);
           if (!mbar_wait(&empty[sl], ph ^ 1u, ctx, SITE_PRODUCER_EMPTY)) {
             ok = false;
             break;

@@ -116,6 +116,15 @@ SVD_DEV void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* dst, int c
       : "memory");
 }
 
+// L2 prefetch of the same 4-D tile (no shared memory, no barrier): pulls the
+// tile's lines into L2 so that a later tma_load_4d of it hits there.
+SVD_DEV void tma_prefetch_4d(const CUtensorMap* map, int c2, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %1, %2, %3}];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(0), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 SVD_DEV void tma_store_2d(const CUtensorMap* map, const void* src, int x, int y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
@@ -335,7 +344,7 @@ SVD_DEV void red_add_release_gpu(int* p, int v) {
 SVD_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Waits until *ctr >= target (bounded like mbar_wait; the counter is written
-// by other CTAs of the same grid, all of which are co-resident).
+// by other running CTAs of the same grid).
 SVD_DEV bool wait_counter_geq(const int* ctr, int target, const WaitCtx& ctx, int site) {
   if (ld_acquire_gpu(ctr) >= target) return true;
   const uint64_t t0 = global_timer_ns();

@@ -30,7 +30,10 @@ static thread_local int g_last_cuda_error = 0;
 static std::atomic<int64_t> g_launches{0};
 static int g_split_override[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 static unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s: far above any legal wait
-static bool g_layer_decode_enabled = true;  // whole-layer decode kernel for M <= 64
+static constexpr int kLayerDecodeMaxM = 64;        // largest M the whole-layer decode kernel handles
+static constexpr int kLayerDecodeDefaultMaxM = 16; // measured: per-stage kernels are faster above 16 tokens
+static int g_layer_decode_max_m = kLayerDecodeDefaultMaxM;
+static int g_pf_ahead = 1, g_pf_wait = 0;    // L2 prefetch window of the whole-layer decode kernel (slots)
 static unsigned long long* g_trace = nullptr;  // whole-layer decode timeline (diagnostics)
 
 // Optional per-stage event timing (a diagnostics pass; off by default).
@@ -301,12 +304,24 @@ static Plan plan_layer_stage(int M, int tok, int N, int K, int nb, int slots, in
   return p;
 }
 
-static constexpr int kLayerDecodeMaxM = 64;
+// CTAs per SM of the whole-layer decode kernel.  Two fit (shared memory and
+// TMEM allow it) but measure slower than one: the weight stream is bound by
+// HBM and the TMA path, not by copies in flight, and twice the CTAs only
+// lengthen each stage's tail.
+static constexpr int kLayerDecodeCtasPerSm = 1;
+// Shared-memory ring depth (slots of two weight and two token tiles) of the
+// whole-layer decode kernel for 16- and 64-token tiles.
+#ifndef SVDMLP_LD_RING16
+#define SVDMLP_LD_RING16 5
+#endif
+#ifndef SVDMLP_LD_RING64
+#define SVDMLP_LD_RING64 4
+#endif
 
 // Partial bytes of the whole-layer decode kernel (all four stages at once).
 static int64_t layer_decode_partials(const svdmlp_layout* L, int M, int sms) {
   const int tok = M <= 16 ? 16 : 64;
-  const int slots = 2 * sms;
+  const int slots = kLayerDecodeCtasPerSm * sms;
   const int shapes[4][3] = {{2 * L->rp_gu, L->d, 1}, {L->ff, L->r_gu, 2}, {L->r_d, L->ff, 1}, {L->d, L->r_d, 1}};
   int64_t total = 0;
   for (int st = 0; st < 4; ++st) {
@@ -354,20 +369,30 @@ static int64_t partial_bytes(const Plan& p, int BN, int NB) {
 #ifndef SVDMLP_PLAIN_EPI_WARPS
 #define SVDMLP_PLAIN_EPI_WARPS 4
 #endif
+#ifndef SVDMLP_XU_BN
+#define SVDMLP_XU_BN 256      // N of the X.[u_g|u_u] tile
+#endif
+#ifndef SVDMLP_DU_BN
+#define SVDMLP_DU_BN 256      // N of the H.u_down tile
+#endif
+#ifndef SVDMLP_DV_BN
+#define SVDMLP_DV_BN 256      // N of the T.v_down tile
+#endif
 constexpr int kGuBn = SVDMLP_GU_BN, kGuSt = SVDMLP_GU_STAGES, kGuEw = SVDMLP_GU_EPI_WARPS;
+constexpr int kXuBn = SVDMLP_XU_BN, kDuBn = SVDMLP_DU_BN, kDvBn = SVDMLP_DV_BN;
 constexpr int kDgSt = SVDMLP_DENSE_GU_STAGES;
 constexpr int kPlSt = SVDMLP_PLAIN_STAGES, kPlEw = SVDMLP_PLAIN_EPI_WARPS;
 
 // Prefill (M > 128): CTA pairs, 256-row tiles.
 //                          BN     NB shared STG    epilogue   fp16-in out       CTAs epi-warps
-using CfgXU     = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  false, OUT_F16,  2, kPlEw>;  // X.[u_g|u_u] -> XU
+using CfgXU     = GemmCfg<kXuBn,   1, false, kPlSt, EPI_PLAIN,  false, OUT_F16,  2, kPlEw>;  // X.[u_g|u_u] -> XU
 using CfgGU     = GemmCfg<kGuBn, 2, false, kGuSt, EPI_SWIGLU, true,  OUT_F16,  2, kGuEw>;  // XU.v -> H (internal)
 using CfgGUbf   = GemmCfg<kGuBn, 2, false, kGuSt, EPI_SWIGLU, true,  OUT_BF16, 2, kGuEw>;  // XU.v -> H (to caller)
-using CfgDU     = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_F16,  2, kPlEw>;  // H.u_down -> T
-using CfgDUbf   = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  false, OUT_F16,  2, kPlEw>;  // bf16 H.u_down
-using CfgDUf32  = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_F32,  2, kPlEw>;  // H.u_down -> fp32 (TP)
-using CfgDV     = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_BF16, 2, kPlEw>;  // T.v_down -> y
-using CfgDVres  = GemmCfg<256,   1, false, kPlSt, EPI_RESID,  true,  OUT_BF16, 2, kPlEw>;  // + residual
+using CfgDU     = GemmCfg<kDuBn,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_F16,  2, kPlEw>;  // H.u_down -> T
+using CfgDUbf   = GemmCfg<kDuBn,   1, false, kPlSt, EPI_PLAIN,  false, OUT_F16,  2, kPlEw>;  // bf16 H.u_down
+using CfgDUf32  = GemmCfg<kDuBn,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_F32,  2, kPlEw>;  // H.u_down -> fp32 (TP)
+using CfgDV     = GemmCfg<kDvBn,   1, false, kPlSt, EPI_PLAIN,  true,  OUT_BF16, 2, kPlEw>;  // T.v_down -> y
+using CfgDVres  = GemmCfg<kDvBn,   1, false, kPlSt, EPI_RESID,  true,  OUT_BF16, 2, kPlEw>;  // + residual
 using CfgDenseGU = GemmCfg<kGuBn, 2, true, kDgSt, EPI_SWIGLU, false, OUT_F16,  2, kGuEw>;  // X.[w_g|w_u] -> H
 using CfgGemm   = GemmCfg<256,   1, false, kPlSt, EPI_PLAIN,  false, OUT_BF16, 2, kPlEw, false>;  // row-major B
 // Decode (M <= 128): one CTA per tile, split-K across the SMs.
@@ -975,14 +1000,22 @@ static int run_dense(const svdmlp_layout* L, const uint8_t* packed, const void* 
   return gemm_stage<CfgDV, CfgDV1>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s);
 }
 
-// The whole layer for M <= 64 in one cooperative launch (layer_decode_sm100.cuh).
+// The whole layer for M <= 64 in one persistent launch (layer_decode_sm100.cuh).
+//
+// The launch is an ordinary one, not a cooperative one.  A CTA only ever waits
+// for units claimed before its own, and only running CTAs claim units, so the
+// earliest unfinished unit always has its inputs complete and the grid makes
+// progress however many of its CTAs are resident.  (The runtime's occupancy
+// query reports one CTA per SM for every kernel that allocates tensor memory,
+// which would cap a cooperative grid at one CTA per SM; the hardware runs as
+// many as shared memory and the 512 TMEM columns allow.)
 template <int TOK, int STAGES>
 static int launch_layer_decode(LayerDecParams& prm, cudaStream_t s, int sms) {
   using Cfg = LayerDecCfg<TOK, STAGES>;
   static std::mutex mu;
+  int cur = 0;
+  SVD_CUDA(cudaGetDevice(&cur));
   {
-    int cur = 0;
-    SVD_CUDA(cudaGetDevice(&cur));
     static uint64_t done_mask = 0;
     std::lock_guard<std::mutex> lock(mu);
     if (!(done_mask & (1ull << cur))) {
@@ -993,21 +1026,21 @@ static int launch_layer_decode(LayerDecParams& prm, cudaStream_t s, int sms) {
       done_mask |= 1ull << cur;
     }
   }
-  // A cooperative grid must fit on the device at once.
-  int per_sm = 0;
-  SVD_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, layer_decode_kernel<Cfg>, 192, Cfg::SMEM_BYTES));
+  int smem_sm = 0, smem_resv = 0;
+  SVD_CUDA(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, cur));
+  SVD_CUDA(cudaDeviceGetAttribute(&smem_resv, cudaDevAttrReservedSharedMemoryPerBlock, cur));
+  const int by_smem = smem_sm / (Cfg::SMEM_BYTES + smem_resv);
+  const int by_tmem = 512 / static_cast<int>(Cfg::TMEM_COLS);
+  const int per_sm = std::min(kLayerDecodeCtasPerSm, std::min(by_smem, by_tmem));
   if (per_sm < 1) return SVDMLP_ERR_BUDGET;
-  const int grid = std::min(prm.total_units, std::min(per_sm, 2) * sms);
+  const int grid = std::min(prm.total_units, per_sm * sms);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: they wait on one another
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
   TimedLaunch* tl = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_timing_mu);
@@ -1028,13 +1061,10 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
   DeviceInfo* dev = nullptr;
   SVD_CHECK(device_info(&dev));
   const int tok = M <= 16 ? 16 : 64;
-  const int slots = 2 * dev->sms;  // the planning grid; the launch checks that it fits
+  const int slots = kLayerDecodeCtasPerSm * dev->sms;  // the planning grid; the launch checks that it fits
   LayerDecParams prm;
   std::memset(&prm, 0, sizeof(prm));
-#ifndef SVDMLP_LAYER_DECODE_STAGES
-#define SVDMLP_LAYER_DECODE_STAGES 4
-#endif
-  prm.num_stages = SVDMLP_LAYER_DECODE_STAGES;  // fewer only in stage-timing builds
+  prm.num_stages = 4;
   prm.M = M;
   prm.err = w.err;
   prm.timeout_ns = g_wait_limit_ns;
@@ -1044,6 +1074,8 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
   prm.exit_count = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(w.err) + 96);
   prm.next_unit = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(w.err) + 128);
   prm.trace = g_trace;
+  prm.pf_ahead = g_pf_ahead;
+  prm.pf_wait = g_pf_wait;
   const int64_t n1 = 2LL * L->rp_gu;
   // stage operands: token tiles (box TOK rows) and weight panels (box 128 rows)
   struct Spec {
@@ -1104,8 +1136,8 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
     part_left -= pb;
   }
   prm.total_units = prm.st[prm.num_stages - 1].unit_base + prm.st[prm.num_stages - 1].units;
-  if (tok == 16) return launch_layer_decode<16, 3>(prm, s, dev->sms);
-  return launch_layer_decode<64, 2>(prm, s, dev->sms);
+  if (tok == 16) return launch_layer_decode<16, SVDMLP_LD_RING16>(prm, s, dev->sms);
+  return launch_layer_decode<64, SVDMLP_LD_RING64>(prm, s, dev->sms);
 }
 
 // Output target: the caller's buffer when TMA-legal, else workspace staging.
@@ -1331,7 +1363,7 @@ int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, in
   const void* xa;
   int64_t ldxa;
   SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
-  if (M <= kLayerDecodeMaxM && g_layer_decode_enabled) {
+  if (M <= g_layer_decode_max_m) {
     // Decode sizes: the whole layer in one launch; its stores need no TMA
     // alignment, and the residual is read in place (it must not alias y).
     return run_layer_decode(L, P, xa, ldxa, M, y, ldy, residual, ld_res, w, s);
@@ -1513,8 +1545,16 @@ int svdmlp_set_trace_buffer(void* buffer, int64_t bytes) {
   return SVDMLP_OK;
 }
 
-int svdmlp_set_layer_decode(int enable) {
-  g_layer_decode_enabled = enable != 0;
+int svdmlp_set_layer_decode(int max_m) {
+  if (max_m > kLayerDecodeMaxM) return SVDMLP_ERR_INVALID_VALUE;
+  g_layer_decode_max_m = max_m < 0 ? kLayerDecodeDefaultMaxM : max_m;
+  return SVDMLP_OK;
+}
+
+int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots) {
+  if (ahead_slots < 0 || ahead_slots > 64 || wait_slots < 0 || wait_slots > 64) return SVDMLP_ERR_INVALID_VALUE;
+  g_pf_ahead = ahead_slots;
+  g_pf_wait = wait_slots;
   return SVDMLP_OK;
 }
 
@@ -1599,7 +1639,9 @@ int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
   const bool dual = stage == ST_GATEUP || stage == ST_DENSE_GU;
   const int nb = dual ? 2 : 1;
   const int tok = M <= 16 ? 16 : M <= 64 ? 64 : 128;
-  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, N, K, dual ? CfgGU::BN : 256, planning_sms())
+  const int pair_bn = dual ? CfgGU::BN : stage == ST_XU ? CfgXU::BN : stage == ST_DOWN_U ? CfgDU::BN
+                    : stage == ST_DOWN_V || stage == ST_DENSE_D ? CfgDV::BN : CfgGemm::BN;
+  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, N, K, pair_bn, planning_sms())
                                 : plan_stream(M, tok, N, K, nb, (tok <= 64 ? 2 : 1) * planning_sms(),
                                               g_split_override[stage]);
   out6[0] = p.m_tiles;

@@ -119,8 +119,9 @@ def test_decode_sizes_split_k(cuda_device):
 
 @pytest.mark.parametrize("m", [1, 5, 16, 17, 64])
 def test_whole_layer_decode_kernel(cuda_device, m):
-    """M <= 64 runs the one-launch whole-layer decode kernel; it matches the
-    oracle and the four per-stage kernels, with and without a residual."""
+    """The one-launch whole-layer decode kernel (forced up to M = 64, both token
+    tile widths) matches the oracle and the four per-stage kernels, with and
+    without a residual."""
     from svdflash_b200 import _lib
     from svdflash_b200.kernels import ops
     lib = _lib.load()
@@ -131,14 +132,14 @@ def test_whole_layer_decode_kernel(cuda_device, m):
     res = orc.bf16_round(np.random.default_rng(m).standard_normal((m, h), dtype=np.float32))
     rd = to_dev(res, cuda_device)
     try:
-        lib.svdmlp_set_layer_decode(1)
+        assert lib.svdmlp_set_layer_decode(64) == 0
         y1 = ops.svd_mlp_packed(layer, xd)
         y1r = ops.svd_mlp_packed(layer, xd, residual=rd)
         y1b = ops.svd_mlp_packed(layer, xd)
         lib.svdmlp_set_layer_decode(0)
         y0 = ops.svd_mlp_packed(layer, xd)
     finally:
-        lib.svdmlp_set_layer_decode(1)
+        lib.svdmlp_set_layer_decode(-1)
     torch.cuda.synchronize()
     ops.check_device_status(cuda_device)
     ref = orc.svd_mlp(x, *f)
