@@ -57,17 +57,38 @@ def load_peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the run."""
+    """SM clock, power and clock-event (throttle) reasons sampled during the
+    timed region.  NVML is polled from a thread every millisecond, so that a
+    timed region of a few milliseconds still gets samples; nvidia-smi (whose
+    period is at least 100 ms) is the fallback when NVML is not importable."""
 
+    # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, uuid: str | None, period_ms: int = 100):
-        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", f"-lms={period_ms}"]
+    def __init__(self, uuid: str | None, period_ms: float = 1.0):
+        self.samples: list[tuple[float, float, float, int]] = []  # (sm MHz, max MHz, W, reason bits)
+        self.proc = None
+        self.lines: list[str] = []
+        self.nvml = None
+        self.stop_evt = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid) if uuid else pynvml.nvmlDeviceGetHandleByIndex(0)
+            self.nvml, self.h = pynvml, h
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.thread = threading.Thread(target=self._poll, args=(period_ms / 1e3,), daemon=True)
+            self.thread.start()
+            return
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            self.nvml = None
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms=100"]
         if uuid:
             cmd.insert(1, f"-i={uuid}")
-        self.lines: list[str] = []
         try:
             self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
@@ -76,11 +97,40 @@ class ClockSampler:
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
 
+    def _poll(self, period_s: float):
+        nv, h = self.nvml, self.h
+        while not self.stop_evt.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                pw = nv.nvmlDeviceGetPowerUsage(h) / 1000.0
+                rs = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((sm, self.max_mhz, pw, rs))
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(period_s)
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def stop(self) -> dict:
+        if self.nvml is not None:
+            self.stop_evt.set()
+            self.thread.join(timeout=5)
+            reasons = set()
+            for _, _, _, rs in self.samples:
+                for bit, name in self.REASONS.items():
+                    if rs & bit:
+                        reasons.add(name)
+            sm = [x[0] for x in self.samples]
+            return {
+                "sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": self.max_mhz,
+                "power_w_max": max(x[2] for x in self.samples) if self.samples else None,
+                "reasons": sorted(reasons),
+                "samples": len(sm),
+                "source": "nvml",
+            }
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         self.proc.terminate()
@@ -111,6 +161,7 @@ class ClockSampler:
             "power_w_max": max(power) if power else None,
             "reasons": sorted(reasons),
             "samples": len(sm),
+            "source": "nvidia-smi",
         }
 
 

@@ -278,6 +278,16 @@ int svdmlp_set_layer_decode(int max_m);
  * off; both are at most 64. */
 int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots);
 
+/* Prefill layers (M > 128) in svdmlp_forward run their four GEMMs as a chain:
+ * each stage waits per 256-row M-tile on counters the previous stage
+ * publishes, instead of on the whole previous launch, and each stage's units
+ * are ordered in `groups` groups of M-tiles that complete one after another,
+ * so that a stage starts on its first group while its predecessor finishes
+ * the last.  0 (the default) turns chaining off: each stage waits for the
+ * previous launch.  Under the power cap that sustained prefill runs at on B200
+ * chaining measures neutral, so it is opt-in. */
+int svdmlp_set_prefill_chain(int groups);
+
 /* Timeline of the whole-layer decode kernel (tracing; NULL turns it off).
  * Each launch writes, per CTA, 64 pairs of uint64 (tag | (unit + 1) << 8,
  * globaltimer ns): tags 1 start, 2 unit claimed, 3/4 dependency wait

@@ -32,9 +32,21 @@
 // barriers of both CTAs; both epilogues release the accumulator on the even
 // CTA's `acc_empty` barrier.
 //
-// Work units are (m_tile, split, n_tile) with m fastest: the CTAs that run at
-// the same time share the same weight (B) tile, so each weight tile is read
-// from HBM once and served from L2 to the other M-tiles.
+// Work units are (m_tile, split, n_tile), ordered in groups of `m_group`
+// M-tiles: within a group m runs fastest, so the CTAs that run at the same
+// time share the same weight (B) tile (read from HBM once per group and
+// served from L2 to the group's other M-tiles), and the groups complete one
+// after another.
+//
+// Chained stages (the four GEMMs of one prefill layer): instead of waiting for
+// the whole previous launch (griddepcontrol.wait), a stage waits per M-tile on
+// counters that the previous stage bumps once a tile's output is in global
+// memory, and it lets its own dependents launch at once.  The next stage's
+// CTAs therefore take the SMs that the previous stage's tail leaves idle and
+// start on the M-tile groups that are already complete.  A launch only starts
+// once every CTA of its predecessor is resident, and every wait points to an
+// earlier launch, so the chain cannot deadlock.  The last stage's last CTA
+// resets the counters.
 //
 // Split-K (one-CTA configurations only): every split writes an fp32 partial
 // tile (its valid rows) to the workspace and bumps a per-tile counter; the
@@ -73,7 +85,16 @@ struct GemmParams {
   unsigned long long timeout_ns;
   const __nv_bfloat16* residual;  // EPI_RESID: C = acc + residual (bf16)
   long long ld_residual;
+  int m_group;       // M-tiles per group of the unit order (m_tiles: one group, m fastest)
+  // Chained stages (null: not chained, wait for the whole previous launch).
+  const int* dep;    // previous stage's per-M-tile tile counters
+  int dep_target;    // count that marks an M-tile of the previous stage complete
+  int* pub;          // this stage's per-M-tile counters, bumped by each CTA per tile
+  int* reset;        // last stage: counters [3][kChainStride] cleared by the last CTA
+  int* exit_count;   // last stage: CTAs that have left
 };
+
+constexpr int kChainStride = 4096;  // M-tile counters per chained stage
 
 template <int BN_, int NB_, bool SHARED_A_, int STAGES_, int EPI_, bool IN_F16_, int OUT_, int CTAS_ = 1,
           int EPI_WARPS_ = 4, bool B_TILED_ = true>
@@ -135,8 +156,12 @@ struct UnitCoord {
 
 SVD_DEV UnitCoord decode_unit(const GemmParams& p, int u) {
   UnitCoord c;
-  c.m_t = u % p.m_tiles;
-  const int rest = u / p.m_tiles;
+  const int group_units = p.m_group * p.n_tiles * p.splits;
+  const int g = u / group_units;
+  const int gm = min(p.m_group, p.m_tiles - g * p.m_group);  // M-tiles in this (possibly last, short) group
+  const int in_g = u - g * group_units;
+  c.m_t = g * p.m_group + in_g % gm;
+  const int rest = in_g / gm;
   c.ks = rest % p.splits;
   c.n_t = rest / p.splits;
   c.kb0 = c.ks * p.kb_per_split;
@@ -240,15 +265,19 @@ SVD_DEV void add_partials(float (&acc)[32], const float4 (&t0)[8], const float4 
 template <class Cfg>
 SVD_DEV void issue_stage_loads(const CUtensorMap* tm_a, const CUtensorMap* tm_a2, const CUtensorMap* tm_b,
                                const CUtensorMap* tm_b2, uint8_t* smem, int s, uint64_t* full_local,
-                               uint32_t full_leader, int kx, int a_row, int b_row) {
+                               uint32_t full_leader, int kx, int a_row, int b_row, bool do_a = true,
+                               bool do_b = true) {
   uint8_t* a = smem + Cfg::OFF_A + s * Cfg::A_BYTES;
   uint8_t* a2 = smem + Cfg::OFF_A2 + s * Cfg::A_BYTES;
   uint8_t* b = smem + Cfg::OFF_B + s * Cfg::B_BYTES;
   uint8_t* b2 = smem + Cfg::OFF_B2 + s * Cfg::B_BYTES;
   const int kb = kx / Cfg::BK, grp = b_row / 16;
   if constexpr (Cfg::CTAS == 1) {
-    tma_load_2d(tm_a, full_local, a, kx, a_row);
-    if constexpr (Cfg::NA == 2) tma_load_2d(tm_a2, full_local, a2, kx, a_row);
+    if (do_a) {
+      tma_load_2d(tm_a, full_local, a, kx, a_row);
+      if constexpr (Cfg::NA == 2) tma_load_2d(tm_a2, full_local, a2, kx, a_row);
+    }
+    if (!do_b) return;
     if constexpr (Cfg::B_TILED) {
       tma_load_4d(tm_b, full_local, b, kb, grp);
       if constexpr (Cfg::NB == 2) tma_load_4d(tm_b2, full_local, b2, kb, grp);
@@ -257,8 +286,11 @@ SVD_DEV void issue_stage_loads(const CUtensorMap* tm_a, const CUtensorMap* tm_a2
       if constexpr (Cfg::NB == 2) tma_load_2d(tm_b2, full_local, b2, kx, b_row);
     }
   } else {
-    tma_load_2d_pair(tm_a, full_leader, a, kx, a_row);
-    if constexpr (Cfg::NA == 2) tma_load_2d_pair(tm_a2, full_leader, a2, kx, a_row);
+    if (do_a) {
+      tma_load_2d_pair(tm_a, full_leader, a, kx, a_row);
+      if constexpr (Cfg::NA == 2) tma_load_2d_pair(tm_a2, full_leader, a2, kx, a_row);
+    }
+    if (!do_b) return;
     if constexpr (Cfg::B_TILED) {
       tma_load_4d_pair(tm_b, full_leader, b, kb, grp);
       if constexpr (Cfg::NB == 2) tma_load_4d_pair(tm_b2, full_leader, b2, kb, grp);
@@ -336,7 +368,13 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   if (warp == Cfg::PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      grid_dependency_wait();  // inputs of this launch come from the previous one
+      const bool chained = p.dep != nullptr || p.pub != nullptr;
+      // Inputs of an unchained launch (and of a chain's first stage) come from
+      // the previous launch as a whole.  The first stage waits for it before
+      // it lets the chain's later stages launch: those trust the counters,
+      // which the previous chain's last stage clears just before it completes.
+      if (p.dep == nullptr) grid_dependency_wait();
+      if (chained) grid_launch_dependents();  // the next stage may take SMs as this one drains
       const uint32_t full_leader0 = PAIR ? mapa_shared(smem_addr(&full[0]), 0) : 0u;
       int it = 0;
       bool ok = true;
@@ -344,7 +382,37 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         const UnitCoord c = decode_unit(p, u);
         const int a_row = c.m_t * Cfg::TILE_M + static_cast<int>(rank) * Cfg::BM;
         const int b_row = c.n_t * Cfg::BN + static_cast<int>(rank) * Cfg::B_ROWS;
-        for (int kb = c.kb0; kb < c.kb1; ++kb, ++it) {
+        int kb = c.kb0;
+        if (p.dep != nullptr && ld_acquire_gpu(&p.dep[c.m_t]) < p.dep_target) {
+          // Weights first (they do not depend on the previous stage): as many
+          // stages as the ring frees, then the wait, then those stages' A tiles.
+          int pre = 0;
+          for (; pre < min(STAGES, c.kb1 - c.kb0); ++pre) {
+            const int s = (it + pre) % STAGES;
+            const uint32_t ph = static_cast<uint32_t>((it + pre) / STAGES) & 1u;
+            if (!mbar_wait(&empty[s], ph ^ 1u, ctx, SITE_PRODUCER_EMPTY)) {
+              ok = false;
+              break;
+            }
+            if (leader) mbar_arrive_expect_tx(&full[s], Cfg::STAGE_BYTES * Cfg::CTAS);
+            issue_stage_loads<Cfg>(&tm_a, &tm_a2, &tm_b, &tm_b2, smem, s, &full[s], full_leader0 + 8u * s,
+                                   (c.kb0 + pre) * Cfg::BK, a_row, b_row, false, true);
+          }
+          // On a timeout the announced stages still get their A tiles, so that
+          // every barrier phase completes; the error word reports the failure.
+          if (ok && !wait_counter_geq(&p.dep[c.m_t], p.dep_target, ctx, SITE_DEPENDENCY)) ok = false;
+          fence_proxy_async_global();
+          for (int j = 0; j < pre; ++j)
+            issue_stage_loads<Cfg>(&tm_a, &tm_a2, &tm_b, &tm_b2, smem, (it + j) % STAGES, &full[(it + j) % STAGES],
+                                   full_leader0 + 8u * ((it + j) % STAGES), (c.kb0 + j) * Cfg::BK, a_row, b_row,
+                                   true, false);
+          it += pre;
+          kb += pre;
+          if (!ok) break;
+        } else if (p.dep != nullptr) {
+          fence_proxy_async_global();
+        }
+        for (; kb < c.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
           if (!mbar_wait(&empty[s], ph ^ 1u, ctx, SITE_PRODUCER_EMPTY)) {
@@ -356,7 +424,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
                                  kb * Cfg::BK, a_row, b_row);
         }
       }
-      grid_launch_dependents();
+      if (!chained) grid_launch_dependents();
       // Drain: every stage's most recent load must have landed before the CTA
       // may exit (on the normal path these waits return at once).  In a pair
       // the loads complete on the even CTA's barrier, so the odd CTA waits for
@@ -481,6 +549,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
           store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
         }
+        if (p.pub != nullptr) {
+          // Publish this CTA's rows of the tile: each warp's output boxes are
+          // written, then one release increment once every epilogue warp is here.
+          if (lane == 0) {
+            bulk_wait_group<0>();
+            fence_proxy_async_global();
+          }
+          __syncwarp();
+          named_barrier_sync(3, EPI_THREADS);
+          if (threadIdx.x == 0) red_add_release_gpu(&p.pub[c.m_t], 1);
+        }
       } else if constexpr (Cfg::CTAS == 1) {
         // Pass 1: publish this split's fp32 partial tile (valid rows only).
         float* slot = p.partials + static_cast<size_t>(c.tile * p.splits + c.ks) * Cfg::NB * (Cfg::BM * Cfg::BN);
@@ -560,6 +639,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   }
 
   __syncthreads();
+  if (p.exit_count != nullptr && threadIdx.x == 0) {
+    // Last stage of a chain: the last CTA to leave clears the chain's
+    // counters (every wait on them has returned by now) for the next launch.
+    __threadfence();
+    const int e = atomicAdd(p.exit_count, 1);
+    if (e == static_cast<int>(gridDim.x) - 1) {
+      for (int st = 0; st < 3; ++st)
+        for (int m = 0; m < p.m_tiles; ++m) atomicExch(&p.reset[st * kChainStride + m], 0);
+      atomicExch(p.exit_count, 0);
+      __threadfence();
+    }
+  }
   if constexpr (PAIR) cluster_sync();  // the peer's MMAs and arrivals are done
   if (warp == Cfg::MMA_WARP) {
     tc_fence_after();

@@ -33,7 +33,13 @@ static unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s: far above an
 static constexpr int kLayerDecodeMaxM = 64;        // largest M the whole-layer decode kernel handles
 static constexpr int kLayerDecodeDefaultMaxM = 16; // measured: per-stage kernels are faster above 16 tokens
 static int g_layer_decode_max_m = kLayerDecodeDefaultMaxM;
-static int g_pf_ahead = 1, g_pf_wait = 0;    // L2 prefetch window of the whole-layer decode kernel (slots)
+static int g_pf_ahead = 1, g_pf_wait = 0;
+// Prefill stage chaining: M-tile groups per stage (0: off).  Off by default:
+// under the 1 kW power cap that sustained prefill runs at, filling the SMs a
+// stage's tail leaves idle only lowers the clock of the others (measured
+// 330 vs 334 us per layer at M = 1024, 1575 vs 1485 MHz), and two groups
+// read the gate/up weights from HBM twice.
+static int g_chain_groups = 0;    // L2 prefetch window of the whole-layer decode kernel (slots)
 static unsigned long long* g_trace = nullptr;  // whole-layer decode timeline (diagnostics)
 
 // Optional per-stage event timing (a diagnostics pass; off by default).
@@ -431,6 +437,17 @@ enum Stage : int {
 
 // Workspace carving.  The control block holds the error word (int 0) and the
 // split-K counters; the rest holds the intermediates.
+// One link of a chained prefill layer (gemm_sm100.cuh): the counters a stage
+// waits on and the ones it publishes to.
+struct ChainLink {
+  const int* dep;    // previous stage's M-tile counters (null: the first stage)
+  int dep_target;    // 2 x the previous stage's N-tiles (both CTAs of a pair publish)
+  int* pub;          // this stage's M-tile counters (null: the last stage)
+  int* reset;        // last stage: the chain's counter block
+  int* exit_count;   // last stage: exit counter
+  int m_group;       // M-tiles per unit group
+};
+
 struct Workspace {
   int* err;
   int* counters;
@@ -444,6 +461,7 @@ struct Workspace {
   // When the split-K partials of a plan do not fit in partial_cap: false
   // fails the call with SVDMLP_ERR_WORKSPACE, true runs the GEMM unsplit.
   bool unsplit_if_short = false;
+  const ChainLink* chain = nullptr;  // set for the stages of a chained prefill layer
 };
 
 static constexpr int64_t kCtlBytes = 256;
@@ -451,6 +469,9 @@ static constexpr int64_t kCtlBytes = 256;
 // the control block, so that every entry point and layout carves it at the
 // same place and svdmlp_workspace_init zeroes exactly it.
 static constexpr int64_t kCounterBytes = 1 << 20;
+// The last 64 KiB of the counter region hold the chained-prefill counters:
+// [3 stages][kChainStride M-tiles] and one exit counter.
+static constexpr int64_t kChainOffsetInts = (kCounterBytes - 65536) / 4;
 static int64_t counters_bytes(const svdmlp_layout*, int) { return kCounterBytes; }
 
 template <class Cfg>
@@ -589,6 +610,17 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   p.timeout_ns = g_wait_limit_ns;
   p.residual = residual;
   p.ld_residual = ld_res;
+  p.m_group = pl.m_tiles;
+  if (w.chain) {
+    // Chained stages are CTA-pair, unsplit plans by construction of the caller.
+    if (Cfg::CTAS != 2 || pl.splits != 1 || pl.m_tiles > kChainStride) return SVDMLP_ERR_INVALID_VALUE;
+    p.m_group = std::min(w.chain->m_group, pl.m_tiles);
+    p.dep = w.chain->dep;
+    p.dep_target = w.chain->dep_target;
+    p.pub = w.chain->pub;
+    p.reset = w.chain->reset;
+    p.exit_count = w.chain->exit_count;
+  }
   if (partial_bytes(pl, Cfg::BN, Cfg::NB) > w.partial_cap) return SVDMLP_ERR_WORKSPACE;
 
   cudaLaunchConfig_t cfg{};
@@ -940,13 +972,20 @@ template <class S> using PickDVres = typename S::DVres;
 
 // Stage 1 + 2: h = silu(X.u_g.v_g) * (X.u_u.v_u); `h_bf16` selects the
 // caller-facing bf16 output instead of the internal fp16 H.
-static int run_gate_up(const svdmlp_layout* L, const uint8_t* packed, const void* x, int64_t ldx, int M, void* h,
-                       int64_t ldh, bool h_bf16, const Workspace& w, cudaStream_t s) {
+// XU = X . [u_g|u_u]  (fp16, [M, 2 rp_gu])
+static int run_xu(const svdmlp_layout* L, const uint8_t* packed, const void* x, int64_t ldx, int M,
+                  const Workspace& w, cudaStream_t s) {
   const int64_t n1 = 2LL * L->rp_gu;
   const Operand xa{x, false, L->d, M, ldx};
   const Operand w1{packed + L->off_w1, false, L->d, n1, L->ld_d};
-  SVD_CHECK(gemm_stage_dec<CfgXU, PickXU>(xa, xa, w1, w1, Output{w.xu, n1, M, n1}, M, static_cast<int>(n1), L->d,
-                                          ST_XU, w, s));
+  return gemm_stage_dec<CfgXU, PickXU>(xa, xa, w1, w1, Output{w.xu, n1, M, n1}, M, static_cast<int>(n1), L->d,
+                                       ST_XU, w, s);
+}
+
+// H = silu(XU_g . v_g) * (XU_u . v_u)
+static int run_gu(const svdmlp_layout* L, const uint8_t* packed, int M, void* h, int64_t ldh, bool h_bf16,
+                  const Workspace& w, cudaStream_t s) {
+  const int64_t n1 = 2LL * L->rp_gu;
   const Operand ag{w.xu, true, L->r_gu, M, n1};
   const Operand au{w.xu + L->rp_gu, true, L->r_gu, M, n1};
   const Operand bg{packed + L->off_vg, true, L->r_gu, L->ff, L->rp_gu};
@@ -954,6 +993,12 @@ static int run_gate_up(const svdmlp_layout* L, const uint8_t* packed, const void
   const Output ho{h, L->ff, M, ldh};
   if (h_bf16) return gemm_stage<CfgGUbf, CfgGUbf1>(ag, au, bg, bu, ho, M, L->ff, L->r_gu, ST_GATEUP, w, s);
   return gemm_stage_dec<CfgGU, PickGU>(ag, au, bg, bu, ho, M, L->ff, L->r_gu, ST_GATEUP, w, s);
+}
+
+static int run_gate_up(const svdmlp_layout* L, const uint8_t* packed, const void* x, int64_t ldx, int M, void* h,
+                       int64_t ldh, bool h_bf16, const Workspace& w, cudaStream_t s) {
+  SVD_CHECK(run_xu(L, packed, x, ldx, M, w, s));
+  return run_gu(L, packed, M, h, ldh, h_bf16, w, s);
 }
 
 // Stage 3: H . u_down -> T (fp16, workspace) or an fp32 partial.  `h_f16`
@@ -1368,11 +1413,37 @@ int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, in
     // alignment, and the residual is read in place (it must not alias y).
     return run_layer_decode(L, P, xa, ldxa, M, y, ldy, residual, ld_res, w, s);
   }
-  SVD_CHECK(run_gate_up(L, P, xa, ldxa, M, w.h, L->ld_ff, false, w, s));
-  SVD_CHECK(run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, 0, w, s));
   const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
   const void* res = nullptr;
   int64_t ldr = 0;
+  const bool residual_in_place = residual && aligned16(residual, ld_res);
+  if (M >= kPairMinM && g_chain_groups > 0 && cdiv(M, 256) <= kChainStride && (!residual || residual_in_place)) {
+    // Prefill: the four stages as a chain (gemm_sm100.cuh), each stage
+    // starting on the M-tile groups its predecessor has completed.
+    int* base = w.counters + kChainOffsetInts;
+    const int nt_xu = static_cast<int>(cdiv(2LL * L->rp_gu, CfgXU::BN));
+    const int nt_gu = static_cast<int>(cdiv(L->ff, CfgGU::BN));
+    const int nt_du = static_cast<int>(cdiv(L->r_d, CfgDU::BN));
+    const int mg = static_cast<int>(cdiv(cdiv(M, 256), g_chain_groups));  // M-tiles per group
+    const ChainLink links[4] = {
+        {nullptr, 0, base, nullptr, nullptr, mg},
+        {base, 2 * nt_xu, base + kChainStride, nullptr, nullptr, mg},
+        {base + kChainStride, 2 * nt_gu, base + 2 * kChainStride, nullptr, nullptr, mg},
+        {base + 2 * kChainStride, 2 * nt_du, nullptr, base, base + 3 * kChainStride, mg}};
+    Workspace wc[4] = {w, w, w, w};
+    for (int i = 0; i < 4; ++i) wc[i].chain = &links[i];
+    SVD_CHECK(run_xu(L, P, xa, ldxa, M, wc[0], s));
+    SVD_CHECK(run_gu(L, P, M, w.h, L->ld_ff, false, wc[1], s));
+    SVD_CHECK(run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, 0, wc[2], s));
+    if (residual) {
+      res = residual;
+      ldr = ld_res;
+    }
+    SVD_CHECK(run_down_v(L, P, M, yt.ptr, yt.ld, res, ldr, wc[3], s));
+    return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
+  }
+  SVD_CHECK(run_gate_up(L, P, xa, ldxa, M, w.h, L->ld_ff, false, w, s));
+  SVD_CHECK(run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, 0, w, s));
   // An unaligned residual is staged in the x staging buffer once x is consumed.
   if (residual) SVD_CHECK(stage_in(residual, ld_res, M, L->d, w.xs, L->ld_d, &res, &ldr, s));
   SVD_CHECK(run_down_v(L, P, M, yt.ptr, yt.ld, res, ldr, w, s));
@@ -1555,6 +1626,12 @@ int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots) {
   if (ahead_slots < 0 || ahead_slots > 64 || wait_slots < 0 || wait_slots > 64) return SVDMLP_ERR_INVALID_VALUE;
   g_pf_ahead = ahead_slots;
   g_pf_wait = wait_slots;
+  return SVDMLP_OK;
+}
+
+int svdmlp_set_prefill_chain(int groups) {
+  if (groups < 0 || groups > 64) return SVDMLP_ERR_INVALID_VALUE;
+  g_chain_groups = groups;
   return SVDMLP_OK;
 }
 

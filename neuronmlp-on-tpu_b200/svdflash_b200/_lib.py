@@ -83,6 +83,7 @@ SIGNATURES = {
     "svdmlp_set_split_override": (c_int, [c_int, c_int]),
     "svdmlp_set_layer_decode": (c_int, [c_int]),
     "svdmlp_set_decode_prefetch": (c_int, [c_int, c_int]),
+    "svdmlp_set_prefill_chain": (c_int, [c_int]),
     "svdmlp_set_trace_buffer": (c_int, [V, I64]),
     "svdmlp_plan_info": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_int)]),
     "svdmlp_stage_timing": (c_int, [c_int]),

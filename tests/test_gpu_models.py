@@ -148,3 +148,39 @@ def test_whole_layer_decode_kernel(cuda_device, m):
     assert torch.equal(y1, y1b), "repeated launches differ"
     from helpers import assert_close_bf16_output
     assert_close_bf16_output(to_np(y1), to_np(y0), what=f"layer decode vs per-stage m={m}")
+
+
+@pytest.mark.parametrize("m", [129, 300, 700])
+def test_prefill_chain_matches_unchained(cuda_device, m):
+    """Prefill layers run their four GEMMs as a chain (per-M-tile counters in
+    place of whole-launch waits, M-tile groups in the unit order).  The tiles
+    and their accumulation order are the same as the unchained path, so the
+    outputs are bit-identical; repeated calls re-arm the counters; partial
+    and odd M-tile counts and the residual epilogue are covered."""
+    from svdflash_b200 import _lib
+    from svdflash_b200.kernels import ops
+    lib = _lib.load()
+    h, r, i = 1024, 700, 3584
+    x, f = orc.make_inputs(120 + m, m, h, i, r)
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f])
+    xd = to_dev(x, cuda_device)
+    res = orc.bf16_round(np.random.default_rng(m).standard_normal((m, h), dtype=np.float32))
+    rd = to_dev(res, cuda_device)
+    try:
+        assert lib.svdmlp_set_prefill_chain(2) == 0
+        ys = [ops.svd_mlp_packed(layer, xd) for _ in range(3)]
+        yr = ops.svd_mlp_packed(layer, xd, residual=rd)
+        assert lib.svdmlp_set_prefill_chain(3) == 0
+        y1 = ops.svd_mlp_packed(layer, xd)
+        assert lib.svdmlp_set_prefill_chain(0) == 0
+        y0 = ops.svd_mlp_packed(layer, xd)
+        y0r = ops.svd_mlp_packed(layer, xd, residual=rd)
+    finally:
+        lib.svdmlp_set_prefill_chain(0)
+    torch.cuda.synchronize()
+    ops.check_device_status(cuda_device)
+    for k, y in enumerate(ys):
+        assert torch.equal(y, y0), f"chained call {k} differs from the unchained path"
+    assert torch.equal(y1, y0), "three M-tile groups differ from the unchained path"
+    assert torch.equal(yr, y0r), "chained residual epilogue differs"
+    assert_close(to_np(ys[0]), orc.svd_mlp(x, *f), what=f"chained prefill m={m}")
