@@ -248,6 +248,119 @@ def parity_sample(x, factors, y, nrows=16):
     return orc.error_metrics(y[rows].float().cpu().numpy(), ref)
 
 
+def _time_events(fn, steps: int, warmup: int) -> float:
+    """Milliseconds per call of fn() on the current stream (CUDA events)."""
+    import torch
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_sweep(args) -> None:
+    """--sweep: one JSON line per point of BASELINE configs 2, 3 and 5 (single GPU).
+
+    decode  config 2: M in {1, 8, 32, 128} x ratio {0.6, 0.8, 0.9}; HBM-bound, bytes =
+            the three factor pairs once + x and y, against the measured copy bandwidth.
+    shapes  config 5: ratio {0.4, 0.6, 0.8, 0.9, 1.0 = dense} x seq {512..8192} x batch
+            {1, 4}; SVD/dense speed-up and tensor roofline fraction.
+    stack   config 3: 32 blocks of x + mlp(rmsnorm(x)) at seq {1024, 4096}, SVD (0.9) and
+            dense arms, each captured as one CUDA graph.
+    Weights are synthetic seeded draws of the named shapes; every point streams factor
+    matrices larger than L2 per call, so no flush is needed between calls."""
+    import torch
+
+    from svdflash_b200 import _lib
+    from svdflash_b200.kernels import ops
+    from svdflash_b200.models import DenseLlamaMLP, MlpBlockStack, SvdLlamaMLP
+    _lib.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks, src = load_peaks()
+    d, ff = 4096, 14336
+
+    def dense_w(seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        mk = lambda a, b: (torch.randn(a, b, generator=g, device=dev) / math.sqrt(a)).to(torch.bfloat16)
+        return mk(d, ff), mk(d, ff), mk(ff, d)
+
+    def emit(rec):
+        rec.setdefault("data", "synthetic")
+        print(json.dumps(rec), flush=True)
+
+    if args.sweep == "decode":
+        for ratio in (0.6, 0.8, 0.9):
+            r = rank_for(d, ff, ratio)
+            layer = ops.pack_svd_layer(*make_factors(d, ff, r, args.seed, dev))
+            for m in (1, 8, 32, 128):
+                x = torch.randn(m, d, device=dev).to(torch.bfloat16)
+                y = torch.empty_like(x)
+                ms = _time_events(lambda: ops.svd_mlp_packed(layer, x, out=y), args.steps, args.warmup)
+                nbytes = 2.0 * 3 * r * (d + ff) + 4.0 * m * d
+                gbs = nbytes / (ms * 1e-3) / 1e9
+                emit({"sweep": "decode", "ratio": ratio, "r": r, "tokens": m, "us_per_layer": ms * 1e3,
+                      "hbm_gbs": gbs, "frac_of_measured_hbm": gbs / float(peaks["hbm_gbs"]),
+                      "frac_of_nominal_8tbs": gbs / 8000.0, "bytes_per_layer": nbytes, "peak_source": src})
+            del layer
+            torch.cuda.empty_cache()
+    elif args.sweep == "shapes":
+        dense = ops.pack_dense_layer(*dense_w(args.seed + 7))
+        layers = {ratio: ops.pack_svd_layer(*make_factors(d, ff, rank_for(d, ff, ratio), args.seed, dev))
+                  for ratio in (0.4, 0.6, 0.8, 0.9)}
+        peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+        for batch in (1, 4):
+            for seq in (512, 1024, 2048, 4096, 8192):
+                m = batch * seq
+                x = torch.randn(m, d, device=dev).to(torch.bfloat16)
+                y = torch.empty_like(x)
+                steps = max(3, min(args.steps, int(2e5 / m)))
+                ms_dense = _time_events(lambda: ops.dense_mlp_packed(dense, x, out=y), steps, args.warmup)
+                fl_dense = 6.0 * m * d * ff
+                emit({"sweep": "shapes", "batch": batch, "seq": seq, "tokens": m, "ratio": 1.0, "arm": "dense",
+                      "us_per_layer": ms_dense * 1e3, "tflops": fl_dense / (ms_dense * 1e-3) / 1e12,
+                      "frac_of_sustained_peak": fl_dense / (ms_dense * 1e-3) / 1e12 / peak})
+                for ratio, layer in layers.items():
+                    r = rank_for(d, ff, ratio)
+                    ms = _time_events(lambda: ops.svd_mlp_packed(layer, x, out=y), steps, args.warmup)
+                    fl = 6.0 * m * r * (d + ff)
+                    emit({"sweep": "shapes", "batch": batch, "seq": seq, "tokens": m, "ratio": ratio, "r": r,
+                          "arm": "svd", "us_per_layer": ms * 1e3, "tflops": fl / (ms * 1e-3) / 1e12,
+                          "frac_of_sustained_peak": fl / (ms * 1e-3) / 1e12 / peak,
+                          "speedup_vs_dense": ms_dense / ms})
+                del x, y
+    elif args.sweep == "stack":
+        n_layers, ratio = 32, 0.9
+        r = rank_for(d, ff, ratio)
+        gn = torch.Generator(device=dev)
+        gn.manual_seed(args.seed + 99)
+        norms = [(1 + 0.02 * torch.randn(d, generator=gn, device=dev)).to(torch.bfloat16) for _ in range(n_layers)]
+        for arm in ("svd", "dense"):
+            if arm == "svd":
+                mlps = [SvdLlamaMLP(*make_factors(d, ff, r, args.seed + 1000 + l, dev)) for l in range(n_layers)]
+            else:
+                mlps = [DenseLlamaMLP(*dense_w(args.seed + 2000 + l)) for l in range(n_layers)]
+            stack = MlpBlockStack(mlps, norms)
+            for seq in (1024, 4096):
+                x = torch.randn(seq, d, device=dev).to(torch.bfloat16)
+                stack.capture(seq, d, dev)
+                ms = _time_events(lambda: stack.replay(x), max(3, min(args.steps, 50)), args.warmup)
+                fl = n_layers * 6.0 * seq * (r * (d + ff) if arm == "svd" else d * ff)
+                emit({"sweep": "stack", "arm": arm, "layers": n_layers, "seq": seq, "ratio": ratio if arm == "svd" else 1.0,
+                      "ms_per_stack": ms, "tokens_per_s": seq / (ms * 1e-3), "tflops": fl / (ms * 1e-3) / 1e12,
+                      "graph": True})
+                stack._graph = None
+            del mlps, stack
+            torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -258,9 +371,14 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-reps", type=int, default=3)
+    ap.add_argument("--sweep", choices=("decode", "shapes", "stack"), default=None,
+                    help="print one JSON line per point of BASELINE configs 2, 5 or 3 instead of the bench line")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
+    if args.sweep:
+        run_sweep(args)
+        return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
         run_reference_arm(args, wl)

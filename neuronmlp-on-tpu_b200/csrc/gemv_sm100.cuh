@@ -8,9 +8,13 @@
 // tokens are the MMA's N (TOK = 16..128, zero-filled beyond M by the TMA
 // unit), so the tensor core does little wasted work and the activation tile
 // is small.  The accumulator in TMEM is transposed: TMEM lane = output
-// feature, column = token.  Each epilogue thread owns one output feature and
-// writes out[t][f] for t < M (consecutive features across a warp, so the
-// stores coalesce).
+// feature, column = token.  The epilogue moves each 16-token chunk through
+// shared memory (one thread per feature writes a column of an fp32
+// [16][128] tile) and then writes whole output rows: a warp stores the 128
+// features of one token (256 bytes of fp16/bf16) with 8-byte vectors, so
+// every store fills whole 128-byte lines.  Per-token scattered 2-byte stores
+// (one half-line per warp and token) cost ~50 ns each under a full weight
+// stream; full-line stores do not.
 //
 // Dual form (NB == 2): C = silu(X.Wg^T) * (X2.Wu^T), the decode gate/up stage.
 //
@@ -56,7 +60,9 @@ struct DecCfg {
   static constexpr uint32_t IDESC = make_idesc_16bit(BM, TOK, IN_F16);
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = OFF_W + STAGES * NB * W_BYTES;
-  static constexpr int OFF_BAR = OFF_X + STAGES * NB * X_BYTES;
+  static constexpr int STG_BYTES = 16 * BM * 4;  // fp32 [16 tokens][128 features] output staging
+  static constexpr int OFF_STG = OFF_X + STAGES * NB * X_BYTES;
+  static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
@@ -77,21 +83,54 @@ SVD_DEV DecUnit decode_dec_unit(const GemmParams& p, int u) {
   return c;
 }
 
-// Stores tokens [t0, t0 + 16) of feature f (bounds-checked against M and N).
+// Writes four consecutive features [f, f + 4) of token t: epilogue residual,
+// conversion and a vector store when all four are inside N (scalar tail
+// otherwise).  Rows and the output base are 16-byte aligned.
 template <class Cfg>
-SVD_DEV void dec_store_chunk(const GemmParams& p, void* out, long long ld_out, int f, int t0, const float (&v)[16]) {
-  if (f >= p.N) return;
+SVD_DEV void dec_store4(const GemmParams& p, void* out, long long ld_out, int t, int f, float4 v) {
+  if (t >= p.M || f >= p.N) return;
+  float x[4] = {v.x, v.y, v.z, v.w};
+  const bool full = f + 4 <= p.N;
+  if constexpr (Cfg::EPI == EPI_RESID) {
+    const __nv_bfloat16* r = p.residual + static_cast<long long>(t) * p.ld_residual + f;
+    if (full) {
+      const uint2 w = *reinterpret_cast<const uint2*>(r);
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w.y));
+      x[0] += a.x;
+      x[1] += a.y;
+      x[2] += b.x;
+      x[3] += b.y;
+    } else {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    const int t = t0 + j;
-    if (t < p.M) {
-      float x = v[j];
-      if constexpr (Cfg::EPI == EPI_RESID) x += __bfloat162float(p.residual[static_cast<long long>(t) * p.ld_residual + f]);
-      const long long off = static_cast<long long>(t) * ld_out + f;
-      if constexpr (Cfg::OUT == OUT_F32) static_cast<float*>(out)[off] = x;
-      else if constexpr (Cfg::OUT == OUT_F16)
-        static_cast<__half*>(out)[off] = __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f));
-      else static_cast<__nv_bfloat16*>(out)[off] = __float2bfloat16(x);
+      for (int j = 0; j < 4; ++j)
+        if (f + j < p.N) x[j] += __bfloat162float(r[j]);
+    }
+  }
+  const long long off = static_cast<long long>(t) * ld_out + f;
+  if constexpr (Cfg::OUT == OUT_F32) {
+    float* o = static_cast<float*>(out) + off;
+    if (full) *reinterpret_cast<float4*>(o) = make_float4(x[0], x[1], x[2], x[3]);
+    else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (f + j < p.N) o[j] = x[j];
+    }
+  } else if constexpr (Cfg::OUT == OUT_F16) {
+    __half* o = static_cast<__half*>(out) + off;
+    if (full) *reinterpret_cast<uint2*>(o) = make_uint2(pack_f16x2_sat(x[0], x[1]), pack_f16x2_sat(x[2], x[3]));
+    else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (f + j < p.N) o[j] = __float2half_rn(fminf(fmaxf(x[j], -65504.f), 65504.f));
+    }
+  } else {
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out) + off;
+    if (full) *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(x[0], x[1]), pack_bf16x2(x[2], x[3]));
+    else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (f + j < p.N) o[j] = __float2bfloat16(x[j]);
     }
   }
 }
@@ -262,13 +301,15 @@ __global__ void __launch_bounds__(192)
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
       const int row = q * 32 + static_cast<int>(lane);   // feature within the 128-row panel
-      const int f = c.n_t * Cfg::BM + row;
       const int tv = min(p.M, TOK);                      // valid tokens
       constexpr int NCH = TOK / 16;
-      // Partial slot of this split: [tile][split][branch][128 features][TOK tokens] fp32.
+      // Partial slot of this split: [tile][split][branch][TOK tokens][128 features] fp32,
+      // token-major so that a warp's 32 features of one token are one 128-byte line.
       const size_t tile_slot = static_cast<size_t>(c.n_t) * p.splits;
-      float* slot = p.partials + ((tile_slot + c.ks) * Cfg::NB) * (Cfg::BM * TOK) + static_cast<size_t>(row) * TOK;
-#pragma unroll
+      float* slot = p.partials + ((tile_slot + c.ks) * Cfg::NB) * (Cfg::BM * TOK) + row;
+      float* stg = reinterpret_cast<float*>(smem + Cfg::OFF_STG);
+      const int f0 = c.n_t * Cfg::BM;
+#pragma unroll 1
       for (int ch = 0; ch < NCH; ++ch) {
         uint32_t rg[16], ru[16];
         tmem_ld_x16(tacc + ch * 16, rg);
@@ -279,7 +320,7 @@ __global__ void __launch_bounds__(192)
           __syncwarp();
           if (lane == 0) mbar_arrive(&acc_empty[b]);  // every TMEM read has returned
         }
-        if (16 * ch >= tv) continue;
+        if (16 * ch >= tv) continue;  // the same for all four warps
         float v[16], w[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
@@ -291,79 +332,122 @@ __global__ void __launch_bounds__(192)
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = silu_mul(v[j], w[j]);
           }
-          dec_store_chunk<Cfg>(p, out, ld_out, f, 16 * ch, v);
+          // column `row` of the fp32 [16 tokens][128 features] staging tile
+#pragma unroll
+          for (int j = 0; j < 16; ++j) stg[j * Cfg::BM + row] = v[j];
+          named_barrier_sync(3, 128);
+          // whole rows: thread -> (token row, feature quad), a warp per row
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int idx = static_cast<int>(threadIdx.x) + 128 * i;
+            const int rr = idx >> 5, c4 = idx & 31;
+            const float4 x = *reinterpret_cast<const float4*>(stg + rr * Cfg::BM + 4 * c4);
+            dec_store4<Cfg>(p, out, ld_out, 16 * ch + rr, f0 + 4 * c4, x);
+          }
+          named_barrier_sync(3, 128);  // read before the next chunk overwrites it
         } else {
 #pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4) {
-            __stcg(reinterpret_cast<float4*>(slot + 16 * ch) + j4,
-                   make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]));
-            if constexpr (Cfg::NB == 2)
-              __stcg(reinterpret_cast<float4*>(slot + Cfg::BM * TOK + 16 * ch) + j4,
-                     make_float4(w[4 * j4], w[4 * j4 + 1], w[4 * j4 + 2], w[4 * j4 + 3]));
+          for (int j = 0; j < 16; ++j) {
+            if (16 * ch + j < tv) {
+              __stcg(slot + (16 * ch + j) * Cfg::BM, v[j]);
+              if constexpr (Cfg::NB == 2) __stcg(slot + Cfg::BM * TOK + (16 * ch + j) * Cfg::BM, w[j]);
+            }
           }
         }
       }
       if (p.splits > 1) {
+        // Fix-up.  Up to 16 tokens: the split that arrives last sums every
+        // split's partial (tiny).  Beyond that the reads of S fp32 partial
+        // tiles are too much for one CTA, so every split of the tile waits
+        // (bounded) until all S partials are in and sums the token rows
+        // r = ks (mod S); a second pass over the same counter lets the last
+        // one to finish reset it.
+        const bool spread = tv > 16;
         __threadfence();
         named_barrier_sync(1, 128);
         if (threadIdx.x == 0) {
           const int old = atomicAdd(&p.counters[c.n_t], 1);
-          *fix_flag = (old == p.splits - 1) ? 1 : 0;
+          int go = spread ? 1 : (old == p.splits - 1 ? 1 : 0);
+          if (spread && !wait_counter_geq(&p.counters[c.n_t], p.splits, ctx, SITE_DEPENDENCY)) go = 0;
+          *fix_flag = go;
         }
         named_barrier_sync(1, 128);
         if (*fix_flag) {
           __threadfence();
-          const float* base = p.partials + (tile_slot * Cfg::NB) * (Cfg::BM * TOK) + static_cast<size_t>(row) * TOK;
+          // Row-vector mapping (thread -> token row, feature quad): the
+          // token-major partials are read as whole 512-byte rows, up to four
+          // splits' loads in flight, summed in split order.
+          const float* base = p.partials + (tile_slot * Cfg::NB) * (Cfg::BM * TOK);
+          constexpr int VI = Cfg::NB == 2 ? 2 : 4;  // row vectors per thread and pass
+          const int r0 = spread ? c.ks : 0, rstep = spread ? p.splits : 1;
+          const int rows = (tv - r0 + rstep - 1) / rstep;  // token rows this CTA sums
+#pragma unroll 1
+          for (int lr0 = 0; lr0 < rows; lr0 += 4 * VI) {
+            float4 g[VI], uacc[VI];
+            int tt[VI], ff[VI];
 #pragma unroll
-          for (int ch = 0; ch < NCH; ++ch) {
-            if (16 * ch >= tv) continue;
-            float v[16], w[16];
-#pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              v[j] = 0.f;
-              w[j] = 0.f;
+            for (int i = 0; i < VI; ++i) {
+              const int idx = static_cast<int>(threadIdx.x) + 128 * i;
+              const int lr = lr0 + (idx >> 5);
+              tt[i] = lr < rows ? r0 + lr * rstep : TOK;  // TOK: no row
+              ff[i] = 4 * (idx & 31);
+              g[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+              uacc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
             }
-            // Up to 4 splits' loads in flight per step; the sum is in split order.
 #pragma unroll 1
             for (int s0 = 0; s0 < p.splits; s0 += 4) {
-              float4 g4[4][4], u4[4][4];
+              float4 lg[4][VI], lu[4][VI];
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
-                const bool have = s0 + j < p.splits;
-                const float* src = base + static_cast<size_t>((s0 + j) * Cfg::NB) * (Cfg::BM * TOK) + 16 * ch;
 #pragma unroll
-                for (int j4 = 0; j4 < 4; ++j4) {
-                  g4[j][j4] = have ? __ldcg(reinterpret_cast<const float4*>(src) + j4) : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int i = 0; i < VI; ++i) {
+                  const bool ld = s0 + j < p.splits && tt[i] < tv;
+                  const float* src = base + static_cast<size_t>((s0 + j) * Cfg::NB) * (Cfg::BM * TOK) +
+                                     (ld ? tt[i] : 0) * Cfg::BM + ff[i];
+                  lg[j][i] = ld ? __ldcg(reinterpret_cast<const float4*>(src)) : make_float4(0.f, 0.f, 0.f, 0.f);
                   if constexpr (Cfg::NB == 2)
-                    u4[j][j4] = have ? __ldcg(reinterpret_cast<const float4*>(src + Cfg::BM * TOK) + j4)
-                                     : make_float4(0.f, 0.f, 0.f, 0.f);
+                    lu[j][i] = ld ? __ldcg(reinterpret_cast<const float4*>(src + Cfg::BM * TOK))
+                                  : make_float4(0.f, 0.f, 0.f, 0.f);
                 }
               }
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
 #pragma unroll
-                for (int j4 = 0; j4 < 4; ++j4) {
-                  v[4 * j4] += g4[j][j4].x;
-                  v[4 * j4 + 1] += g4[j][j4].y;
-                  v[4 * j4 + 2] += g4[j][j4].z;
-                  v[4 * j4 + 3] += g4[j][j4].w;
+                for (int i = 0; i < VI; ++i) {
+                  g[i].x += lg[j][i].x;
+                  g[i].y += lg[j][i].y;
+                  g[i].z += lg[j][i].z;
+                  g[i].w += lg[j][i].w;
                   if constexpr (Cfg::NB == 2) {
-                    w[4 * j4] += u4[j][j4].x;
-                    w[4 * j4 + 1] += u4[j][j4].y;
-                    w[4 * j4 + 2] += u4[j][j4].z;
-                    w[4 * j4 + 3] += u4[j][j4].w;
+                    uacc[i].x += lu[j][i].x;
+                    uacc[i].y += lu[j][i].y;
+                    uacc[i].z += lu[j][i].z;
+                    uacc[i].w += lu[j][i].w;
                   }
                 }
               }
             }
-            if constexpr (Cfg::EPI == EPI_SWIGLU) {
 #pragma unroll
-              for (int j = 0; j < 16; ++j) v[j] = silu_mul(v[j], w[j]);
+            for (int i = 0; i < VI; ++i) {
+              if constexpr (Cfg::EPI == EPI_SWIGLU) {
+                g[i].x = silu_mul(g[i].x, uacc[i].x);
+                g[i].y = silu_mul(g[i].y, uacc[i].y);
+                g[i].z = silu_mul(g[i].z, uacc[i].z);
+                g[i].w = silu_mul(g[i].w, uacc[i].w);
+              }
+              if (tt[i] < tv) dec_store4<Cfg>(p, out, ld_out, tt[i], f0 + ff[i], g[i]);
             }
-            dec_store_chunk<Cfg>(p, out, ld_out, f, 16 * ch, v);
           }
-          named_barrier_sync(1, 128);
-          if (threadIdx.x == 0) p.counters[c.n_t] = 0;
+        }
+        named_barrier_sync(1, 128);
+        if (threadIdx.x == 0) {
+          if (!spread) {
+            if (*fix_flag) p.counters[c.n_t] = 0;
+          } else {
+            // second pass: the last split to finish its rows re-arms the counter
+            const int old = atomicAdd(&p.counters[c.n_t], 1);
+            if (old == 2 * p.splits - 1) p.counters[c.n_t] = 0;
+          }
         }
       }
       ++acc_it;

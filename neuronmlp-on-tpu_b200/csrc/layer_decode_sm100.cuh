@@ -41,7 +41,7 @@ struct alignas(64) DecStage {
   CUtensorMap x, x2, w, w2;  // token operand(s) [M, K] (2-D) and packed tiled weight(s) [N, K] (4-D)
   void* out;
   long long ld_out;
-  float* partials;   // [tiles][splits][nb][128][TOK] fp32
+  float* partials;   // [tiles][splits][nb][TOK][128] fp32 (token-major)
   int* tile_counters;
   int N, K, n_tiles, k_blocks, splits, kb_per_split, units, unit_base;
   int nb;            // 1, or 2 for the dual SwiGLU stage
@@ -418,7 +418,8 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
       const bool dual = st.nb == 2;
       constexpr int NCH = TOK / 16;
       const size_t tile_slot = static_cast<size_t>(c.n_t) * st.splits;
-      float* slot = st.partials + ((tile_slot + c.ks) * 2) * (Cfg::BM * TOK) + static_cast<size_t>(row) * TOK;
+      // token-major partial: a warp's 32 features of one token are one 128-byte line
+      float* slot = st.partials + ((tile_slot + c.ks) * 2) * (Cfg::BM * TOK) + row;
 #pragma unroll
       for (int ch = 0; ch < NCH; ++ch) {
         uint32_t rg[16], ru[16];
@@ -445,12 +446,11 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
           ld_store_chunk<TOK>(p, st, f, 16 * ch, v);
         } else {
 #pragma unroll
-          for (int j4 = 0; j4 < 4; ++j4) {
-            __stcg(reinterpret_cast<float4*>(slot + 16 * ch) + j4,
-                   make_float4(v[4 * j4], v[4 * j4 + 1], v[4 * j4 + 2], v[4 * j4 + 3]));
-            if (dual)
-              __stcg(reinterpret_cast<float4*>(slot + Cfg::BM * TOK + 16 * ch) + j4,
-                     make_float4(w[4 * j4], w[4 * j4 + 1], w[4 * j4 + 2], w[4 * j4 + 3]));
+          for (int j = 0; j < 16; ++j) {
+            if (16 * ch + j < tv) {
+              __stcg(slot + (16 * ch + j) * Cfg::BM, v[j]);
+              if (dual) __stcg(slot + Cfg::BM * TOK + (16 * ch + j) * Cfg::BM, w[j]);
+            }
           }
         }
       }
@@ -465,7 +465,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         }
         named_barrier_sync(1, 128);
         if (*fix_flag) {
-          const float* base = st.partials + (tile_slot * 2) * (Cfg::BM * TOK) + static_cast<size_t>(row) * TOK;
+          const float* base = st.partials + (tile_slot * 2) * (Cfg::BM * TOK) + row;
 #pragma unroll
           for (int ch = 0; ch < NCH; ++ch) {
             if (16 * ch >= tv) continue;
@@ -475,32 +475,28 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
               v[j] = 0.f;
               w[j] = 0.f;
             }
+            // Two splits' loads in flight per step (one 128-byte line per warp
+            // and token); the sum is in split order.
 #pragma unroll 1
-            for (int s0 = 0; s0 < st.splits; s0 += 4) {
-              float4 g4[4][4], u4[4][4];
+            for (int s0 = 0; s0 < st.splits; s0 += 2) {
+              float g[2][16], u[2][16];
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
+              for (int j = 0; j < 2; ++j) {
                 const bool have = s0 + j < st.splits;
-                const float* src = base + static_cast<size_t>((s0 + j) * 2) * (Cfg::BM * TOK) + 16 * ch;
+                const float* src = base + static_cast<size_t>((s0 + j) * 2) * (Cfg::BM * TOK) + 16 * ch * Cfg::BM;
 #pragma unroll
-                for (int j4 = 0; j4 < 4; ++j4) {
-                  g4[j][j4] = have ? __ldcg(reinterpret_cast<const float4*>(src) + j4) : make_float4(0.f, 0.f, 0.f, 0.f);
-                  u4[j][j4] = have && dual ? __ldcg(reinterpret_cast<const float4*>(src + Cfg::BM * TOK) + j4)
-                                           : make_float4(0.f, 0.f, 0.f, 0.f);
+                for (int t = 0; t < 16; ++t) {
+                  const bool ld = have && 16 * ch + t < tv;
+                  g[j][t] = ld ? __ldcg(src + t * Cfg::BM) : 0.f;
+                  u[j][t] = ld && dual ? __ldcg(src + Cfg::BM * TOK + t * Cfg::BM) : 0.f;
                 }
               }
 #pragma unroll
-              for (int j = 0; j < 4; ++j) {
+              for (int j = 0; j < 2; ++j) {
 #pragma unroll
-                for (int j4 = 0; j4 < 4; ++j4) {
-                  v[4 * j4] += g4[j][j4].x;
-                  v[4 * j4 + 1] += g4[j][j4].y;
-                  v[4 * j4 + 2] += g4[j][j4].z;
-                  v[4 * j4 + 3] += g4[j][j4].w;
-                  w[4 * j4] += u4[j][j4].x;
-                  w[4 * j4 + 1] += u4[j][j4].y;
-                  w[4 * j4 + 2] += u4[j][j4].z;
-                  w[4 * j4 + 3] += u4[j][j4].w;
+                for (int t = 0; t < 16; ++t) {
+                  v[t] += g[j][t];
+                  w[t] += u[j][t];
                 }
               }
             }

@@ -418,7 +418,7 @@ using CfgGemm1   = GemmCfg<256, 1, false, 4, EPI_PLAIN,  false, OUT_BF16, 1, 4, 
 template <int TOK>
 struct DecSet {
   static constexpr int PST = TOK == 16 ? 5 : TOK == 64 ? 4 : 3;  // stages, one-branch kernels
-  static constexpr int DST = TOK == 16 ? 3 : TOK == 64 ? 2 : 3;  // stages, dual kernels
+  static constexpr int DST = TOK == 64 ? 2 : TOK == 16 ? 2 : 3;  // stages, dual kernels (TOK <= 64: two CTAs per SM)
   using XU = DecCfg<TOK, 1, PST, EPI_PLAIN, false, OUT_F16>;
   using GU = DecCfg<TOK, 2, DST, EPI_SWIGLU, true, OUT_F16>;
   using DU = DecCfg<TOK, 1, PST, EPI_PLAIN, true, OUT_F16>;
