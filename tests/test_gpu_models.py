@@ -117,6 +117,42 @@ def test_decode_sizes_split_k(cuda_device):
     ops.check_device_status(cuda_device)
 
 
+@pytest.mark.parametrize("m", [17, 40, 100, 128])
+def test_per_stage_decode_forced_splits(cuda_device, m):
+    """Per-stage decode kernels (16 < M <= 128) with split-K forced on every
+    stage, the dual gate/up included: above 16 tokens all splits of a tile sum
+    a share of its token rows; outputs go through the staged row stores, with
+    a partial last 16-token chunk (m = 40, 100), a rank that leaves a scalar
+    tail at N (763), and the residual epilogue.  Matches the oracle, repeats
+    bitwise, and agrees with the unsplit run."""
+    from svdflash_b200 import _lib
+    from svdflash_b200.kernels import ops
+    lib = _lib.load()
+    h, r, i = 1024, 763, 3584
+    x, f = orc.make_inputs(140 + m, m, h, i, r)
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f])
+    xd = to_dev(x, cuda_device)
+    res = orc.bf16_round(np.random.default_rng(m).standard_normal((m, h), dtype=np.float32))
+    rd = to_dev(res, cuda_device)
+    ref = orc.svd_mlp(x, *f)
+    try:
+        y0 = ops.svd_mlp_packed(layer, xd, residual=rd)
+        for splits in (2, 3, 5):
+            for st in range(4):
+                assert lib.svdmlp_set_split_override(st, splits) == 0
+            y1 = ops.svd_mlp_packed(layer, xd, residual=rd)
+            y2 = ops.svd_mlp_packed(layer, xd, residual=rd)
+            torch.cuda.synchronize()
+            assert torch.equal(y1, y2), f"m={m} splits={splits}: runs differ"
+            assert_close(to_np(y1), res + ref, what=f"per-stage decode m={m} splits={splits}")
+            from helpers import assert_close_bf16_output
+            assert_close_bf16_output(to_np(y1), to_np(y0), what=f"split {splits} vs planner m={m}")
+    finally:
+        for st in range(4):
+            lib.svdmlp_set_split_override(st, 0)
+    ops.check_device_status(cuda_device)
+
+
 @pytest.mark.parametrize("m", [1, 5, 16, 17, 64])
 def test_whole_layer_decode_kernel(cuda_device, m):
     """The one-launch whole-layer decode kernel (forced up to M = 64, both token
