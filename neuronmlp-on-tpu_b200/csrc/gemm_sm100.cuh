@@ -5,6 +5,9 @@
 // Dual form (NB == 2): two accumulators per tile, C = silu(A.Bg^T) * (A2.Bu^T);
 // this is the fused low-rank gate/up operator's second stage (the SwiGLU
 // epilogue of kernels/reference.py:54-72 applied on fp32 accumulators).
+// Dual-store form (EPI_DUAL_STORE, NB == 2, shared A): C1 = A.B1^T and
+// C2 = A.B2^T, two output maps; the first stage X.[u_g|u_u] as one tile of
+// 2 x BN columns that reads its A tile once for both halves.
 //
 // Operands are bf16 or fp16 (both the same type in one MMA); the output is
 // bf16, fp16 or fp32.  The SVD layer keeps its rank-r and ff intermediates in
@@ -59,7 +62,7 @@
 
 namespace svdmlp {
 
-enum EpiKind : int { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESID = 2 };
+enum EpiKind : int { EPI_PLAIN = 0, EPI_SWIGLU = 1, EPI_RESID = 2, EPI_DUAL_STORE = 3 };
 enum OutKind : int { OUT_BF16 = 0, OUT_F16 = 1, OUT_F32 = 2 };
 
 // Error sites recorded in the device error word when a bounded wait expires.
@@ -120,7 +123,8 @@ struct GemmCfg {
   static_assert(B_ROWS % 8 == 0, "B half-tile must hold whole 8-row core-matrix groups");
   static_assert(!B_TILED || B_ROWS % 16 == 0, "tiled B loads whole 16-row groups");
   static_assert(NB == 1 || NB == 2, "one or two accumulators per tile");
-  static_assert(NB == 1 || EPI == EPI_SWIGLU, "dual GEMMs use the SwiGLU epilogue");
+  static_assert(NB == 1 || EPI == EPI_SWIGLU || EPI == EPI_DUAL_STORE, "dual GEMMs: SwiGLU or two outputs");
+  static_assert(EPI != EPI_DUAL_STORE || (NB == 2 && SHARED_A && CTAS == 2), "dual-store: shared A, CTA pairs");
   static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "four or eight epilogue warps");
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = B_ROWS * BK * 2;
@@ -305,7 +309,8 @@ template <class Cfg>
 __global__ void __launch_bounds__(Cfg::THREADS, 1)
     gemm_sm100_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_a2,
                       const __grid_constant__ CUtensorMap tm_b, const __grid_constant__ CUtensorMap tm_b2,
-                      const __grid_constant__ CUtensorMap tm_out, const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tm_out, const __grid_constant__ CUtensorMap tm_out2,
+                      const GemmParams p) {
   constexpr int STAGES = Cfg::STAGES;
   constexpr bool PAIR = Cfg::CTAS == 2;
   extern __shared__ uint8_t smem_raw[];
@@ -348,6 +353,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     prefetch_tensormap(&tm_b);
     if (Cfg::NB == 2) prefetch_tensormap(&tm_b2);
     prefetch_tensormap(&tm_out);
+    if (Cfg::EPI == EPI_DUAL_STORE) prefetch_tensormap(&tm_out2);
   }
   if (warp == Cfg::MMA_WARP) {
     if constexpr (PAIR) {
@@ -548,6 +554,8 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           }
           epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
           store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
+          if constexpr (Cfg::EPI == EPI_DUAL_STORE)
+            store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N);
         }
         if (p.pub != nullptr) {
           // Publish this CTA's rows of the tile: each warp's output boxes are

@@ -391,6 +391,17 @@ constexpr int kPlSt = SVDMLP_PLAIN_STAGES, kPlEw = SVDMLP_PLAIN_EPI_WARPS;
 
 // Prefill (M > 128): CTA pairs, 256-row tiles.
 //                          BN     NB shared STG    epilogue   fp16-in out       CTAs epi-warps
+// X.[u_g|u_u] at prefill as one dual-store tile: 256 x (2 x 160) per CTA pair,
+// the A tile read once for both halves (57.6 operand bytes per MMA cycle per
+// SM against 64 for 256 x 256) and 18 x 4 = 72 tiles for 74 pairs at 1024
+// tokens (256-wide tiles: 92, i.e. 1.24 waves).
+#ifndef SVDMLP_XUD_BN
+#define SVDMLP_XUD_BN 160
+#endif
+#ifndef SVDMLP_XUD_STAGES
+#define SVDMLP_XUD_STAGES 5
+#endif
+using CfgXUd    = GemmCfg<SVDMLP_XUD_BN, 2, true, SVDMLP_XUD_STAGES, EPI_DUAL_STORE, false, OUT_F16, 2, 8>;
 using CfgXU     = GemmCfg<kXuBn,   1, false, kPlSt, EPI_PLAIN,  false, OUT_F16,  2, kPlEw>;  // X.[u_g|u_u] -> XU
 using CfgGU     = GemmCfg<kGuBn, 2, false, kGuSt, EPI_SWIGLU, true,  OUT_F16,  2, kGuEw>;  // XU.v -> H (internal)
 using CfgGUbf   = GemmCfg<kGuBn, 2, false, kGuSt, EPI_SWIGLU, true,  OUT_BF16, 2, kGuEw>;  // XU.v -> H (to caller)
@@ -573,7 +584,7 @@ static int carve(const svdmlp_layout* L, int M, void* ws, int64_t ws_bytes, Work
 // ------------------------------------------------------------------ launches
 template <class Cfg>
 static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& b, const CUtensorMap& b2,
-                       const CUtensorMap& out, int M, int N, int K, int stage, const Workspace& w,
+                       const CUtensorMap& out, const CUtensorMap& out2, int M, int N, int K, int stage, const Workspace& w,
                        const bf16* residual, int64_t ld_res, cudaStream_t stream) {
   DeviceInfo* dev = nullptr;
   SVD_CHECK(device_info(&dev));
@@ -646,7 +657,7 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
     }
   }
   if (tl) SVD_CUDA(cudaEventRecord(tl->start, stream));
-  SVD_CUDA(cudaLaunchKernelEx(&cfg, gemm_sm100_kernel<Cfg>, a, a2, b, b2, out, p));
+  SVD_CUDA(cudaLaunchKernelEx(&cfg, gemm_sm100_kernel<Cfg>, a, a2, b, b2, out, out2, p));
   if (tl) SVD_CUDA(cudaEventRecord(tl->stop, stream));
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return SVDMLP_OK;
@@ -912,8 +923,8 @@ struct Output {
 template <class Cfg>
 static int gemm_cfg(const Operand& a, const Operand& a2, const Operand& b, const Operand& b2, const Output& o, int M,
                     int N, int K, int stage, const Workspace& w, const void* residual, int64_t ld_res,
-                    cudaStream_t s) {
-  CUtensorMap ma, ma2, mb, mb2, mo;
+                    cudaStream_t s, const Output* o2 = nullptr) {
+  CUtensorMap ma, ma2, mb, mb2, mo, mo2;
   SVD_CHECK(operand_map(&ma, a.ptr, a.f16, a.k, a.rows, a.ld, Cfg::BM));
   SVD_CHECK(operand_map(&ma2, a2.ptr, a2.f16, a2.k, a2.rows, a2.ld, Cfg::BM));
   if constexpr (Cfg::B_TILED) {
@@ -924,7 +935,10 @@ static int gemm_cfg(const Operand& a, const Operand& a2, const Operand& b, const
     SVD_CHECK(operand_map(&mb2, b2.ptr, b2.f16, b2.k, b2.rows, b2.ld, Cfg::B_ROWS));
   }
   SVD_CHECK(output_map<Cfg>(&mo, o.ptr, o.n, o.rows, o.ld));
-  return launch_gemm<Cfg>(ma, ma2, mb, mb2, mo, M, N, K, stage, w, static_cast<const bf16*>(residual), ld_res, s);
+  if (o2) SVD_CHECK(output_map<Cfg>(&mo2, o2->ptr, o2->n, o2->rows, o2->ld));
+  else mo2 = mo;
+  return launch_gemm<Cfg>(ma, ma2, mb, mb2, mo, mo2, M, N, K, stage, w, static_cast<const bf16*>(residual), ld_res,
+                          s);
 }
 
 // Runs one GEMM stage with the CTA-pair config for prefill-sized M and the
@@ -977,6 +991,15 @@ static int run_xu(const svdmlp_layout* L, const uint8_t* packed, const void* x, 
                   const Workspace& w, cudaStream_t s) {
   const int64_t n1 = 2LL * L->rp_gu;
   const Operand xa{x, false, L->d, M, ldx};
+  if (M >= kPairMinM) {
+    // the two halves of the packed w1 (rp_gu is a whole number of 16-row groups)
+    const uint8_t* w1 = packed + L->off_w1;
+    const Operand wg{w1, false, L->d, L->rp_gu, L->ld_d};
+    const Operand wu{w1 + tiled_bytes(L->rp_gu, L->d), false, L->d, L->rp_gu, L->ld_d};
+    const Output og{w.xu, L->rp_gu, M, n1};
+    const Output ou{w.xu + L->rp_gu, L->rp_gu, M, n1};
+    return gemm_cfg<CfgXUd>(xa, xa, wg, wu, og, M, L->rp_gu, L->d, ST_XU, w, nullptr, 0, s, &ou);
+  }
   const Operand w1{packed + L->off_w1, false, L->d, n1, L->ld_d};
   return gemm_stage_dec<CfgXU, PickXU>(xa, xa, w1, w1, Output{w.xu, n1, M, n1}, M, static_cast<int>(n1), L->d,
                                        ST_XU, w, s);
@@ -1421,7 +1444,7 @@ int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, in
     // Prefill: the four stages as a chain (gemm_sm100.cuh), each stage
     // starting on the M-tile groups its predecessor has completed.
     int* base = w.counters + kChainOffsetInts;
-    const int nt_xu = static_cast<int>(cdiv(2LL * L->rp_gu, CfgXU::BN));
+    const int nt_xu = static_cast<int>(cdiv(L->rp_gu, CfgXUd::BN));
     const int nt_gu = static_cast<int>(cdiv(L->ff, CfgGU::BN));
     const int nt_du = static_cast<int>(cdiv(L->r_d, CfgDU::BN));
     const int mg = static_cast<int>(cdiv(cdiv(M, 256), g_chain_groups));  // M-tiles per group
@@ -1716,9 +1739,11 @@ int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
   const bool dual = stage == ST_GATEUP || stage == ST_DENSE_GU;
   const int nb = dual ? 2 : 1;
   const int tok = M <= 16 ? 16 : M <= 64 ? 64 : 128;
-  const int pair_bn = dual ? CfgGU::BN : stage == ST_XU ? CfgXU::BN : stage == ST_DOWN_U ? CfgDU::BN
+  const int pair_bn = dual ? CfgGU::BN : stage == ST_XU ? CfgXUd::BN : stage == ST_DOWN_U ? CfgDU::BN
                     : stage == ST_DOWN_V || stage == ST_DENSE_D ? CfgDV::BN : CfgGemm::BN;
-  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, N, K, pair_bn, planning_sms())
+  // prefill X.[u_g|u_u] is a dual-store tile over the two halves of N
+  const int pair_n = stage == ST_XU ? (N + 1) / 2 : N;
+  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, pair_n, K, pair_bn, planning_sms())
                                 : plan_stream(M, tok, N, K, nb, (tok <= 64 ? 2 : 1) * planning_sms(),
                                               g_split_override[stage]);
   out6[0] = p.m_tiles;
