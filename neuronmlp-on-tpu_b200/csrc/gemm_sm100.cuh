@@ -51,11 +51,14 @@
 // earlier launch, so the chain cannot deadlock.  The last stage's last CTA
 // resets the counters.
 //
-// Split-K (one-CTA configurations only): every split writes an fp32 partial
-// tile (its valid rows) to the workspace and bumps a per-tile counter; the
-// split that arrives last sums all partials in split order (deterministic) and
-// runs the epilogue.  Nothing ever waits on another CTA, so split-K cannot
-// deadlock.  The last split resets the counter.
+// Split-K: every split writes an fp32 partial tile (its valid rows) to the
+// workspace and bumps a per-tile counter.  One-CTA tiles: the split that
+// arrives last sums all partials in split order (deterministic) and runs the
+// epilogue; nothing waits on another CTA.  CTA pairs (prefill H.u_down, whose
+// 48 tiles at 1024 tokens fill only 48 of 74 pairs): every split of a tile
+// waits, bounded, for all splits and sums its share of the 32-column chunks,
+// in split order.  Units are ordered splits-fastest, so the lowest unfinished
+// tile always has all its splits running or done, and the waits end.
 #pragma once
 
 #include "ptx.cuh"
@@ -160,14 +163,17 @@ struct UnitCoord {
 
 SVD_DEV UnitCoord decode_unit(const GemmParams& p, int u) {
   UnitCoord c;
-  const int group_units = p.m_group * p.n_tiles * p.splits;
-  const int g = u / group_units;
+  // splits fastest: the units of one tile are consecutive, so the lowest
+  // unfinished tile always has every split running or done (the pair split-K
+  // fix-up waits for all splits of its tile).
+  c.ks = u % p.splits;
+  const int v = u / p.splits;
+  const int group_units = p.m_group * p.n_tiles;
+  const int g = v / group_units;
   const int gm = min(p.m_group, p.m_tiles - g * p.m_group);  // M-tiles in this (possibly last, short) group
-  const int in_g = u - g * group_units;
+  const int in_g = v - g * group_units;
   c.m_t = g * p.m_group + in_g % gm;
-  const int rest = in_g / gm;
-  c.ks = rest % p.splits;
-  c.n_t = rest / p.splits;
+  c.n_t = in_g / gm;
   c.kb0 = c.ks * p.kb_per_split;
   c.kb1 = min(c.kb0 + p.kb_per_split, p.k_blocks);
   c.tile = c.n_t * p.m_tiles + c.m_t;
@@ -529,7 +535,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       const int n0 = c.n_t * Cfg::BN;
       const int y_box = row_base + q * 32;
 
-      if (Cfg::CTAS == 2 || p.splits == 1) {
+      if (p.splits == 1) {
 #pragma unroll 1
         for (int ch = half; ch < NCH; ch += CH_STEP) {
           uint32_t rg[32];
@@ -568,9 +574,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           named_barrier_sync(3, EPI_THREADS);
           if (threadIdx.x == 0) red_add_release_gpu(&p.pub[c.m_t], 1);
         }
-      } else if constexpr (Cfg::CTAS == 1) {
-        // Pass 1: publish this split's fp32 partial tile (valid rows only).
-        float* slot = p.partials + static_cast<size_t>(c.tile * p.splits + c.ks) * Cfg::NB * (Cfg::BM * Cfg::BN);
+      } else {
+        // Split-K.  Each split writes its fp32 partial (this CTA's rows) and
+        // bumps the (tile, CTA) counter.  One CTA per tile: the split that
+        // arrives last sums all partials in split order and runs the
+        // epilogue.  CTA pairs: a 256 x BN partial tile is too much for one
+        // CTA to read, so every split waits (bounded) until all are in and
+        // sums the 32-column chunks ch = ks (mod splits); a second pass over
+        // the counter lets the last one to finish re-arm it.
+        const int ctile = c.tile * Cfg::CTAS + static_cast<int>(rank);
+        const size_t tile_elems = static_cast<size_t>(Cfg::NB) * (Cfg::BM * Cfg::BN);
+        float* slot = p.partials + static_cast<size_t>((c.tile * p.splits + c.ks) * Cfg::CTAS + rank) * tile_elems;
         const bool row_ok = grow < p.M;
 #pragma unroll 1
         for (int ch = half; ch < NCH; ch += CH_STEP) {
@@ -580,30 +594,39 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             tmem_ld_x32(tacc + br * Cfg::BSTRIDE + ch * 32, r);
             tmem_ld_wait();
             if (row_ok) {
+              // [chunk][float4 j][128 rows]: a warp's 32 rows of one float4
+              // column are 512 contiguous bytes
               float4* dst = reinterpret_cast<float4*>(slot + static_cast<size_t>(br) * (Cfg::BM * Cfg::BN) +
-                                                      ch * (Cfg::BM * 32) + row_in_tile * 32);
+                                                      ch * (Cfg::BM * 32)) + row_in_tile;
 #pragma unroll
               for (int j = 0; j < 8; ++j)
-                __stcg(dst + j, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                                            __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
+                __stcg(dst + j * Cfg::BM, make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                                                      __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3])));
             }
           }
         }
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&acc_empty[b]);  // TMEM no longer needed for this unit
+        if (lane == 0) {  // TMEM no longer needed for this unit
+          if constexpr (PAIR) mbar_arrive_cluster(acc_empty_leader0 + 8u * b);
+          else mbar_arrive(&acc_empty[b]);
+        }
         __threadfence();
         named_barrier_sync(1, EPI_THREADS);
         if (threadIdx.x == 0) {
-          const int old = atomicAdd(&p.counters[c.tile], 1);
-          *fix_flag = (old == p.splits - 1) ? 1 : 0;
+          const int old = atomicAdd(&p.counters[ctile], 1);
+          int go = PAIR ? 1 : (old == p.splits - 1 ? 1 : 0);
+          if (PAIR && !wait_counter_geq(&p.counters[ctile], p.splits, ctx, SITE_DEPENDENCY)) go = 0;
+          *fix_flag = go;
         }
         named_barrier_sync(1, EPI_THREADS);
         if (*fix_flag) {
           __threadfence();
-          const float* base = p.partials + static_cast<size_t>(c.tile * p.splits) * Cfg::NB * (Cfg::BM * Cfg::BN);
+          const float* base = p.partials + static_cast<size_t>(c.tile * p.splits * Cfg::CTAS + rank) * tile_elems;
+          const size_t split_stride = static_cast<size_t>(Cfg::CTAS) * tile_elems;
 #pragma unroll 1
           for (int ch = half; ch < NCH; ch += CH_STEP) {
+            if (PAIR && ch % p.splits != c.ks) continue;  // the same for every lane of the warp
             float v[32], w[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -615,18 +638,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
               for (int s = 0; s < p.splits; s += 2) {
                 // two splits' loads in flight per step; the sum order is the split order
                 const bool two = s + 1 < p.splits;
-                const float* src0 = base + static_cast<size_t>(s) * Cfg::NB * (Cfg::BM * Cfg::BN) +
-                                    ch * (Cfg::BM * 32) + row_in_tile * 32;
-                const float* src1 = src0 + static_cast<size_t>(Cfg::NB) * (Cfg::BM * Cfg::BN);
+                const float* src0 = base + static_cast<size_t>(s) * split_stride + ch * (Cfg::BM * 32);
+                const float* src1 = src0 + split_stride;
 #pragma unroll
                 for (int br = 0; br < Cfg::NB; ++br) {
-                  const float4* s0 = reinterpret_cast<const float4*>(src0 + br * (Cfg::BM * Cfg::BN));
-                  const float4* s1 = reinterpret_cast<const float4*>(src1 + br * (Cfg::BM * Cfg::BN));
+                  const float4* s0 = reinterpret_cast<const float4*>(src0 + br * (Cfg::BM * Cfg::BN)) + row_in_tile;
+                  const float4* s1 = reinterpret_cast<const float4*>(src1 + br * (Cfg::BM * Cfg::BN)) + row_in_tile;
                   float4 t0[8], t1[8];
 #pragma unroll
                   for (int j = 0; j < 8; ++j) {
-                    t0[j] = __ldcg(s0 + j);
-                    t1[j] = two ? __ldcg(s1 + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    t0[j] = __ldcg(s0 + j * Cfg::BM);
+                    t1[j] = two ? __ldcg(s1 + j * Cfg::BM) : make_float4(0.f, 0.f, 0.f, 0.f);
                   }
                   if (br == 0) add_partials(v, t0, t1);
                   else add_partials(w, t0, t1);
@@ -635,9 +657,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             }
             epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
             store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
+            if constexpr (Cfg::EPI == EPI_DUAL_STORE)
+              store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N);
           }
-          named_barrier_sync(1, EPI_THREADS);
-          if (threadIdx.x == 0) p.counters[c.tile] = 0;
+        }
+        named_barrier_sync(1, EPI_THREADS);
+        if (threadIdx.x == 0) {
+          if constexpr (!PAIR) {
+            if (*fix_flag) p.counters[ctile] = 0;
+          } else {
+            const int old = atomicAdd(&p.counters[ctile], 1);
+            if (old == 2 * p.splits - 1) p.counters[ctile] = 0;
+          }
         }
       }
       ++acc_it;

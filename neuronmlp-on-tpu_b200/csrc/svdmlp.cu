@@ -226,21 +226,48 @@ static Plan plan_gemm(int M, int N, int K, int BN, int NB, int sms, int forced_s
 
 // CTA-pair plans (prefill-sized M): 256-row tiles, no split-K, one cluster of
 // two CTAs per pair of SMs.
-static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms) {
+// CTA-pair plans (prefill).  Split-K over the pairs when it fills more of the
+// waves (tiles x splits over sms/2 pairs) than the extra fix-up costs: each
+// split writes an fp32 partial of its 256 x BN tile, and once all splits are
+// in, every split sums a share of the tile's 32-column chunks (modelled as ~10
+// k-blocks of work).  Plain (one-accumulator) tiles only, and only while the
+// partials stay within kPairPartialBudget.
+static constexpr int64_t kPairPartialBudget = 48ll << 20;
+static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms, bool allow_split = false, int forced_splits = 0) {
   Plan p{};
   p.m_tiles = static_cast<int>(cdiv(M, 256));
   p.n_tiles = static_cast<int>(cdiv(N, BN));
   p.k_blocks = static_cast<int>(cdiv(K, 64));
-  p.splits = 1;
-  p.kb_per_split = p.k_blocks;
-  p.units = p.m_tiles * p.n_tiles;
-  p.grid = 2 * std::min(p.units, sms / 2);
+  const int pairs = std::max(1, sms / 2);
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles;
+  int best_s = 1;
+  if (allow_split) {
+    if (forced_splits > 0) {
+      best_s = std::min(forced_splits, p.k_blocks);
+    } else {
+      double best = 1e30;
+      for (int s = 1; s <= 4; ++s) {
+        const int kbs = static_cast<int>(cdiv(p.k_blocks, s));
+        if (s > 1 && (kbs < 8 || tiles * s * 2 * 128 * BN * 4 > kPairPartialBudget)) break;
+        const double cost = static_cast<double>(cdiv(tiles * s, pairs)) * kbs + (s > 1 ? 10.0 : 0.0);
+        if (cost < best * 0.95) {
+          best = cost;
+          best_s = s;
+        }
+      }
+    }
+  }
+  p.kb_per_split = static_cast<int>(cdiv(p.k_blocks, best_s));
+  p.splits = static_cast<int>(cdiv(p.k_blocks, p.kb_per_split));
+  p.units = static_cast<int>(tiles) * p.splits;
+  p.grid = 2 * std::min(p.units, pairs);
   return p;
 }
 
 template <class Cfg>
 static Plan plan_for(int M, int N, int K, int sms, int forced_splits) {
-  if constexpr (Cfg::CTAS == 2) return plan_gemm_pair(M, N, K, Cfg::BN, sms);
+  if constexpr (Cfg::CTAS == 2)
+    return plan_gemm_pair(M, N, K, Cfg::BN, sms, Cfg::NB == 1, forced_splits);
   else return plan_gemm(M, N, K, Cfg::BN, Cfg::NB, sms, forced_splits);
 }
 
@@ -345,9 +372,9 @@ static int64_t dec_partial_bytes(const Plan& p) {
 }
 
 // Bytes of split-K partials a plan needs (NB accumulators of BM x BN fp32).
-static int64_t partial_bytes(const Plan& p, int BN, int NB) {
+static int64_t partial_bytes(const Plan& p, int BN, int NB, int ctas = 1) {
   if (p.splits <= 1) return 0;
-  return static_cast<int64_t>(p.units) * NB * 128 * BN * 4;
+  return static_cast<int64_t>(p.units) * ctas * NB * 128 * BN * 4;
 }
 
 // ------------------------------------------------------------ kernel configs
@@ -488,7 +515,7 @@ static int64_t counters_bytes(const svdmlp_layout*, int) { return kCounterBytes;
 template <class Cfg>
 static int64_t stage_partials(int M, int N, int K, int sms, int stage) {
   const Plan p = plan_for<Cfg>(M, N, K, sms, g_split_override[stage]);
-  return Cfg::CTAS == 1 ? partial_bytes(p, Cfg::BN, Cfg::NB) : 0;
+  return partial_bytes(p, Cfg::BN, Cfg::NB, Cfg::CTAS);
 }
 
 template <class Set>
@@ -509,11 +536,23 @@ static int64_t dec_set_partials(const svdmlp_layout* L, int M, int sms) {
   return b;
 }
 
-// Largest split-K partial buffer any M <= max_m can ask for (split-K runs
-// only in the one-CTA and decode kernels, i.e. for M <= 128).
+// Largest split-K partial buffer any M <= max_m can ask for: the one-CTA and
+// decode kernels (M <= 128) and the CTA-pair plain GEMMs (M >= 129; their
+// partials are capped at kPairPartialBudget), evaluated on every 256-row step.
 static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
   const int M = std::min(max_m, kPairMinM - 1);
   int64_t best = 0;
+  for (int mp = kPairMinM; mp <= max_m && best < kPairPartialBudget; mp = mp < 256 ? 256 : mp + 256) {
+    if (L->kind == SVDMLP_KIND_SVD) {
+      if (L->r_d > 0) {
+        best = std::max(best, stage_partials<CfgDU>(mp, L->r_d, L->ff, sms, ST_DOWN_U));
+        best = std::max(best, stage_partials<CfgDUf32>(mp, L->r_d, L->ff, sms, ST_DOWN_U));
+        best = std::max(best, stage_partials<CfgDV>(mp, L->d, L->r_d, sms, ST_DOWN_V));
+      }
+    } else {
+      best = std::max(best, stage_partials<CfgDV>(mp, L->d, L->ff, sms, ST_DENSE_D));
+    }
+  }
   if (L->kind == SVDMLP_KIND_SVD) {
     if (L->r_gu > 0) {
       best = std::max(best, stage_partials<CfgXU1>(M, 2 * L->rp_gu, L->d, sms, ST_XU));
@@ -603,7 +642,8 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
     }
   }
   Plan pl = plan_for<Cfg>(M, N, K, dev->sms, g_split_override[stage]);
-  if (partial_bytes(pl, Cfg::BN, Cfg::NB) > w.partial_cap && w.unsplit_if_short)
+  if ((partial_bytes(pl, Cfg::BN, Cfg::NB, Cfg::CTAS) > w.partial_cap && w.unsplit_if_short) ||
+      (w.chain && pl.splits > 1))  // chained stages publish whole tiles: unsplit
     pl = plan_for<Cfg>(M, N, K, dev->sms, 1);
   GemmParams p{};
   p.M = M;
@@ -632,7 +672,7 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
     p.reset = w.chain->reset;
     p.exit_count = w.chain->exit_count;
   }
-  if (partial_bytes(pl, Cfg::BN, Cfg::NB) > w.partial_cap) return SVDMLP_ERR_WORKSPACE;
+  if (partial_bytes(pl, Cfg::BN, Cfg::NB, Cfg::CTAS) > w.partial_cap) return SVDMLP_ERR_WORKSPACE;
 
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
@@ -1552,9 +1592,9 @@ int svdmlp_down_finish(const svdmlp_layout* L, const void* packed, const float* 
 int64_t svdmlp_gemm_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return SVDMLP_ERR_INVALID_VALUE;
   const int sms = planning_sms();
-  const Plan pl = M >= kPairMinM ? plan_for<CfgGemm>(M, N, K, sms, 0)
+  const Plan pl = M >= kPairMinM ? plan_for<CfgGemm>(M, N, K, sms, g_split_override[ST_GEMM])
                                  : plan_for<CfgGemm1>(M, N, K, sms, g_split_override[ST_GEMM]);
-  const int64_t part = M >= kPairMinM ? 0 : partial_bytes(pl, CfgGemm1::BN, 1);
+  const int64_t part = M >= kPairMinM ? partial_bytes(pl, CfgGemm::BN, 1, 2) : partial_bytes(pl, CfgGemm1::BN, 1);
   return kCtlBytes + kCounterBytes + round_up(part, 256);
 }
 
@@ -1743,7 +1783,8 @@ int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
                     : stage == ST_DOWN_V || stage == ST_DENSE_D ? CfgDV::BN : CfgGemm::BN;
   // prefill X.[u_g|u_u] is a dual-store tile over the two halves of N
   const int pair_n = stage == ST_XU ? (N + 1) / 2 : N;
-  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, pair_n, K, pair_bn, planning_sms())
+  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, pair_n, K, pair_bn, planning_sms(), !dual && stage != ST_XU,
+                                                g_split_override[stage])
                                 : plan_stream(M, tok, N, K, nb, (tok <= 64 ? 2 : 1) * planning_sms(),
                                               g_split_override[stage]);
   out6[0] = p.m_tiles;

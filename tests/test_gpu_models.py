@@ -189,10 +189,11 @@ def test_whole_layer_decode_kernel(cuda_device, m):
 @pytest.mark.parametrize("m", [129, 300, 700])
 def test_prefill_chain_matches_unchained(cuda_device, m):
     """Prefill layers run their four GEMMs as a chain (per-M-tile counters in
-    place of whole-launch waits, M-tile groups in the unit order).  The tiles
-    and their accumulation order are the same as the unchained path, so the
-    outputs are bit-identical; repeated calls re-arm the counters; partial
-    and odd M-tile counts and the residual epilogue are covered."""
+    place of whole-launch waits, M-tile groups in the unit order).  Chained
+    stages are unsplit; with split-K turned off on the unchained side too the
+    tiles and their accumulation order are the same, so the outputs are
+    bit-identical; repeated calls re-arm the counters; partial and odd M-tile
+    counts and the residual epilogue are covered."""
     from svdflash_b200 import _lib
     from svdflash_b200.kernels import ops
     lib = _lib.load()
@@ -203,6 +204,8 @@ def test_prefill_chain_matches_unchained(cuda_device, m):
     res = orc.bf16_round(np.random.default_rng(m).standard_normal((m, h), dtype=np.float32))
     rd = to_dev(res, cuda_device)
     try:
+        for st in range(4):
+            assert lib.svdmlp_set_split_override(st, 1) == 0
         assert lib.svdmlp_set_prefill_chain(2) == 0
         ys = [ops.svd_mlp_packed(layer, xd) for _ in range(3)]
         yr = ops.svd_mlp_packed(layer, xd, residual=rd)
@@ -213,6 +216,8 @@ def test_prefill_chain_matches_unchained(cuda_device, m):
         y0r = ops.svd_mlp_packed(layer, xd, residual=rd)
     finally:
         lib.svdmlp_set_prefill_chain(0)
+        for st in range(4):
+            lib.svdmlp_set_split_override(st, 0)
     torch.cuda.synchronize()
     ops.check_device_status(cuda_device)
     for k, y in enumerate(ys):
