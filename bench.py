@@ -8,7 +8,7 @@ A step is one full layer forward (gate/up + down: 4 GEMM launches).
 
 N>1 (torchrun, one rank per GPU): the same layer tensor-parallel over ff
 (strong scaling): v_gate/v_up column-sharded, u_down row-sharded, one NCCL
-all-reduce of the fp32 [M, r] partial per step.
+all-reduce of the fp16 [M, r] partial per step.
 
 --impl reference: the reference's CPU path (the NumPy oracle restatement of
 kernels/reference.py) on the host cores, rank 0 only.
@@ -523,7 +523,7 @@ def main():
     # minimum HBM bytes per launch: the stage's weights once + its activations in and out
     stage_bytes = {"xu": 2.0 * 2 * rp * d + 2.0 * m * d + 2.0 * m * 2 * rp,
                    "gate_up": 2.0 * 2 * ff_loc * rp + 2.0 * m * 2 * rp + 2.0 * m * ff_loc,
-                   "down_u": 2.0 * rp * ff_loc + 2.0 * m * ff_loc + (4.0 if world > 1 else 2.0) * m * rp,
+                   "down_u": 2.0 * rp * ff_loc + 2.0 * m * ff_loc + 2.0 * m * rp,
                    "down_v": 2.0 * d * rp + 2.0 * m * rp + 2.0 * m * d}
     stage_bytes["layer_decode"] = sum(stage_bytes.values())
 
@@ -574,6 +574,7 @@ def main():
         "data": "synthetic",
         "config": {"workload": args.workload, "d": d, "ff": ff, "r": r, "tokens": m, "ratio": wl["ratio"],
                    "parallelism": f"tp-ff{world}" if world > 1 else "single-gpu",
+                   "allreduce": "fp16 [M, r] partial, NCCL" if world > 1 else None,
                    "l2": f"inputs larger than L2: {weight_bytes / 1e6:.0f} MB of factors streamed per step"},
         "us_per_layer": ms_per_step * 1e3,
         "tflops": flops_layer / (ms_per_step * 1e-3) / 1e12,

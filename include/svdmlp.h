@@ -196,6 +196,19 @@ int svdmlp_down_finish(const svdmlp_layout* layout, const void* packed, const fl
                        int64_t ld_partial, int m, void* y, int64_t ld_y, const void* residual,
                        int64_t ld_residual, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The same exchange with an fp16 partial (half the all-reduce bytes; the
+ * sum is the fp16 T that the single-GPU layer also rounds to): down_u writes
+ * fp16 partial[M, r_d] directly, and svdmlp_down_finish_f16 reads the summed
+ * fp16 buffer as the A operand of . v_down.  partial: 16-byte aligned,
+ * ld_partial a multiple of 8, else SVDMLP_ERR_ALIGNMENT.  The caller reduces
+ * it with an fp16 sum (ncclHalf). */
+int svdmlp_forward_partial_f16(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x,
+                               int m, void* partial, int64_t ld_partial, void* workspace,
+                               int64_t workspace_bytes, void* stream);
+int svdmlp_down_finish_f16(const svdmlp_layout* layout, const void* packed, const void* partial,
+                           int64_t ld_partial, int m, void* y, int64_t ld_y, const void* residual,
+                           int64_t ld_residual, void* workspace, int64_t workspace_bytes, void* stream);
+
 /*
  * XUV down operator, y[M, d] = (h . u_down) . v_down, that allocates nothing
  * and takes no workspace.  It has no counterpart in the reference.

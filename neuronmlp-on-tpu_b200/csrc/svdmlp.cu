@@ -1066,10 +1066,17 @@ static int run_gate_up(const svdmlp_layout* L, const uint8_t* packed, const void
 
 // Stage 3: H . u_down -> T (fp16, workspace) or an fp32 partial.  `h_f16`
 // says whether H is fp16 (it must then match an fp16 ud) or bf16 (bf16 ud).
+// T = H . u_down into the workspace, or into a caller's fp32 (`partial`) or
+// fp16 (`partial16`) buffer for the tensor-parallel all-reduce.
 static int run_down_u(const svdmlp_layout* L, const uint8_t* packed, const void* h, int64_t ldh, bool h_f16, int M,
-                      float* partial, int64_t ldp, const Workspace& w, cudaStream_t s) {
+                      float* partial, int64_t ldp, const Workspace& w, cudaStream_t s, void* partial16 = nullptr) {
   const Operand ha{h, h_f16, L->ff, M, ldh};
   const Operand ud{packed + L->off_ud, h_f16, L->ff, L->r_d, L->ld_ff};
+  if (partial16) {
+    if (!h_f16) return SVDMLP_ERR_DTYPE;
+    return gemm_stage_dec<CfgDU, PickDU>(ha, ha, ud, ud, Output{partial16, L->r_d, M, ldp}, M, L->r_d, L->ff,
+                                         ST_DOWN_U, w, s);
+  }
   if (partial) {
     if (!h_f16) return SVDMLP_ERR_DTYPE;
     return gemm_stage_dec<CfgDUf32, PickDUf32>(ha, ha, ud, ud, Output{partial, L->r_d, M, ldp}, M, L->r_d, L->ff,
@@ -1081,9 +1088,11 @@ static int run_down_u(const svdmlp_layout* L, const uint8_t* packed, const void*
 }
 
 // Stage 4: T . v_down (+ residual) -> y (bf16)
+// y = T . v_down (+ residual), T the workspace's fp16 T or a caller's fp16 buffer.
 static int run_down_v(const svdmlp_layout* L, const uint8_t* packed, int M, void* y, int64_t ldy,
-                      const void* residual, int64_t ld_res, const Workspace& w, cudaStream_t s) {
-  const Operand ta{w.t, true, L->r_d, M, L->rp_d};
+                      const void* residual, int64_t ld_res, const Workspace& w, cudaStream_t s,
+                      const void* t = nullptr, int64_t ldt = 0) {
+  const Operand ta{t ? t : w.t, true, L->r_d, M, t ? ldt : L->rp_d};
   const Operand vd{packed + L->off_vd, true, L->r_d, L->d, L->rp_d};
   const Output yo{y, L->d, M, ldy};
   if (residual)
@@ -1568,6 +1577,43 @@ int svdmlp_down_partial(const svdmlp_layout* L, const void* packed, const void* 
   int64_t ldha;
   SVD_CHECK(stage_h(L, h, ldh, M, w, &ha, &ldha, s));
   return run_down_u(L, static_cast<const uint8_t*>(packed), ha, ldha, true, M, partial, ldp, w, s);
+}
+
+int svdmlp_forward_partial_f16(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M,
+                               void* partial, int64_t ldp, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || L->r_d <= 0 || !packed || !x || !partial || M <= 0 ||
+      ldx < L->d || ldp < L->r_d)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if (!aligned16(partial, ldp)) return SVDMLP_ERR_ALIGNMENT;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  const void* xa;
+  int64_t ldxa;
+  SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
+  SVD_CHECK(run_gate_up(L, P, xa, ldxa, M, w.h, L->ld_ff, false, w, s));
+  return run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, ldp, w, s, partial);
+}
+
+int svdmlp_down_finish_f16(const svdmlp_layout* L, const void* packed, const void* partial, int64_t ldp, int M,
+                           void* y, int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes,
+                           void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_d <= 0 || !packed || !partial || !y || M <= 0 || ldp < L->r_d ||
+      ldy < L->d || (residual && ld_res < L->d))
+    return SVDMLP_ERR_INVALID_VALUE;
+  if (!aligned16(partial, ldp)) return SVDMLP_ERR_ALIGNMENT;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
+  const void* res = nullptr;
+  int64_t ldr = 0;
+  if (residual) SVD_CHECK(stage_in(residual, ld_res, M, L->d, w.xs, L->ld_d, &res, &ldr, s));
+  SVD_CHECK(run_down_v(L, static_cast<const uint8_t*>(packed), M, yt.ptr, yt.ld, res, ldr, w, s, partial, ldp));
+  return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
 }
 
 int svdmlp_down_finish(const svdmlp_layout* L, const void* packed, const float* partial, int64_t ldp, int M,

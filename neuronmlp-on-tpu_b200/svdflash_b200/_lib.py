@@ -74,6 +74,8 @@ SIGNATURES = {
     "svdmlp_down_partial": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_forward_partial": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_down_finish": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
+    "svdmlp_forward_partial_f16": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
+    "svdmlp_down_finish_f16": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
     "svdmlp_xuv_noalloc": (c_int, [LP, V, V, I64, c_int, V, I64, V]),
     "svdmlp_gemm": (c_int, [V, I64, V, I64, V, I64, c_int, c_int, c_int, V, I64, V]),
     "svdmlp_gemm_workspace_bytes": (c_int64, [c_int, c_int, c_int]),

@@ -366,26 +366,35 @@ def xuv_packed(layer: PackedLayer, h: torch.Tensor) -> torch.Tensor:
     return y
 
 
-def forward_partial_packed(layer: PackedLayer, x: torch.Tensor, partial: Optional[torch.Tensor] = None):
-    """Stages 1-3 of an ff-shard: fp32 [M, r_d] partial for the all-reduce."""
+def forward_partial_packed(layer: PackedLayer, x: torch.Tensor, partial: Optional[torch.Tensor] = None,
+                           dtype: torch.dtype = torch.float32):
+    """Stages 1-3 of an ff-shard: the [M, r_d] partial for the all-reduce, fp32
+    or fp16 (the dtype of `partial` when given, else `dtype`)."""
     xb = _prep_x(x, layer.d)
     m = xb.shape[0]
     if partial is None:
-        partial = torch.empty((m, layer.r_d + (-layer.r_d) % 4), dtype=torch.float32, device=xb.device)[:, :layer.r_d]
+        align = 4 if dtype == torch.float32 else 8
+        partial = torch.empty((m, layer.r_d + (-layer.r_d) % align), dtype=dtype, device=xb.device)[:, :layer.r_d]
+    if partial.dtype not in (torch.float32, torch.float16):
+        raise TypeError("the partial must be fp32 or fp16 (supported dtypes)")
+    fn = _lib.load().svdmlp_forward_partial if partial.dtype == torch.float32 else _lib.load().svdmlp_forward_partial_f16
     ws = layer.workspace(m)
-    _lib.check(_lib.load().svdmlp_forward_partial(
-        ctypes.byref(layer.layout), layer.packed.data_ptr(), xb.data_ptr(), _ld(xb), m, partial.data_ptr(),
-        partial.stride(0), ws.ptr, ws.nbytes, _stream(xb.device)), "forward_partial")
+    _lib.check(fn(ctypes.byref(layer.layout), layer.packed.data_ptr(), xb.data_ptr(), _ld(xb), m, partial.data_ptr(),
+                  partial.stride(0), ws.ptr, ws.nbytes, _stream(xb.device)), "forward_partial")
     return partial
 
 
 def down_finish_packed(layer: PackedLayer, partial: torch.Tensor, residual: Optional[torch.Tensor] = None,
                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = sum(partials) . v_down (+ residual) from the all-reduced fp32 or fp16 partial."""
     m = partial.shape[0]
+    if partial.dtype not in (torch.float32, torch.float16):
+        raise TypeError("the partial must be fp32 or fp16 (supported dtypes)")
     y = out if out is not None else _out(m, layer.d, partial.device)
     ws = layer.workspace(m)
     res = None if residual is None else _bf16(residual)
-    _lib.check(_lib.load().svdmlp_down_finish(
+    fn = _lib.load().svdmlp_down_finish if partial.dtype == torch.float32 else _lib.load().svdmlp_down_finish_f16
+    _lib.check(fn(
         ctypes.byref(layer.layout), layer.packed.data_ptr(), partial.data_ptr(), partial.stride(0), m,
         y.data_ptr(), _ld(y), _ptr(res), 0 if res is None else _ld(res), ws.ptr, ws.nbytes,
         _stream(partial.device)), "down_finish")

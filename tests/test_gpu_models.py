@@ -80,26 +80,33 @@ def test_tensor_parallel_single_rank(cuda_device):
     assert_close(to_np(y), orc.svd_mlp(x, *f), what="tp world=1")
 
 
-def test_tensor_parallel_shards_summed_on_one_gpu(cuda_device):
-    """Two ff-shards run on one GPU; their fp32 partials summed on the host side
-    of the exchange reproduce the full layer (the all-reduce's arithmetic)."""
+@pytest.mark.parametrize("world,dtype", [(2, "float32"), (2, "float16"), (8, "float16")])
+def test_tensor_parallel_shards_summed_on_one_gpu(cuda_device, world, dtype):
+    """`world` ff-shards run on one GPU; their partials (fp32, or fp16 summed
+    one rank after another in fp16, as a ring all-reduce of ncclHalf rounds)
+    reproduce the full layer through down_finish; each shard's partial
+    matches the oracle's shard arithmetic."""
     from svdflash_b200.kernels import ops
     from svdflash_b200.tp import TensorParallelSvdMlp
-    m, h, r, i = 64, 256, 100, 512
+    m, h, r, i = 128, 1024, 700, 3584
     x, f = orc.make_inputs(51, m, h, i, r)
     fd = [to_dev(a, cuda_device) for a in f]
     xd = to_dev(x, cuda_device)
+    td = getattr(torch, dtype)
     parts = []
-    shards = [TensorParallelSvdMlp(*fd, rank=p, world=2) for p in range(2)]
+    shards = [TensorParallelSvdMlp(*fd, rank=p, world=world, reduce_dtype=td) for p in range(world)]
     for sh in shards:
         buf = sh._partial_buffer(m, cuda_device).clone()
         ops.forward_partial_packed(sh.layer, xd, buf[:, :sh.r_d])
+        assert buf.dtype == td
         parts.append(buf)
-    total = parts[0] + parts[1]
+    total = parts[0].clone()
+    for p in parts[1:]:
+        total = total + p  # rounds to the partial's dtype after every rank
     y = ops.down_finish_packed(shards[0].layer, total[:, :r])
-    assert_close(to_np(y), orc.svd_mlp(x, *f), what="tp 2 shards on one gpu")
-    for p, sh in enumerate(shards):
-        want = orc.shard_partial(x, orc.shard_factors(f, p, 2))
+    assert_close(to_np(y), orc.svd_mlp(x, *f), what=f"tp {world} shards ({dtype}) on one gpu")
+    for p, sh in enumerate(shards[:2]):
+        want = orc.shard_partial(x, orc.shard_factors(f, p, world))
         got = to_np(parts[p][:, :r])
         assert orc.error_metrics(got, want)["rel_fro"] < 5e-3
 
