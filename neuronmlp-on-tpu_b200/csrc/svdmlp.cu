@@ -233,6 +233,10 @@ static Plan plan_gemm(int M, int N, int K, int BN, int NB, int sms, int forced_s
 // k-blocks of work).  Plain (one-accumulator) tiles only, and only while the
 // partials stay within kPairPartialBudget.
 static constexpr int64_t kPairPartialBudget = 48ll << 20;
+// L2 bytes one group of M-tiles' A rows may take (of 126 MB; the rest holds
+// the weight tiles in flight, outputs and partials).
+static constexpr int64_t kL2GroupBytes = 40ll << 20;
+static constexpr double kL2Bytes = 96.0 * (1 << 20);  // L2 a GEMM's A operand can count on keeping
 static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms, bool allow_split = false, int forced_splits = 0) {
   Plan p{};
   p.m_tiles = static_cast<int>(cdiv(M, 256));
@@ -661,7 +665,22 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   p.timeout_ns = g_wait_limit_ns;
   p.residual = residual;
   p.ld_residual = ld_res;
+  // Unit raster, from an estimate of HBM traffic.  m-fastest (one group):
+  // the weights are read once, A once if it fits in L2, else once per span
+  // of N-tiles that one wave of pairs covers.  Grouped: M-tiles in groups
+  // whose A rows fit in kL2GroupBytes, A read once, the weights once per
+  // group.  Grouping pays for very long M (32 K tokens: ~10x less traffic).
   p.m_group = pl.m_tiles;
+  if constexpr (Cfg::CTAS == 2) {
+    const double a_tile = static_cast<double>(Cfg::TILE_M) * K * 2 * Cfg::NA;
+    const double a_total = a_tile * pl.m_tiles;
+    const double b_total = static_cast<double>(N) * K * 2 * Cfg::NB;
+    const double waves_n = std::max(1.0, (dev->sms / 2.0) / pl.m_tiles);  // N-tiles one wave spans
+    const double t0 = b_total + (a_total > kL2Bytes ? a_total * pl.n_tiles / waves_n : a_total);
+    const int g = static_cast<int>(std::max(1.0, std::min<double>(pl.m_tiles, kL2GroupBytes / a_tile)));
+    const double t1 = a_total + b_total * static_cast<double>(cdiv(pl.m_tiles, g));
+    if (g < pl.m_tiles && t1 < 0.7 * t0) p.m_group = g;
+  }
   if (w.chain) {
     // Chained stages are CTA-pair, unsplit plans by construction of the caller.
     if (Cfg::CTAS != 2 || pl.splits != 1 || pl.m_tiles > kChainStride) return SVDMLP_ERR_INVALID_VALUE;
