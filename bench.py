@@ -371,6 +371,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-reps", type=int, default=3)
+    ap.add_argument("--tp-mode", choices=("auto", "allreduce", "split"), default="auto",
+                    help="N>1: one all-reduce of the partial (default) or the all-gather split of the replicated stages")
     ap.add_argument("--sweep", choices=("decode", "shapes", "stack"), default=None,
                     help="print one JSON line per point of BASELINE configs 2, 5 or 3 instead of the bench line")
     args = ap.parse_args()
@@ -422,7 +424,7 @@ def main():
         def step(inp, out=y):
             return ops.svd_mlp_packed(layer, inp, out=out)
     else:
-        tp = TensorParallelSvdMlp(*factors, rank=rank, world=world)
+        tp = TensorParallelSvdMlp(*factors, rank=rank, world=world, mode=args.tp_mode)
         y = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
 
         def step(inp, out=y):
@@ -574,7 +576,8 @@ def main():
         "data": "synthetic",
         "config": {"workload": args.workload, "d": d, "ff": ff, "r": r, "tokens": m, "ratio": wl["ratio"],
                    "parallelism": f"tp-ff{world}" if world > 1 else "single-gpu",
-                   "allreduce": "fp16 [M, r] partial, NCCL" if world > 1 else None,
+                   "allreduce": ("split: all-gather XU, reduce-scatter fp16 partial, all-gather y"
+                                 if tp._use_split(m, d) else "fp16 [M, r] partial, NCCL") if world > 1 else None,
                    "l2": f"inputs larger than L2: {weight_bytes / 1e6:.0f} MB of factors streamed per step"},
         "us_per_layer": ms_per_step * 1e3,
         "tflops": flops_layer / (ms_per_step * 1e-3) / 1e12,

@@ -209,6 +209,21 @@ int svdmlp_down_finish_f16(const svdmlp_layout* layout, const void* packed, cons
                            int64_t ld_partial, int m, void* y, int64_t ld_y, const void* residual,
                            int64_t ld_residual, void* workspace, int64_t workspace_bytes, void* stream);
 
+/* The all-gather split of the replicated stages (the survey's "next" item:
+ * shard X . [u_g|u_u] over M, then all-gather).  Per rank of P:
+ *   svdmlp_xu_project on its M/P rows -> fp16 XU rows [M/P, 2*rp_gu];
+ *   all-gather XU over ranks (rows);
+ *   svdmlp_partial_from_xu_f16 on all M rows (this rank's ff shard) -> fp16
+ *     partial [M, r_d];
+ *   reduce-scatter the partial over ranks (rows, sum);
+ *   svdmlp_down_finish_f16 on its M/P rows; all-gather y over ranks.
+ * xu: 16-byte aligned, ld_xu >= 2*rp_gu and a multiple of 8. */
+int svdmlp_xu_project(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x, int m,
+                      void* xu, int64_t ld_xu, void* workspace, int64_t workspace_bytes, void* stream);
+int svdmlp_partial_from_xu_f16(const svdmlp_layout* layout, const void* packed, const void* xu, int64_t ld_xu,
+                               int m, void* partial, int64_t ld_partial, void* workspace,
+                               int64_t workspace_bytes, void* stream);
+
 /*
  * XUV down operator, y[M, d] = (h . u_down) . v_down, that allocates nothing
  * and takes no workspace.  It has no counterpart in the reference.

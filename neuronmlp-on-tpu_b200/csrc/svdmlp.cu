@@ -1047,29 +1047,33 @@ template <class S> using PickDVres = typename S::DVres;
 // caller-facing bf16 output instead of the internal fp16 H.
 // XU = X . [u_g|u_u]  (fp16, [M, 2 rp_gu])
 static int run_xu(const svdmlp_layout* L, const uint8_t* packed, const void* x, int64_t ldx, int M,
-                  const Workspace& w, cudaStream_t s) {
+                  const Workspace& w, cudaStream_t s, void* xu_out = nullptr, int64_t ld_xu = 0) {
   const int64_t n1 = 2LL * L->rp_gu;
   const Operand xa{x, false, L->d, M, ldx};
+  __half* xu = xu_out ? static_cast<__half*>(xu_out) : w.xu;  // the workspace's XU or a caller's buffer
+  const int64_t ldo = xu_out ? ld_xu : n1;
   if (M >= kPairMinM) {
     // the two halves of the packed w1 (rp_gu is a whole number of 16-row groups)
     const uint8_t* w1 = packed + L->off_w1;
     const Operand wg{w1, false, L->d, L->rp_gu, L->ld_d};
     const Operand wu{w1 + tiled_bytes(L->rp_gu, L->d), false, L->d, L->rp_gu, L->ld_d};
-    const Output og{w.xu, L->rp_gu, M, n1};
-    const Output ou{w.xu + L->rp_gu, L->rp_gu, M, n1};
+    const Output og{xu, L->rp_gu, M, ldo};
+    const Output ou{xu + L->rp_gu, L->rp_gu, M, ldo};
     return gemm_cfg<CfgXUd>(xa, xa, wg, wu, og, M, L->rp_gu, L->d, ST_XU, w, nullptr, 0, s, &ou);
   }
   const Operand w1{packed + L->off_w1, false, L->d, n1, L->ld_d};
-  return gemm_stage_dec<CfgXU, PickXU>(xa, xa, w1, w1, Output{w.xu, n1, M, n1}, M, static_cast<int>(n1), L->d,
+  return gemm_stage_dec<CfgXU, PickXU>(xa, xa, w1, w1, Output{xu, n1, M, ldo}, M, static_cast<int>(n1), L->d,
                                        ST_XU, w, s);
 }
 
 // H = silu(XU_g . v_g) * (XU_u . v_u)
 static int run_gu(const svdmlp_layout* L, const uint8_t* packed, int M, void* h, int64_t ldh, bool h_bf16,
-                  const Workspace& w, cudaStream_t s) {
+                  const Workspace& w, cudaStream_t s, const void* xu_in = nullptr, int64_t ld_xu = 0) {
   const int64_t n1 = 2LL * L->rp_gu;
-  const Operand ag{w.xu, true, L->r_gu, M, n1};
-  const Operand au{w.xu + L->rp_gu, true, L->r_gu, M, n1};
+  const __half* xu = xu_in ? static_cast<const __half*>(xu_in) : w.xu;
+  const int64_t ldi = xu_in ? ld_xu : n1;
+  const Operand ag{xu, true, L->r_gu, M, ldi};
+  const Operand au{xu + L->rp_gu, true, L->r_gu, M, ldi};
   const Operand bg{packed + L->off_vg, true, L->r_gu, L->ff, L->rp_gu};
   const Operand bu{packed + L->off_vu, true, L->r_gu, L->ff, L->rp_gu};
   const Output ho{h, L->ff, M, ldh};
@@ -1613,6 +1617,37 @@ int svdmlp_forward_partial_f16(const svdmlp_layout* L, const void* packed, const
   int64_t ldxa;
   SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
   SVD_CHECK(run_gate_up(L, P, xa, ldxa, M, w.h, L->ld_ff, false, w, s));
+  return run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, ldp, w, s, partial);
+}
+
+int svdmlp_xu_project(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* xu,
+                      int64_t ld_xu, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || !packed || !x || !xu || M <= 0 || ldx < L->d ||
+      ld_xu < 2LL * L->rp_gu)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if (!aligned16(xu, ld_xu)) return SVDMLP_ERR_ALIGNMENT;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const void* xa;
+  int64_t ldxa;
+  SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
+  return run_xu(L, static_cast<const uint8_t*>(packed), xa, ldxa, M, w, s, xu, ld_xu);
+}
+
+int svdmlp_partial_from_xu_f16(const svdmlp_layout* L, const void* packed, const void* xu, int64_t ld_xu, int M,
+                               void* partial, int64_t ldp, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || L->r_d <= 0 || !packed || !xu || !partial || M <= 0 ||
+      ld_xu < 2LL * L->rp_gu || ldp < L->r_d)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if (!aligned16(xu, ld_xu) || !aligned16(partial, ldp)) return SVDMLP_ERR_ALIGNMENT;
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  SVD_CHECK(run_gu(L, P, M, w.h, L->ld_ff, false, w, s, xu, ld_xu));
   return run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, ldp, w, s, partial);
 }
 

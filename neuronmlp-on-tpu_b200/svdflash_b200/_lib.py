@@ -76,6 +76,8 @@ SIGNATURES = {
     "svdmlp_down_finish": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
     "svdmlp_forward_partial_f16": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_down_finish_f16": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
+    "svdmlp_xu_project": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
+    "svdmlp_partial_from_xu_f16": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_xuv_noalloc": (c_int, [LP, V, V, I64, c_int, V, I64, V]),
     "svdmlp_gemm": (c_int, [V, I64, V, I64, V, I64, c_int, c_int, c_int, V, I64, V]),
     "svdmlp_gemm_workspace_bytes": (c_int64, [c_int, c_int, c_int]),

@@ -384,6 +384,35 @@ def forward_partial_packed(layer: PackedLayer, x: torch.Tensor, partial: Optiona
     return partial
 
 
+def xu_project_packed(layer: PackedLayer, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Stage 1 alone: XU = x . [u_g|u_u], fp16 [M, 2*rp_gu] (the layout stages 2-3 read)."""
+    xb = _prep_x(x, layer.d)
+    m = xb.shape[0]
+    n1 = 2 * layer.layout.rp_gu
+    xu = out if out is not None else torch.empty((m, n1), dtype=torch.float16, device=xb.device)
+    if xu.dtype != torch.float16 or xu.shape[1] < n1:
+        raise ValueError("xu must be fp16 [M, 2*rp_gu]")
+    ws = layer.workspace(m)
+    _lib.check(_lib.load().svdmlp_xu_project(
+        ctypes.byref(layer.layout), layer.packed.data_ptr(), xb.data_ptr(), _ld(xb), m, xu.data_ptr(), _ld(xu),
+        ws.ptr, ws.nbytes, _stream(xb.device)), "xu_project")
+    return xu
+
+
+def partial_from_xu_packed(layer: PackedLayer, xu: torch.Tensor, partial: Optional[torch.Tensor] = None):
+    """Stages 2-3 of an ff-shard from a given XU: fp16 [M, r_d] partial."""
+    m = xu.shape[0]
+    if partial is None:
+        partial = torch.empty((m, layer.r_d + (-layer.r_d) % 8), dtype=torch.float16, device=xu.device)[:, :layer.r_d]
+    if xu.dtype != torch.float16 or partial.dtype != torch.float16:
+        raise TypeError("xu and the partial must be fp16 (supported dtypes)")
+    ws = layer.workspace(m)
+    _lib.check(_lib.load().svdmlp_partial_from_xu_f16(
+        ctypes.byref(layer.layout), layer.packed.data_ptr(), xu.data_ptr(), _ld(xu), m, partial.data_ptr(),
+        partial.stride(0), ws.ptr, ws.nbytes, _stream(xu.device)), "partial_from_xu")
+    return partial
+
+
 def down_finish_packed(layer: PackedLayer, partial: torch.Tensor, residual: Optional[torch.Tensor] = None,
                        out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """y = sum(partials) . v_down (+ residual) from the all-reduced fp32 or fp16 partial."""

@@ -111,6 +111,37 @@ def test_tensor_parallel_shards_summed_on_one_gpu(cuda_device, world, dtype):
         assert orc.error_metrics(got, want)["rel_fro"] < 5e-3
 
 
+@pytest.mark.parametrize("world", [2, 8])
+def test_tensor_parallel_split_mode_on_one_gpu(cuda_device, world):
+    """The all-gather split of the replicated stages, `world` ranks emulated on
+    one GPU: X.[u_g|u_u] per row block (all-gathered), stages 2-3 per ff shard
+    on all rows, the fp16 partials summed rank after rank (reduce-scatter by
+    rows), .v_down (+ residual) per row block (all-gathered): the full layer."""
+    from svdflash_b200.kernels import ops
+    from svdflash_b200.tp import TensorParallelSvdMlp
+    m, h, r, i = 128, 1024, 700, 3584
+    x, f = orc.make_inputs(52, m, h, i, r)
+    res = orc.bf16_round(np.random.default_rng(53).standard_normal((m, h), dtype=np.float32))
+    fd = [to_dev(a, cuda_device) for a in f]
+    xd, rd = to_dev(x, cuda_device), to_dev(res, cuda_device)
+    shards = [TensorParallelSvdMlp(*fd, rank=p, world=world, mode="split") for p in range(world)]
+    rows = m // world
+    xu = torch.cat([ops.xu_project_packed(shards[p].layer, xd[p * rows:(p + 1) * rows]) for p in range(world)])
+    xu_full = ops.xu_project_packed(shards[0].layer, xd)
+    torch.cuda.synchronize()
+    assert torch.equal(xu, xu_full) or orc.error_metrics(to_np(xu), to_np(xu_full))["rel_fro"] < 1e-3
+    total = None
+    for sh in shards:
+        buf = sh._partial_buffer(m, cuda_device).clone()  # 16-byte rows (r padded to 8)
+        ops.partial_from_xu_packed(sh.layer, xu, buf[:, :r])
+        total = buf if total is None else total + buf
+    ys = [ops.down_finish_packed(shards[p].layer, total[p * rows:(p + 1) * rows, :r],
+                                 residual=rd[p * rows:(p + 1) * rows]) for p in range(world)]
+    y = torch.cat(ys)
+    assert_close(to_np(y), res + orc.svd_mlp(x, *f), what=f"tp split mode, {world} ranks on one gpu")
+    ops.check_device_status(cuda_device)
+
+
 def test_decode_sizes_split_k(cuda_device):
     """M <= 128 runs the one-CTA split-K kernels (config 2 regime, small dims)."""
     from svdflash_b200.kernels import ops
