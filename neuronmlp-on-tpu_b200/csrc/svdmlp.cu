@@ -230,14 +230,15 @@ static Plan plan_gemm(int M, int N, int K, int BN, int NB, int sms, int forced_s
 // waves (tiles x splits over sms/2 pairs) than the extra fix-up costs: each
 // split writes an fp32 partial of its 256 x BN tile, and once all splits are
 // in, every split sums a share of the tile's 32-column chunks (modelled as ~10
-// k-blocks of work).  Plain (one-accumulator) tiles only, and only while the
-// partials stay within kPairPartialBudget.
+// k-blocks of work), while the partials stay within kPairPartialBudget (not
+// for the dual-store X.[u_g|u_u] tile).
 static constexpr int64_t kPairPartialBudget = 48ll << 20;
 // L2 bytes one group of M-tiles' A rows may take (of 126 MB; the rest holds
 // the weight tiles in flight, outputs and partials).
 static constexpr int64_t kL2GroupBytes = 40ll << 20;
 static constexpr double kL2Bytes = 96.0 * (1 << 20);  // L2 a GEMM's A operand can count on keeping
-static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms, bool allow_split = false, int forced_splits = 0) {
+static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms, bool allow_split = false, int forced_splits = 0,
+                           int nb = 1) {
   Plan p{};
   p.m_tiles = static_cast<int>(cdiv(M, 256));
   p.n_tiles = static_cast<int>(cdiv(N, BN));
@@ -252,7 +253,7 @@ static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms, bool allow_spli
       double best = 1e30;
       for (int s = 1; s <= 4; ++s) {
         const int kbs = static_cast<int>(cdiv(p.k_blocks, s));
-        if (s > 1 && (kbs < 8 || tiles * s * 2 * 128 * BN * 4 > kPairPartialBudget)) break;
+        if (s > 1 && (kbs < 8 || tiles * s * 2 * nb * 128 * BN * 4 > kPairPartialBudget)) break;
         const double cost = static_cast<double>(cdiv(tiles * s, pairs)) * kbs + (s > 1 ? 10.0 : 0.0);
         if (cost < best * 0.95) {
           best = cost;
@@ -271,7 +272,7 @@ static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms, bool allow_spli
 template <class Cfg>
 static Plan plan_for(int M, int N, int K, int sms, int forced_splits) {
   if constexpr (Cfg::CTAS == 2)
-    return plan_gemm_pair(M, N, K, Cfg::BN, sms, Cfg::NB == 1, forced_splits);
+    return plan_gemm_pair(M, N, K, Cfg::BN, sms, Cfg::EPI != EPI_DUAL_STORE, forced_splits, Cfg::NB);
   else return plan_gemm(M, N, K, Cfg::BN, Cfg::NB, sms, forced_splits);
 }
 
@@ -541,19 +542,22 @@ static int64_t dec_set_partials(const svdmlp_layout* L, int M, int sms) {
 }
 
 // Largest split-K partial buffer any M <= max_m can ask for: the one-CTA and
-// decode kernels (M <= 128) and the CTA-pair plain GEMMs (M >= 129; their
-// partials are capped at kPairPartialBudget), evaluated on every 256-row step.
+// decode kernels (M <= 128) and the CTA-pair GEMMs (M >= 129; the planner caps
+// their partials at kPairPartialBudget, forced split counts may exceed it),
+// evaluated on every 256-row step.
 static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
   const int M = std::min(max_m, kPairMinM - 1);
   int64_t best = 0;
-  for (int mp = kPairMinM; mp <= max_m && best < kPairPartialBudget; mp = mp < 256 ? 256 : mp + 256) {
+  for (int mp = kPairMinM; mp <= max_m; mp = mp < 256 ? 256 : mp + 256) {
     if (L->kind == SVDMLP_KIND_SVD) {
+      if (L->r_gu > 0) best = std::max(best, stage_partials<CfgGU>(mp, L->ff, L->r_gu, sms, ST_GATEUP));
       if (L->r_d > 0) {
         best = std::max(best, stage_partials<CfgDU>(mp, L->r_d, L->ff, sms, ST_DOWN_U));
         best = std::max(best, stage_partials<CfgDUf32>(mp, L->r_d, L->ff, sms, ST_DOWN_U));
         best = std::max(best, stage_partials<CfgDV>(mp, L->d, L->r_d, sms, ST_DOWN_V));
       }
     } else {
+      best = std::max(best, stage_partials<CfgDenseGU>(mp, L->ff, L->d, sms, ST_DENSE_GU));
       best = std::max(best, stage_partials<CfgDV>(mp, L->d, L->ff, sms, ST_DENSE_D));
     }
   }
@@ -1883,8 +1887,8 @@ int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
                     : stage == ST_DOWN_V || stage == ST_DENSE_D ? CfgDV::BN : CfgGemm::BN;
   // prefill X.[u_g|u_u] is a dual-store tile over the two halves of N
   const int pair_n = stage == ST_XU ? (N + 1) / 2 : N;
-  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, pair_n, K, pair_bn, planning_sms(), !dual && stage != ST_XU,
-                                                g_split_override[stage])
+  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, pair_n, K, pair_bn, planning_sms(), stage != ST_XU,
+                                                g_split_override[stage], nb)
                                 : plan_stream(M, tok, N, K, nb, (tok <= 64 ? 2 : 1) * planning_sms(),
                                               g_split_override[stage]);
   out6[0] = p.m_tiles;
