@@ -16,7 +16,7 @@ CSRC = PKG_DIR.parent / "csrc"
 INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "_native" / "libsvdmlp.so"
 SOURCES = [CSRC / "svdmlp.cu"]
-HEADERS = [CSRC / "gemm_sm100.cuh", CSRC / "ptx.cuh", INCLUDE / "svdmlp.h"]
+HEADERS = [*sorted(CSRC.glob("*.cuh")), INCLUDE / "svdmlp.h"]
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
