@@ -306,6 +306,13 @@ int svdmlp_set_layer_decode(int max_m);
  * off; both are at most 64. */
 int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots);
 
+/* prefetch_units >= 1 (default 1) launches the whole-layer decode kernel with
+ * programmatic dependent launch: its CTAs start on SMs that the previous
+ * kernel on the stream has left, prefetch the weights of `prefetch_units`
+ * units each to L2, and wait for that kernel before touching anything it
+ * writes; 0 launches it plainly.  At most 8. */
+int svdmlp_set_decode_overlap(int prefetch_units);
+
 /* Prefill layers (M > 128) in svdmlp_forward run their four GEMMs as a chain:
  * each stage waits per 256-row M-tile on counters the previous stage
  * publishes, instead of on the whole previous launch, and each stage's units

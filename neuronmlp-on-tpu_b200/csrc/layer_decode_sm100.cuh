@@ -63,6 +63,9 @@ struct LayerDecParams {
   // into L2; while a unit waits on the previous stage it requests up to
   // `pf_wait` slots beyond those it has already loaded to shared memory.
   int pf_ahead, pf_wait;
+  // units blockIdx.x + j * gridDim.x (j < pdl_units) whose weights a CTA
+  // prefetches to L2 before it waits for the previous grid
+  int pdl_units;
   const __nv_bfloat16* residual;
   long long ld_residual;
   // Optional timeline (null: off): per CTA kTraceEvents pairs of
@@ -167,6 +170,10 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
 
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = lane_id();
+  // Programmatic dependent launch: the next launch on the stream may start its
+  // CTAs as soon as SMs free up (they wait for this grid before touching any
+  // state it writes), so the next layer's weight stream overlaps this one's tail.
+  grid_launch_dependents();
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -255,6 +262,19 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
       };
       int it = 0;  // slot index over the whole run
       bool ok = true;
+      // Weights are never written by a kernel: before waiting for the previous
+      // grid, request into L2 the weights of the units the CTAs will most
+      // likely claim first (blockIdx.x, then one grid further per round).
+      // Everything else (claims, activations, counters, partials) comes
+      // after the wait.
+      for (int j = 0; j < p.pdl_units; ++j) {
+        const int u0 = static_cast<int>(blockIdx.x) + j * static_cast<int>(gridDim.x);
+        if (u0 >= p.total_units) break;
+        const LdUnit c0 = layer_dec_unit(p, u0);
+        const int n0 = unit_slots(p, c0);
+        for (int i = 0; i < n0; ++i) slot_pf(c0, i);
+      }
+      grid_dependency_wait();
       int ready_stage = 0;  // stages whose inputs are known complete (stage 0 always)
       int ntr = 0;          // producer trace events (slots [0, 40))
       trace_event(p, ntr, TR_START, -1);
@@ -330,6 +350,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
     __syncwarp();
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issuer
+    grid_dependency_wait();
     if (lane == 0) {
       const uint32_t idesc_bf = make_idesc_16bit(Cfg::BM, TOK, false);
       const uint32_t idesc_h = make_idesc_16bit(Cfg::BM, TOK, true);
@@ -385,6 +406,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue
+    grid_dependency_wait();
     const int q = warp;
     int acc_it = 0;
     int ntr = 40;  // epilogue trace events (slots [40, 64))

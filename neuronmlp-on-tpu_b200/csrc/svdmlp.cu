@@ -34,6 +34,9 @@ static constexpr int kLayerDecodeMaxM = 64;        // largest M the whole-layer 
 static constexpr int kLayerDecodeDefaultMaxM = 16; // measured: per-stage kernels are faster above 16 tokens
 static int g_layer_decode_max_m = kLayerDecodeDefaultMaxM;
 static int g_pf_ahead = 1, g_pf_wait = 0;
+// Programmatic dependent launch of the whole-layer decode kernel: 0 = off,
+// k >= 1 = on, each CTA prefetching k units' weights before its wait.
+static int g_layer_decode_pdl = 1;
 // Prefill stage chaining: M-tile groups per stage (0: off).  Off by default:
 // under the 1 kW power cap that sustained prefill runs at, filling the SMs a
 // stage's tail leaves idle only lowers the clock of the others (measured
@@ -1183,8 +1186,11 @@ static int launch_layer_decode(LayerDecParams& prm, cudaStream_t s, int sms) {
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
   cfg.stream = s;
-  cfg.attrs = nullptr;
-  cfg.numAttrs = 0;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = g_layer_decode_pdl > 0 ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   TimedLaunch* tl = nullptr;
   {
     std::lock_guard<std::mutex> lock(g_timing_mu);
@@ -1220,6 +1226,7 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
   prm.trace = g_trace;
   prm.pf_ahead = g_pf_ahead;
   prm.pf_wait = g_pf_wait;
+  prm.pdl_units = g_layer_decode_pdl;
   const int64_t n1 = 2LL * L->rp_gu;
   // stage operands: token tiles (box TOK rows) and weight panels (box 128 rows)
   struct Spec {
@@ -1793,6 +1800,12 @@ int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots) {
   if (ahead_slots < 0 || ahead_slots > 64 || wait_slots < 0 || wait_slots > 64) return SVDMLP_ERR_INVALID_VALUE;
   g_pf_ahead = ahead_slots;
   g_pf_wait = wait_slots;
+  return SVDMLP_OK;
+}
+
+int svdmlp_set_decode_overlap(int prefetch_units) {
+  if (prefetch_units < 0 || prefetch_units > 8) return SVDMLP_ERR_INVALID_VALUE;
+  g_layer_decode_pdl = prefetch_units;
   return SVDMLP_OK;
 }
 

@@ -86,6 +86,7 @@ SIGNATURES = {
     "svdmlp_debug_wait_timeout": (c_int, [V, I64, I64, V]),
     "svdmlp_set_split_override": (c_int, [c_int, c_int]),
     "svdmlp_set_layer_decode": (c_int, [c_int]),
+    "svdmlp_set_decode_overlap": (c_int, [c_int]),
     "svdmlp_set_decode_prefetch": (c_int, [c_int, c_int]),
     "svdmlp_set_prefill_chain": (c_int, [c_int]),
     "svdmlp_set_trace_buffer": (c_int, [V, I64]),
