@@ -195,7 +195,8 @@ def test_per_stage_decode_forced_splits(cuda_device, m):
 def test_whole_layer_decode_kernel(cuda_device, m):
     """The one-launch whole-layer decode kernel (forced up to M = 64, both token
     tile widths) matches the oracle and the four per-stage kernels, with and
-    without a residual."""
+    without a residual, and gives the same bits with the overlapped
+    (programmatic dependent) launch turned off."""
     from svdflash_b200 import _lib
     from svdflash_b200.kernels import ops
     lib = _lib.load()
@@ -210,16 +211,22 @@ def test_whole_layer_decode_kernel(cuda_device, m):
         y1 = ops.svd_mlp_packed(layer, xd)
         y1r = ops.svd_mlp_packed(layer, xd, residual=rd)
         y1b = ops.svd_mlp_packed(layer, xd)
+        assert lib.svdmlp_set_decode_overlap(0) == 0
+        y1s = ops.svd_mlp_packed(layer, xd)
+        lib.svdmlp_set_decode_overlap(1)
         lib.svdmlp_set_layer_decode(0)
         y0 = ops.svd_mlp_packed(layer, xd)
     finally:
         lib.svdmlp_set_layer_decode(-1)
+        lib.svdmlp_set_decode_overlap(1)
     torch.cuda.synchronize()
     ops.check_device_status(cuda_device)
     ref = orc.svd_mlp(x, *f)
     assert_close(to_np(y1), ref, what=f"layer decode m={m}")
     assert_close(to_np(y1r), res + ref, what=f"layer decode + residual m={m}")
     assert torch.equal(y1, y1b), "repeated launches differ"
+    # a plain launch (no programmatic dependent launch): identical bits
+    assert torch.equal(y1, y1s), "the overlapped launch changes the result"
     from helpers import assert_close_bf16_output
     assert_close_bf16_output(to_np(y1), to_np(y0), what=f"layer decode vs per-stage m={m}")
 
