@@ -70,3 +70,11 @@ def test_config_tables_and_budget():
 def test_silu_helper_matches_formula():
     x = torch.linspace(-20, 20, 101)
     torch.testing.assert_close(ops.silu(x), x * torch.sigmoid(x))
+
+
+def test_host_pipeline_argument_checks():
+    """HostPipeline refuses a depth that cannot overlap the copies (checked
+    before any device buffer or stream is created)."""
+    from svdflash_b200.pipeline import HostPipeline
+    with pytest.raises(ValueError, match="depth"):
+        HostPipeline(lambda x, out: out, (4, 8), (4, 8), device="cuda:0", depth=1)

@@ -270,3 +270,29 @@ def test_prefill_chain_matches_unchained(cuda_device, m):
     assert torch.equal(y1, y0), "three M-tile groups differ from the unchained path"
     assert torch.equal(yr, y0r), "chained residual epilogue differs"
     assert_close(to_np(ys[0]), orc.svd_mlp(x, *f), what=f"chained prefill m={m}")
+
+
+def test_host_pipeline_matches_direct_calls(cuda_device):
+    """HostPipeline (uploads, layer calls and downloads on three streams with
+    double-buffered device tensors) returns exactly the direct calls' outputs
+    for a sequence of distinct host batches, including one longer than the
+    buffer depth and a second run on the same pipeline."""
+    from svdflash_b200.kernels import ops
+    from svdflash_b200.pipeline import HostPipeline
+    m, h, r, i = 300, 1024, 700, 3584
+    _, f = orc.make_inputs(170, m, h, i, r)
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f])
+    rng = np.random.default_rng(171)
+    xs = [torch.from_numpy(orc.bf16_round(rng.standard_normal((m, h), dtype=np.float32))).to(torch.bfloat16)
+          for _ in range(5)]
+    ref = [ops.svd_mlp_packed(layer, x.to(cuda_device)).cpu() for x in xs]
+    pipe = HostPipeline(lambda x, out: ops.svd_mlp_packed(layer, x, out=out), (m, h), (m, h), device=cuda_device)
+    for _ in range(2):
+        x_host = [x.pin_memory() for x in xs]
+        y_host = [torch.empty(m, h, dtype=torch.bfloat16).pin_memory() for _ in xs]
+        pipe.run(x_host, y_host)
+        torch.cuda.current_stream(cuda_device).synchronize()
+        for k, (y, yr) in enumerate(zip(y_host, ref)):
+            assert torch.equal(y, yr), f"batch {k} differs from the direct call"
+    with pytest.raises(ValueError):
+        HostPipeline(lambda x, out: x, (m, h), (m, h), device=cuda_device, depth=1)
