@@ -313,6 +313,11 @@ int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots);
  * writes; 0 launches it plainly.  At most 8. */
 int svdmlp_set_decode_overlap(int prefetch_units);
 
+/* Layers (and svdmlp_gemm calls) of M >= m tokens run on the CTA-pair GEMMs,
+ * smaller ones on the decode kernels.  Default 129; values below 17 act as 17;
+ * a negative value restores the default; above 129 is invalid. */
+int svdmlp_set_pair_min_m(int m);
+
 /* Prefill layers (M > 128) in svdmlp_forward run their four GEMMs as a chain:
  * each stage waits per 256-row M-tile on counters the previous stage
  * publishes, instead of on the whole previous launch, and each stage's units

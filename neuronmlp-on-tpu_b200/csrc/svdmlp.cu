@@ -281,7 +281,12 @@ static Plan plan_for(int M, int N, int K, int sms, int forced_splits) {
 
 // Token counts above this use the CTA-pair kernels; below, one-CTA kernels
 // with split-K stream the weights across all SMs.
-static constexpr int kPairMinM = 129;
+// Smallest M run on the CTA-pair GEMMs (below it: the one-CTA and streaming
+// decode kernels).  Tunable at run time down to kPairMinMLowest; workspaces are
+// sized for any threshold in that range.
+static constexpr int kPairMinMDefault = 129;
+static constexpr int kPairMinMLowest = 17;
+static int g_pair_min_m = kPairMinMDefault;
 
 // Split choice for a weight-streaming (decode) stage, from a model fitted to
 // B200 measurements of these kernels: a CTA streams about 60 GB/s (its
@@ -545,13 +550,14 @@ static int64_t dec_set_partials(const svdmlp_layout* L, int M, int sms) {
 }
 
 // Largest split-K partial buffer any M <= max_m can ask for: the one-CTA and
-// decode kernels (M <= 128) and the CTA-pair GEMMs (M >= 129; the planner caps
-// their partials at kPairPartialBudget, forced split counts may exceed it),
-// evaluated on every 256-row step.
+// decode kernels (M <= 128) and the CTA-pair GEMMs (any M >= kPairMinMLowest,
+// so that every run-time threshold fits; the planner caps their partials at
+// kPairPartialBudget, forced split counts may exceed it), evaluated on every
+// 256-row step.
 static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
-  const int M = std::min(max_m, kPairMinM - 1);
+  const int M = std::min(max_m, kPairMinMDefault - 1);
   int64_t best = 0;
-  for (int mp = kPairMinM; mp <= max_m; mp = mp < 256 ? 256 : mp + 256) {
+  for (int mp = kPairMinMLowest; mp <= max_m; mp = mp < 256 ? 256 : mp + 256) {
     if (L->kind == SVDMLP_KIND_SVD) {
       if (L->r_gu > 0) best = std::max(best, stage_partials<CfgGU>(mp, L->ff, L->r_gu, sms, ST_GATEUP));
       if (L->r_d > 0) {
@@ -1013,7 +1019,7 @@ template <class CPair, class COne>
 static int gemm_stage(const Operand& a, const Operand& a2, const Operand& b, const Operand& b2, const Output& o,
                       int M, int N, int K, int stage, const Workspace& w, cudaStream_t s,
                       const void* residual = nullptr, int64_t ld_res = 0) {
-  if (M >= kPairMinM) return gemm_cfg<CPair>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
+  if (M >= g_pair_min_m) return gemm_cfg<CPair>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
   return gemm_cfg<COne>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
 }
 
@@ -1038,7 +1044,7 @@ template <class CPair, template <class> class Pick>
 static int gemm_stage_dec(const Operand& a, const Operand& a2, const Operand& b, const Operand& b2, const Output& o,
                           int M, int N, int K, int stage, const Workspace& w, cudaStream_t s,
                           const void* residual = nullptr, int64_t ld_res = 0) {
-  if (M >= kPairMinM) return gemm_cfg<CPair>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
+  if (M >= g_pair_min_m) return gemm_cfg<CPair>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
   if (M <= 16) return gemv_cfg<Pick<Dec16>>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
   if (M <= 64) return gemv_cfg<Pick<Dec64>>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
   return gemv_cfg<Pick<Dec128>>(a, a2, b, b2, o, M, N, K, stage, w, residual, ld_res, s);
@@ -1059,7 +1065,7 @@ static int run_xu(const svdmlp_layout* L, const uint8_t* packed, const void* x, 
   const Operand xa{x, false, L->d, M, ldx};
   __half* xu = xu_out ? static_cast<__half*>(xu_out) : w.xu;  // the workspace's XU or a caller's buffer
   const int64_t ldo = xu_out ? ld_xu : n1;
-  if (M >= kPairMinM) {
+  if (M >= g_pair_min_m) {
     // the two halves of the packed w1 (rp_gu is a whole number of 16-row groups)
     const uint8_t* w1 = packed + L->off_w1;
     const Operand wg{w1, false, L->d, L->rp_gu, L->ld_d};
@@ -1523,7 +1529,7 @@ int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, in
   const void* res = nullptr;
   int64_t ldr = 0;
   const bool residual_in_place = residual && aligned16(residual, ld_res);
-  if (M >= kPairMinM && g_chain_groups > 0 && cdiv(M, 256) <= kChainStride && (!residual || residual_in_place)) {
+  if (M >= g_pair_min_m && g_chain_groups > 0 && cdiv(M, 256) <= kChainStride && (!residual || residual_in_place)) {
     // Prefill: the four stages as a chain (gemm_sm100.cuh), each stage
     // starting on the M-tile groups its predecessor has completed.
     int* base = w.counters + kChainOffsetInts;
@@ -1703,9 +1709,9 @@ int svdmlp_down_finish(const svdmlp_layout* L, const void* packed, const float* 
 int64_t svdmlp_gemm_workspace_bytes(int M, int N, int K) {
   if (M <= 0 || N <= 0 || K <= 0) return SVDMLP_ERR_INVALID_VALUE;
   const int sms = planning_sms();
-  const Plan pl = M >= kPairMinM ? plan_for<CfgGemm>(M, N, K, sms, g_split_override[ST_GEMM])
+  const Plan pl = M >= g_pair_min_m ? plan_for<CfgGemm>(M, N, K, sms, g_split_override[ST_GEMM])
                                  : plan_for<CfgGemm1>(M, N, K, sms, g_split_override[ST_GEMM]);
-  const int64_t part = M >= kPairMinM ? partial_bytes(pl, CfgGemm::BN, 1, 2) : partial_bytes(pl, CfgGemm1::BN, 1);
+  const int64_t part = M >= g_pair_min_m ? partial_bytes(pl, CfgGemm::BN, 1, 2) : partial_bytes(pl, CfgGemm1::BN, 1);
   return kCtlBytes + kCounterBytes + round_up(part, 256);
 }
 
@@ -1809,6 +1815,12 @@ int svdmlp_set_decode_overlap(int prefetch_units) {
   return SVDMLP_OK;
 }
 
+int svdmlp_set_pair_min_m(int m) {
+  if (m > kPairMinMDefault) return SVDMLP_ERR_INVALID_VALUE;
+  g_pair_min_m = m < 0 ? kPairMinMDefault : std::max(m, kPairMinMLowest);
+  return SVDMLP_OK;
+}
+
 int svdmlp_set_prefill_chain(int groups) {
   if (groups < 0 || groups > 64) return SVDMLP_ERR_INVALID_VALUE;
   g_chain_groups = groups;
@@ -1900,7 +1912,7 @@ int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
                     : stage == ST_DOWN_V || stage == ST_DENSE_D ? CfgDV::BN : CfgGemm::BN;
   // prefill X.[u_g|u_u] is a dual-store tile over the two halves of N
   const int pair_n = stage == ST_XU ? (N + 1) / 2 : N;
-  const Plan p = M >= kPairMinM ? plan_gemm_pair(M, pair_n, K, pair_bn, planning_sms(), stage != ST_XU,
+  const Plan p = M >= g_pair_min_m ? plan_gemm_pair(M, pair_n, K, pair_bn, planning_sms(), stage != ST_XU,
                                                 g_split_override[stage], nb)
                                 : plan_stream(M, tok, N, K, nb, (tok <= 64 ? 2 : 1) * planning_sms(),
                                               g_split_override[stage]);

@@ -87,6 +87,7 @@ SIGNATURES = {
     "svdmlp_set_split_override": (c_int, [c_int, c_int]),
     "svdmlp_set_layer_decode": (c_int, [c_int]),
     "svdmlp_set_decode_overlap": (c_int, [c_int]),
+    "svdmlp_set_pair_min_m": (c_int, [c_int]),
     "svdmlp_set_decode_prefetch": (c_int, [c_int, c_int]),
     "svdmlp_set_prefill_chain": (c_int, [c_int]),
     "svdmlp_set_trace_buffer": (c_int, [V, I64]),

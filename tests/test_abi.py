@@ -81,6 +81,7 @@ def test_entry_points_reject_bad_arguments(lib):
     assert lib.svdmlp_set_split_override(9, 1) == _lib.ERR_INVALID_VALUE
     assert lib.svdmlp_set_layer_decode(65) == _lib.ERR_INVALID_VALUE
     assert lib.svdmlp_set_decode_overlap(9) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_set_pair_min_m(130) == _lib.ERR_INVALID_VALUE
     assert lib.svdmlp_set_decode_prefetch(-1, 0) == _lib.ERR_INVALID_VALUE
     assert lib.svdmlp_set_prefill_chain(-1) == _lib.ERR_INVALID_VALUE
     assert lib.svdmlp_rmsnorm(None, 8, None, None, 8, 1, 8, 1e-5, None) == _lib.ERR_INVALID_VALUE

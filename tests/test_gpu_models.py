@@ -296,3 +296,29 @@ def test_host_pipeline_matches_direct_calls(cuda_device):
             assert torch.equal(y, yr), f"batch {k} differs from the direct call"
     with pytest.raises(ValueError):
         HostPipeline(lambda x, out: x, (m, h), (m, h), device=cuda_device, depth=1)
+
+
+@pytest.mark.parametrize("m", [40, 128])
+def test_pair_gemms_below_default_threshold(cuda_device, m):
+    """With the pair threshold lowered (svdmlp_set_pair_min_m), decode-sized
+    layers run on the CTA-pair GEMMs (one partial 256-row M-tile) and still
+    match the oracle and the decode kernels' result; the workspace sized for
+    the default threshold already covers their split-K partials."""
+    from svdflash_b200 import _lib
+    from svdflash_b200.kernels import ops
+    from helpers import assert_close_bf16_output
+    lib = _lib.load()
+    h, r, i = 1024, 700, 3584
+    x, f = orc.make_inputs(180 + m, m, h, i, r)
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f])
+    xd = to_dev(x, cuda_device)
+    y0 = ops.svd_mlp_packed(layer, xd)
+    try:
+        assert lib.svdmlp_set_pair_min_m(17) == 0
+        y1 = ops.svd_mlp_packed(layer, xd)
+    finally:
+        lib.svdmlp_set_pair_min_m(-1)
+    torch.cuda.synchronize()
+    ops.check_device_status(cuda_device)
+    assert_close(to_np(y1), orc.svd_mlp(x, *f), what=f"pair GEMMs m={m}")
+    assert_close_bf16_output(to_np(y1), to_np(y0), what=f"pair GEMMs vs decode kernels m={m}")
