@@ -293,11 +293,12 @@ static int g_pair_min_m = kPairMinMDefault;
 // in-flight weight bytes over ~1.6 us of memory latency), the GPU about
 // 7 TB/s; every extra unit a CTA runs in a stage costs about one latency, and
 // split-K adds a ~4 us chain to the stage (partial stores, the arrival
-// atomic, the last split's reads and stores), plus a memory round trip per
-// four splits per 16 tokens.
+// atomic, the last split's reads and stores), plus, when the last split sums
+// every partial, a memory round trip per four splits per 16 tokens.
 static constexpr double kHbmBytesPerUs = 7.0e6;
 static constexpr double kCtaBytesPerUs = 6.0e4;
-static Plan plan_stream(int M, int tok, int N, int K, int nb, int slots, int forced_splits) {
+static Plan plan_stream(int M, int tok, int N, int K, int nb, int slots, int forced_splits,
+                        bool spread_fixup = false) {
   Plan p{};
   p.m_tiles = 1;
   p.n_tiles = static_cast<int>(cdiv(N, 128));
@@ -318,7 +319,10 @@ static Plan plan_stream(int M, int tok, int N, int K, int nb, int slots, int for
       const double rounds = static_cast<double>(cdiv(units, slots));
       const double busiest = rounds * kbs * 16384.0 * nb;
       double us = std::max(total / kHbmBytesPerUs, busiest / kCtaBytesPerUs) + 1.5 * rounds;
-      if (s_eff > 1) us += 4.0 + 1.0 * static_cast<double>(cdiv(s_eff, 4) - 1) * tv16;
+      // The last split of a tile sums every partial (cost grows with the split
+      // count and the token chunks); in the spread fix-up every split sums
+      // 1/S of the tile's token rows in parallel, a constant hand-off.
+      if (s_eff > 1) us += spread_fixup ? 4.0 : 4.0 + 1.0 * static_cast<double>(cdiv(s_eff, 4) - 1) * tv16;
       if (us < best * 0.97) {
         best = us;
         best_s = s_eff;
@@ -340,7 +344,20 @@ static Plan plan_dec(int M, int N, int K, int sms, int forced_splits) {
 #define SVDMLP_DEC_CTAS_PER_SM 2
 #endif
   const int slots = (Cfg::TWO_PER_SM ? SVDMLP_DEC_CTAS_PER_SM : 1) * sms;
-  return plan_stream(M, Cfg::TOK, N, K, Cfg::NB, slots, forced_splits);
+  // Above 16 tokens the per-stage kernels use the spread fix-up (gemv_sm100.cuh).
+  const bool spread = std::min(M, Cfg::TOK) > 16;
+  if (spread && Cfg::NB == 1 && forced_splits <= 0) {
+    // One-branch stages: the smallest split count that gives at least 1.2
+    // units per SM.  Split sweeps of the 8B layer at 32 and 128 tokens, ratios
+    // 0.6 and 0.9, put this within ~3 us of the best (X.[u_g,u_u] 4-6,
+    // H.u_down 8-12, T.v_down 4-6 splits); the stream model above
+    // under-splits these stages by 2-9 us.
+    const int n_tiles = static_cast<int>(cdiv(N, Cfg::BM));
+    const int k_blocks = static_cast<int>(cdiv(K, Cfg::BK));
+    const int want = static_cast<int>(std::min<int64_t>(k_blocks / 2, cdiv(static_cast<int64_t>(12 * sms), 10LL * n_tiles)));
+    return plan_stream(M, Cfg::TOK, N, K, Cfg::NB, slots, std::max(1, want), true);
+  }
+  return plan_stream(M, Cfg::TOK, N, K, Cfg::NB, slots, forced_splits, spread);
 }
 
 // One stage of the whole-layer decode kernel (all stages share `slots` CTAs).
