@@ -1929,10 +1929,18 @@ int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
                     : stage == ST_DOWN_V || stage == ST_DENSE_D ? CfgDV::BN : CfgGemm::BN;
   // prefill X.[u_g|u_u] is a dual-store tile over the two halves of N
   const int pair_n = stage == ST_XU ? (N + 1) / 2 : N;
+  // below the pair threshold: the plan of the per-stage decode kernel for M
+  // (the same function the launches use)
+  auto dec_plan = [&](auto set) -> Plan {
+    using Set = decltype(set);
+    return dual ? plan_dec<typename Set::GU>(M, N, K, planning_sms(), g_split_override[stage])
+                : plan_dec<typename Set::XU>(M, N, K, planning_sms(), g_split_override[stage]);
+  };
   const Plan p = M >= g_pair_min_m ? plan_gemm_pair(M, pair_n, K, pair_bn, planning_sms(), stage != ST_XU,
                                                 g_split_override[stage], nb)
-                                : plan_stream(M, tok, N, K, nb, (tok <= 64 ? 2 : 1) * planning_sms(),
-                                              g_split_override[stage]);
+                 : tok == 16         ? dec_plan(Dec16{})
+                 : tok == 64         ? dec_plan(Dec64{})
+                                     : dec_plan(Dec128{});
   out6[0] = p.m_tiles;
   out6[1] = p.n_tiles;
   out6[2] = p.k_blocks;

@@ -106,6 +106,21 @@ def test_plan_info_is_deterministic(lib):
     assert out[0] == 1 and out[3] >= 1 and out[4] == out[1] * out[3]
 
 
+def test_decode_plans_split_one_branch_stages_per_sm(lib):
+    """Per-stage decode plans above 16 tokens: one-branch stages split to at
+    least 1.2 units per SM (148 SMs without a GPU), the dual gate/up stage
+    stays unsplit; the 8B layer at ratio 0.9 gives the measured best splits
+    X.[u_g,u_u] 4, H.u_down 8."""
+    out = (ctypes.c_int * 6)()
+    for m in (32, 128):
+        assert lib.svdmlp_plan_info(0, m, 5760, 4096, out) == 0      # X.[u_g|u_u]: 45 tiles
+        assert out[1] == 45 and out[3] == 4
+        assert lib.svdmlp_plan_info(2, m, 2867, 14336, out) == 0     # H.u_down: 23 tiles
+        assert out[1] == 23 and out[3] == 8 and out[1] * out[3] >= 1.2 * 148
+        assert lib.svdmlp_plan_info(1, m, 14336, 2867, out) == 0     # dual gate/up
+        assert out[3] == 1
+
+
 def test_status_mapping_to_exceptions():
     from svdflash_b200 import _lib
     with pytest.raises(ValueError):
