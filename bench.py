@@ -480,9 +480,18 @@ def main():
     # step uploads its input and downloads its output inside the timed region;
     # HostPipeline overlaps step i+1's upload and step i-1's download with
     # step i's layer (three streams, double-buffered device tensors).
-    x_host = x.cpu().pin_memory()
-    y_hosts = [torch.empty(m, d, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    pipe = HostPipeline(step, (m, d), (m, d), device=dev)
+    # Under tensor parallelism each rank feeds and reads its own row block of
+    # the batch (TensorParallelSvdMlp.forward_rows all-gathers the blocks over
+    # NVLink), so every GPU's host link carries 1/N of the batch.
+    io_rows = m // world if world > 1 and m % world == 0 else m
+    if io_rows < m:
+        x_host = x[rank * io_rows:(rank + 1) * io_rows].cpu().pin_memory()
+        io_step = tp.forward_rows
+    else:
+        x_host = x.cpu().pin_memory()
+        io_step = step
+    y_hosts = [torch.empty(io_rows, d, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+    pipe = HostPipeline(io_step, (io_rows, d), (io_rows, d), device=dev)
     e2e_steps = max(10, min(args.steps, 200))
     pipe.run([x_host] * 3, [y_hosts[i % 2] for i in range(3)])
     torch.cuda.synchronize()
@@ -584,7 +593,9 @@ def main():
         "roofline": roofline,
         "e2e": {"value": m / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": m * d * 2,
                 "d2h_bytes_per_step": m * d * 2, "ms_per_step": e2e_ms,
-                "api": "svdflash_b200.pipeline.HostPipeline over the layer call (copies overlapped, depth 2)"},
+                "api": "svdflash_b200.pipeline.HostPipeline over the layer call (copies overlapped, depth 2)"
+                       + ("" if io_rows == m else "; TensorParallelSvdMlp.forward_rows: each rank copies its "
+                                                 f"{io_rows}-row block in and out, blocks all-gathered over NVLink")},
         "gpu_launches": launches,
         "clocks": clocks,
         "parity_sample": parity,

@@ -35,6 +35,31 @@ def shard_bounds(ff: int, rank: int, world: int) -> tuple[int, int]:
     return rank * step, (rank + 1) * step
 
 
+def gather_rows_forward(forward, x_rows: torch.Tensor, rank: int, world: int, group=None,
+                        residual_rows: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                        returns_rows: bool = False) -> torch.Tensor:
+    """Runs `forward(x, residual=...)` on the whole batch when each rank holds
+    only its row block: rank p passes rows [p*R, (p+1)*R) of X (and of the
+    residual) and receives the same rows of the output.  The row blocks are
+    all-gathered first (NVLink under NCCL), so that a serving loop that feeds
+    each GPU 1/P of the batch from host memory moves 1/P of the bytes over
+    each GPU's host link instead of the whole batch.  With `returns_rows`,
+    `forward` already returns only this rank's rows."""
+    rows = x_rows.shape[0]
+    x = torch.empty((rows * world,) + tuple(x_rows.shape[1:]), dtype=x_rows.dtype, device=x_rows.device)
+    dist.all_gather_into_tensor(x, x_rows.contiguous(), group=group)
+    res = None
+    if residual_rows is not None:
+        res = torch.empty_like(x)
+        dist.all_gather_into_tensor(res, residual_rows.contiguous(), group=group)
+    y = forward(x, residual=res)
+    mine = y if returns_rows else y[rank * rows:(rank + 1) * rows]
+    if out is None:
+        return mine if returns_rows else mine.clone()
+    out.copy_(mine)
+    return out
+
+
 class TensorParallelSvdMlp:
     """One ff-sharded SVD MLP layer on this rank's GPU."""
 
@@ -74,6 +99,21 @@ class TensorParallelSvdMlp:
 
     __call__ = forward
 
+    def forward_rows(self, x_rows: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """The layer for a batch whose rows are spread over the ranks: this
+        rank passes its row block of X (rows [rank*R, (rank+1)*R) of the
+        batch) and gets the same rows of Y (see gather_rows_forward).  In the
+        split mode the final all-gather of y is skipped: this rank's rows are
+        the ones its `. v_down` produced."""
+        if self.world == 1:
+            return self.forward(x_rows, residual=residual, out=out)
+        m = x_rows.shape[0] * self.world
+        if self._use_split(m, x_rows.shape[1]):
+            return gather_rows_forward(lambda x, residual=None: self._forward_split(x, residual, None, own_rows=True),
+                                       x_rows, self.rank, self.world, self.group, residual, out, returns_rows=True)
+        return gather_rows_forward(self.forward, x_rows, self.rank, self.world, self.group, residual, out)
+
     # "auto": the split pays once the replicated stages outweigh the fixed cost
     # of two more collectives (measured on 2 B200s: 70B layer at 4096 tokens
     # 2491 -> 2198 us; 8B layer at 1024 tokens 215 -> 269 us).
@@ -84,7 +124,8 @@ class TensorParallelSvdMlp:
             return self.reduce_dtype == torch.float16 and m * d > self.SPLIT_MIN_ELEMENTS
         return self.mode == "split"
 
-    def _forward_split(self, x: torch.Tensor, residual: Optional[torch.Tensor], out: Optional[torch.Tensor]):
+    def _forward_split(self, x: torch.Tensor, residual: Optional[torch.Tensor], out: Optional[torch.Tensor],
+                       own_rows: bool = False):
         m, d = x.shape
         rows = m // self.world
         lo, hi = self.rank * rows, (self.rank + 1) * rows
@@ -99,6 +140,8 @@ class TensorParallelSvdMlp:
         dist.reduce_scatter_tensor(t_p, full, op=dist.ReduceOp.SUM, group=self.group)
         y_p = ops.down_finish_packed(self.layer, t_p[:, :self.r_d],
                                      residual=None if residual is None else residual[lo:hi])
+        if own_rows:
+            return y_p  # rows [lo, hi) of y: the caller needs no others
         y = out if out is not None else torch.empty((m, d), dtype=torch.bfloat16, device=dev)
         dist.all_gather_into_tensor(y, y_p, group=self.group)
         return y

@@ -55,6 +55,48 @@ def test_ff_sharded_layer_matches_single_rank():
     np.testing.assert_array_equal(outs[0], outs[1])
 
 
+def _rows_worker(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=30))
+    try:
+        from svdflash_b200.tp import gather_rows_forward
+        x, f = orc.make_inputs(23, 12, 64, 128, 40, 24)
+        rows = x.shape[0] // world
+        res = np.arange(x.size, dtype=np.float32).reshape(x.shape) / x.size
+
+        def fwd(xx, residual=None):  # the whole layer, as every rank computes it
+            y = orc.svd_mlp(xx.numpy(), *f)
+            return torch.from_numpy(y + (0 if residual is None else residual.numpy()))
+
+        mine = slice(rank * rows, (rank + 1) * rows)
+        y = gather_rows_forward(fwd, torch.from_numpy(x[mine]), rank, world,
+                                residual_rows=torch.from_numpy(res[mine]))
+        q.put((rank, y.numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_sharded_io_gathers_and_returns_own_rows():
+    """gather_rows_forward: each rank passes its row block of X and of the
+    residual, the blocks are all-gathered, and each rank gets its own rows of
+    the whole-batch result."""
+    world = 2
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rows_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    outs = dict(q.get(timeout=120) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    x, f = orc.make_inputs(23, 12, 64, 128, 40, 24)
+    res = np.arange(x.size, dtype=np.float32).reshape(x.shape) / x.size
+    ref = orc.svd_mlp(x, *f) + res
+    np.testing.assert_allclose(np.concatenate([outs[0], outs[1]]), ref, rtol=1e-6, atol=1e-6)
+
+
 def test_shard_bounds_and_uneven_ff():
     from svdflash_b200.tp import shard_bounds
     assert [shard_bounds(14336, r, 8) for r in (0, 7)] == [(0, 1792), (12544, 14336)]
