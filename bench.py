@@ -47,6 +47,27 @@ def rank_for(d, ff, ratio):
     return int(ratio * d * ff // (d + ff))
 
 
+def workload_config(name: str, wl: dict) -> dict:
+    """The `config` object both arms print (the workload only, so that the
+    reference arm's line and this arm's line name the same thing)."""
+    d, ff, m = wl["d"], wl["ff"], wl["tokens"]
+    r = rank_for(d, ff, wl["ratio"])
+    weight_mb = 2.0 * 3 * r * (d + ff) / 1e6
+    return {"workload": name, "d": d, "ff": ff, "r": r, "tokens": m, "ratio": wl["ratio"],
+            "l2": f"inputs larger than L2: {weight_mb:.0f} MB of factors streamed per step"}
+
+
+def cpu_model() -> str:
+    try:
+        for line in pathlib.Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+    return platform.processor() or "unknown"
+
+
 def load_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -197,11 +218,19 @@ def cpu_baseline(wl: dict, reps: int, warmup: int = 1, rows: int | None = None) 
         "sample": f"{m_s} tokens x 1 layer (d={d}, ff={ff}, r={r}) fp32 NumPy/OpenBLAS, median of {reps} after {warmup} warm-up",
         "seconds_per_sample": med,
         "cpu_count": os.cpu_count(),
+        "cpu_model": cpu_model(),
     }
 
 
 def run_reference_arm(args, wl) -> None:
-    """--impl reference: the reference CPU implementation of the path."""
+    """--impl reference: the reference CPU implementation of the path.
+
+    The reference computes this path on the CPU only in kernels/reference.py
+    (NumPy fp32).  It is not an installable package (no setup.py or
+    pyproject.toml, so `pip install` into baseline/_ref fails), and a Python
+    reference cannot travel to the GPU box, so this arm times the oracle's
+    restatement of it, whose outputs the CPU tests pin bit-for-bit to the
+    reference's own on committed fixtures (kind "port")."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
@@ -215,9 +244,9 @@ def run_reference_arm(args, wl) -> None:
         "metric": METRIC, "value": base["value"], "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": base["seconds_per_sample"] * 1e3, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
-        "config": {"workload": args.workload, "d": d, "ff": ff, "r": r, "tokens": m, "ratio": wl["ratio"],
-                   "parallelism": "cpu"},
-        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "config": workload_config(args.workload, wl),
+        "parallelism": "cpu (rank 0 only)",
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample", "cpu_model")},
         "e2e": {"value": base["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -233,6 +262,47 @@ def make_factors(d, ff, r, seed, device):
         return (torch.randn(rows, cols, generator=g, device=device) / math.sqrt(rows)).to(torch.bfloat16)
 
     return mat(d, r), mat(r, ff), mat(d, r), mat(r, ff), mat(ff, r), mat(r, d)
+
+
+def decode_record(dev, seed: int, steps: int, warmup: int, hbm_peak: float, peak_src: str) -> dict:
+    """BASELINE config 2 inside the default line: the 8B layer (r = 2867) at
+    1 and 128 tokens, rotating over three independently drawn weight copies
+    (3 x 317 MB of factors, well beyond the 126 MB L2), so that every call
+    streams its factors from HBM.  Bytes per call = the three factor pairs
+    once + x in + y out; fraction of the measured copy bandwidth."""
+    import torch
+
+    from svdflash_b200.kernels import ops
+    d, ff, ratio = 4096, 14336, 0.9
+    r = rank_for(d, ff, ratio)
+    layers = [ops.pack_svd_layer(*make_factors(d, ff, r, seed + 100 + i, dev)) for i in range(3)]
+    torch.cuda.empty_cache()
+    rec = {"workload": "llama3-8b-decode", "r": r, "weight_copies": len(layers),
+           "l2": "3 rotated weight copies (951 MB) per 3 calls, larger than L2"}
+    stream = torch.cuda.current_stream(dev)
+    for m in (1, 128):
+        x = torch.randn(m, d, device=dev).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        n = max(30, min(steps, 600)) // 3 * 3
+        for i in range(max(3, warmup)):
+            ops.svd_mlp_packed(layers[i % 3], x, out=y)
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n):
+            ops.svd_mlp_packed(layers[i % 3], x, out=y)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        us = 1e3 * e0.elapsed_time(e1) / n
+        nbytes = 2.0 * 3 * r * (d + ff) + 4.0 * m * d
+        gbs = nbytes / (us * 1e-6) / 1e9
+        rec[f"m{m}"] = {"tokens": m, "us_per_layer": us, "hbm_gbs": gbs, "frac_of_measured_hbm": gbs / hbm_peak,
+                        "bytes_per_layer": nbytes, "calls": n}
+    rec["peak_source"] = f"{peak_src} hbm_gbs (copy bandwidth) = {hbm_peak}"
+    del layers
+    torch.cuda.empty_cache()
+    return rec
 
 
 def parity_sample(x, factors, y, nrows=16):
@@ -370,6 +440,7 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3-8b-layer")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="N=1: leave out the decode (config 2) sub-record")
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--tp-mode", choices=("auto", "allreduce", "split"), default="auto",
                     help="N>1: one all-reduce of the partial (default) or the all-gather split of the replicated stages")
@@ -435,7 +506,6 @@ def main():
     step(x)
     torch.cuda.synchronize()
     parity = parity_sample(x, factors, y) if rank == 0 else None
-    weight_bytes = sum(t.numel() for t in factors) * 2
     del factors
     torch.cuda.empty_cache()
 
@@ -536,6 +606,11 @@ def main():
                    "down_v": 2.0 * d * rp + 2.0 * m * rp + 2.0 * m * d}
     stage_bytes["layer_decode"] = sum(stage_bytes.values())
 
+    decode = None
+    if world == 1 and not args.no_decode:
+        pk, pk_src = load_peaks()
+        decode = decode_record(dev, args.seed, args.steps, args.warmup, float(pk["hbm_gbs"]), pk_src)
+
     if world > 1:
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
@@ -561,11 +636,21 @@ def main():
                         "traffic": traffic, "algorithmic_bytes_per_launch": stage_bytes[dominant]}
         else:
             achieved = stage_flops[dominant] / (stage_us[dominant] * 1e-6) / 1e12
-            peak = float(peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops")))
+            # The denominator follows the clocks seen during the timed region:
+            # the burst cuBLAS rate when the GPU ran unthrottled, the sustained
+            # (power-capped) rate when sw_power_cap was active.
+            burst = float(peaks.get("bf16_tflops", 1590.0))
+            sustained = float(peaks.get("bf16_tflops_sustained", burst))
+            capped = bool(clocks) and "sw_power_cap" in (clocks.get("reasons") or [])
+            peak = sustained if capped else burst
             roofline = {"bound": "tensor", "kernel": kname, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
                         "frac": achieved / peak,
-                        "peak_source": f"{peak_src} bf16_tflops_sustained (kernel timed inside a long run)",
-                        "traffic": traffic, "algorithmic_flops_per_launch": stage_flops[dominant]}
+                        "peak_source": (f"{peak_src} bf16_tflops_sustained (sw_power_cap active in the timed region)"
+                                        if capped else f"{peak_src} bf16_tflops (burst: no clock-event reason "
+                                        "active in the timed region)"),
+                        "frac_of_burst": achieved / burst, "frac_of_sustained": achieved / sustained,
+                        "traffic": traffic, "algorithmic_flops_per_launch": stage_flops[dominant],
+                        "kernel_us": stage_us[dominant]}
     layer_bytes = stage_bytes["layer_decode"]
     tokens_per_s = m / (ms_per_step * 1e-3)
     line = {
@@ -581,18 +666,20 @@ def main():
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": args.workload, "d": d, "ff": ff, "r": r, "tokens": m, "ratio": wl["ratio"],
-                   "parallelism": f"tp-ff{world}" if world > 1 else "single-gpu",
-                   "allreduce": ("split: all-gather XU, reduce-scatter fp16 partial, all-gather y"
-                                 if tp._use_split(m, d) else "fp16 [M, r] partial, NCCL") if world > 1 else None,
-                   "l2": f"inputs larger than L2: {weight_bytes / 1e6:.0f} MB of factors streamed per step"},
+        "config": workload_config(args.workload, wl),
+        "parallelism": f"tp-ff{world}" if world > 1 else "single-gpu",
+        "collectives": ("split: all-gather XU, reduce-scatter fp16 partial, all-gather y"
+                        if tp._use_split(m, d) else "one NCCL all-reduce of the fp16 [M, r] partial")
+                       if world > 1 else None,
         "us_per_layer": ms_per_step * 1e3,
         "tflops": flops_layer / (ms_per_step * 1e-3) / 1e12,
         "stage_us": stage_us,
         "hbm_gbs_layer": layer_bytes / (ms_per_step * 1e-3) / 1e9,
         "roofline": roofline,
         "e2e": {"value": m / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": m * d * 2,
-                "d2h_bytes_per_step": m * d * 2, "ms_per_step": e2e_ms,
+                "d2h_bytes_per_step": m * d * 2, "bytes_per_step_are": "whole job (all ranks together)",
+                "h2d_bytes_per_step_per_rank": io_rows * d * 2, "d2h_bytes_per_step_per_rank": io_rows * d * 2,
+                "ms_per_step": e2e_ms,
                 "api": "svdflash_b200.pipeline.HostPipeline over the layer call (copies overlapped, depth 2)"
                        + ("" if io_rows == m else "; TensorParallelSvdMlp.forward_rows: each rank copies its "
                                                  f"{io_rows}-row block in and out, blocks all-gathered over NVLink")},
@@ -600,9 +687,11 @@ def main():
         "clocks": clocks,
         "parity_sample": parity,
     }
+    if decode is not None:
+        line["decode"] = decode
     if not args.no_cpu_baseline and world == 1:
         line["cpu_baseline"] = {k: v for k, v in cpu_baseline(wl, reps=args.cpu_reps).items()
-                                if k in ("value", "unit", "cores", "kind", "sample")}
+                                if k in ("value", "unit", "cores", "kind", "sample", "cpu_model")}
     print(json.dumps(line), flush=True)
 
 

@@ -7,15 +7,17 @@
  *     H   = SiLU((X . u_gate) . v_gate) * ((X . u_up) . v_up)      "gate/up"
  *     out = (H . u_down) . v_down                                 "XUV down"
  *
- * with bf16 inputs, fp32 accumulation and one bf16 rounding per GEMM boundary.
+ * with bf16 inputs and outputs, fp32 accumulation, and the three intermediates
+ * (X.u, H and H.u_down) rounded once each to fp16 (see svdmlp_layout).
  * Factor names follow the reference Python (kernels/reference.py:54-93):
  * u_* is the first factor [in, r], v_* the second factor [r, out].
  *
  * Conventions
  *  - Every entry point returns an int status: 0 = SVDMLP_OK, negative = error.
  *  - All device buffers are owned by the caller; no entry point allocates
- *    device memory, and none synchronises the stream except
- *    svdmlp_check_device_status().
+ *    device memory, and none synchronises the stream except the status
+ *    reads (svdmlp_check_device_status, svdmlp_pack_status,
+ *    svdmlp_xuv_noalloc_status).
  *  - Matrices are row-major bf16 (uint16 storage) with an explicit leading
  *    dimension in elements; `void*` pointers are device pointers.
  *  - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
@@ -45,6 +47,8 @@ extern "C" {
 #define SVDMLP_ERR_CUDA (-7)            /* CUDA runtime/driver error               */
 #define SVDMLP_ERR_BUDGET (-8)          /* SMEM/TMEM budget exceeds the device     */
 #define SVDMLP_ERR_DEVICE (-9)          /* device is not sm_100 (B200 class)       */
+#define SVDMLP_ERR_RANGE (-10)          /* an fp16 intermediate or fp16-packed weight
+                                           exceeded 65504 (or was NaN) and was saturated */
 
 /* Human-readable text for a status code. */
 const char* svdmlp_status_string(int status);
@@ -81,6 +85,13 @@ int svdmlp_last_cuda_error(void);
  * every weight that multiplies an intermediate is packed as fp16.  bf16 ->
  * fp16 is exact for magnitudes in [2^-14, 65504]; smaller weights become fp16
  * subnormals (absolute error <= 2^-25).  All accumulation is fp32.
+ *
+ * Range: a value that fp16 cannot hold (|v| > 65504, or NaN) is saturated to
+ * +-65504 and never passes silently.  Weights are checked when packed
+ * (svdmlp_pack_status); intermediates when they are stored, which sets the
+ * range word of the workspace's error block (svdmlp_check_device_status
+ * then reports SVDMLP_ERR_RANGE).  Activation outliers of a few hundred times
+ * the typical row scale square in H = SiLU(g) * u and reach this limit.
  */
 typedef struct svdmlp_layout {
   int32_t kind;
@@ -88,6 +99,7 @@ typedef struct svdmlp_layout {
   int32_t rp_gu, rp_d, ld_d, ld_ff;
   int32_t ud_f16; /* 1: ud is stored as fp16 (full layers), 0: bf16 (down-only layouts) */
   int64_t off_w1, off_vg, off_vu, off_ud, off_vd; /* byte offsets into the packed buffer */
+  int64_t off_status; /* 256-byte block holding the pack status word (see svdmlp_pack_status) */
   int64_t packed_bytes;
 } svdmlp_layout;
 
@@ -113,6 +125,12 @@ int svdmlp_pack(const svdmlp_layout* layout, const void* u_gate, int64_t ld_u_ga
                 const void* u_down, int64_t ld_u_down, const void* v_down, int64_t ld_v_down, void* packed,
                 void* stream);
 
+/* Synchronises `stream`, then reports SVDMLP_ERR_RANGE if svdmlp_pack or
+ * svdmlp_dense_pack saturated a weight stored as fp16 (|w| > 65504 or NaN)
+ * into this packed buffer, else SVDMLP_OK.  Packing is a set-up step; the
+ * Python API calls this after every pack. */
+int svdmlp_pack_status(const svdmlp_layout* layout, const void* packed, void* stream);
+
 /* Packs dense weights w_gate, w_up [d, ff] and w_down [ff, d]. */
 int svdmlp_dense_pack(const svdmlp_layout* layout, const void* w_gate, int64_t ld_w_gate, const void* w_up,
                       int64_t ld_w_up, const void* w_down, int64_t ld_w_down, void* packed, void* stream);
@@ -126,8 +144,10 @@ int64_t svdmlp_workspace_bytes(const svdmlp_layout* layout, int max_m);
 int svdmlp_workspace_init(void* workspace, int64_t workspace_bytes, void* stream);
 
 /* Synchronises `stream`, then reports SVDMLP_ERR_DEVICE_TIMEOUT if a device
- * wait expired in an earlier launch on this workspace (and re-arms the
- * control block), SVDMLP_ERR_CUDA on a sticky CUDA error, else SVDMLP_OK. */
+ * wait expired in an earlier launch on this workspace, SVDMLP_ERR_RANGE if an
+ * fp16 intermediate was saturated (see svdmlp_layout), SVDMLP_ERR_CUDA on a
+ * sticky CUDA error, else SVDMLP_OK.  A reported condition is cleared (the
+ * control block re-armed), so the next call reports only later launches. */
 int svdmlp_check_device_status(void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------- operators */
@@ -251,6 +271,16 @@ int svdmlp_partial_from_xu_f16(const svdmlp_layout* layout, const void* packed, 
 int svdmlp_xuv_noalloc(const svdmlp_layout* layout, const void* packed, const void* h, int64_t ld_h, int m,
                        void* y, int64_t ld_y, void* stream);
 
+/*
+ * Status of the svdmlp_xuv_noalloc calls on the current device since its last
+ * call started (that call clears the array's error block first): synchronises
+ * `stream`, then reports SVDMLP_ERR_DEVICE_TIMEOUT if a bounded device wait
+ * expired, SVDMLP_ERR_RANGE if an fp16 intermediate was saturated, else
+ * SVDMLP_OK, and clears what it reported.  Like the entry point it allocates
+ * nothing; its error block is the one inside the library's static array.
+ */
+int svdmlp_xuv_noalloc_status(void* stream);
+
 /* --------------------------------------------------------- building blocks */
 /*
  * c[M, N] = a[M, K] . b[K, N] given b pre-transposed as bt[N, K] (K-major):
@@ -335,6 +365,14 @@ int svdmlp_set_prefill_chain(int groups);
  * least 2 * SMs * 64 * 16 bytes, zeroed by the caller. */
 int svdmlp_set_trace_buffer(void* buffer, int64_t bytes);
 int svdmlp_plan_info(int stage, int m, int n, int k, int* out6);
+
+/* Compile-time resources of the kernel a stage runs with at m tokens (the
+ * B200 counterpart of the reference's tile tables and VMEM estimates,
+ * test_speedup.py:169-191, 303-317): out8 = {tile rows (activation rows per
+ * tile: 256 for CTA pairs, the token tile at decode sizes), tile columns
+ * (output features per tile), K per pipeline stage, pipeline stages, shared
+ * memory bytes per CTA, TMEM columns per CTA, threads per CTA, CTAs per tile}. */
+int svdmlp_tile_info(int stage, int m, int* out8);
 
 /*
  * Per-stage timing for profiling passes: with timing enabled every GEMM launch

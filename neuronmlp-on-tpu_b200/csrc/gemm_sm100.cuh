@@ -184,9 +184,18 @@ SVD_DEV UnitCoord decode_unit(const GemmParams& p, int u) {
 // swizzled staging buffer and a TMA store.  `v` holds this thread's row.
 template <class Cfg>
 SVD_DEV void store_box(const CUtensorMap* tm_out, uint8_t* stg_warp, int& stg_buf, const float (&v)[32], int x,
-                       int y, int M, int N) {
+                       int y, int M, int N, int* err) {
   const uint32_t lane = lane_id();
   uint8_t* stg = stg_warp + stg_buf * Cfg::STG_BYTES;
+  if constexpr (Cfg::OUT == OUT_F16) {
+    // Saturated fp16 intermediates are reported, never silent.  Rows and
+    // columns outside the output hold zeros (zero-filled operands), so the
+    // whole box can be checked.
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bad |= f16_out_of_range(v[j]);
+    if (__any_sync(0xffffffffu, bad) && lane == 0) flag_range(err);
+  }
   // The TMA store issued two boxes ago used this buffer; make sure it has
   // finished reading it (at most one group, the other buffer's, may remain).
   if (lane == 0) bulk_wait_group_read<1>();
@@ -559,9 +568,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             w[j] = Cfg::NB == 2 ? __uint_as_float(ru[j]) : 0.0f;
           }
           epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
-          store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
+          store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
           if constexpr (Cfg::EPI == EPI_DUAL_STORE)
-            store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N);
+            store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N, p.err);
         }
         if (p.pub != nullptr) {
           // Publish this CTA's rows of the tile: each warp's output boxes are
@@ -656,9 +665,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
               }
             }
             epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
-            store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N);
+            store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
             if constexpr (Cfg::EPI == EPI_DUAL_STORE)
-              store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N);
+              store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N, p.err);
           }
         }
         named_barrier_sync(1, EPI_THREADS);

@@ -118,6 +118,10 @@ SVD_DEV void dec_store4(const GemmParams& p, void* out, long long ld_out, int t,
     }
   } else if constexpr (Cfg::OUT == OUT_F16) {
     __half* o = static_cast<__half*>(out) + off;
+    bool bad = false;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) bad |= (full || f + j < p.N) && f16_out_of_range(x[j]);
+    if (bad) flag_range(p.err);  // saturated fp16 intermediates are reported, never silent
     if (full) *reinterpret_cast<uint2*>(o) = make_uint2(pack_f16x2_sat(x[0], x[1]), pack_f16x2_sat(x[2], x[3]));
     else {
 #pragma unroll

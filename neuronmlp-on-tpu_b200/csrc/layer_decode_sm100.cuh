@@ -142,8 +142,10 @@ SVD_DEV void ld_store_chunk(const LayerDecParams& p, const DecStage& st, int f, 
       if (st.epi == EPI_RESID) x += __bfloat162float(p.residual[static_cast<long long>(t) * p.ld_residual + f]);
       const long long off = static_cast<long long>(t) * st.ld_out + f;
       if (st.out_kind == OUT_F32) static_cast<float*>(st.out)[off] = x;
-      else if (st.out_kind == OUT_F16)
+      else if (st.out_kind == OUT_F16) {
+        if (f16_out_of_range(x)) flag_range(p.err);  // reported, never silent
         static_cast<__half*>(st.out)[off] = __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f));
+      }
       else static_cast<__nv_bfloat16*>(st.out)[off] = __float2bfloat16(x);
     }
   }

@@ -385,4 +385,14 @@ SVD_DEV uint32_t pack_f16x2_sat(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// True when v cannot be stored as a finite fp16 without saturating: |v| above
+// the largest finite fp16, or NaN (the comparison is false for NaN).
+SVD_DEV bool f16_out_of_range(float v) { return !(fabsf(v) <= 65504.0f); }
+
+// Word 1 of the device error block: set to 1 when an fp16 intermediate (or
+// an fp16-packed weight) had to be saturated.  Word 0 holds the wait-timeout
+// site.  The host reads both back (svdmlp_check_device_status).
+constexpr int kRangeWord = 1;
+SVD_DEV void flag_range(int* err) { atomicOr(err + kRangeWord, 1); }
+
 }  // namespace svdmlp

@@ -533,6 +533,7 @@ struct Workspace {
 };
 
 static constexpr int64_t kCtlBytes = 256;
+static constexpr int64_t kPackStatusBytes = 256;  // trailing block of a packed layer (its status word)
 // Split-K arrival counters: a fixed 1 MiB region (262144 tiles) right after
 // the control block, so that every entry point and layout carves it at the
 // same place and svdmlp_workspace_init zeroes exactly it.
@@ -825,6 +826,16 @@ SVD_DEV bf16 from_float<bf16>(float v) { return __float2bfloat16(v); }
 template <>
 SVD_DEV __half from_float<__half>(float v) { return __float2half_rn(fminf(fmaxf(v, -65504.f), 65504.f)); }
 
+// Conversion to the stored type that also reports values fp16 cannot hold
+// (|v| > 65504 or NaN) in `*range`: they are saturated, never silently.
+template <typename TO>
+SVD_DEV TO checked_from_float(float v, int* range) {
+  if constexpr (std::is_same<TO, __half>::value) {
+    if (range != nullptr && f16_out_of_range(v)) atomicOr(range, 1);
+  }
+  return from_float<TO>(v);
+}
+
 // dst[i][j] = src[j][i] (bf16 in, bf16 or fp16 out); zero outside the source.
 template <typename TO>
 __global__ void transpose_pack_kernel(const bf16* __restrict__ src, long long ld_src, int rows, int cols,
@@ -850,7 +861,7 @@ __global__ void transpose_pack_kernel(const bf16* __restrict__ src, long long ld
 // the destination; destination columns k >= rows are written as zero.
 template <typename TO>
 __global__ void tiled_pack_kernel(const bf16* __restrict__ src, long long ld_src, int rows, int cols,
-                                  TO* __restrict__ dst, int row0, int kb_count) {
+                                  TO* __restrict__ dst, int row0, int kb_count, int* range) {
   __shared__ float tile[32][33];
   const int k0 = blockIdx.x * 32;  // destination column (k) == source row
   const int n0 = blockIdx.y * 32;  // destination row offset within [0, cols)
@@ -864,7 +875,7 @@ __global__ void tiled_pack_kernel(const bf16* __restrict__ src, long long ld_src
     if (n < cols && k < kb_count * 64) {
       const int gn = row0 + n;
       const long long off = (static_cast<long long>(gn / 16) * kb_count + k / 64) * 1024 + (gn % 16) * 64 + (k % 64);
-      dst[off] = from_float<TO>(tile[threadIdx.x][y]);
+      dst[off] = checked_from_float<TO>(tile[threadIdx.x][y], range);
     }
   }
 }
@@ -872,7 +883,7 @@ __global__ void tiled_pack_kernel(const bf16* __restrict__ src, long long ld_src
 // 2-D element-wise conversion with leading dimensions (fp32 -> fp16, bf16 -> fp16).
 template <typename TI, typename TO>
 __global__ void convert_kernel(const TI* __restrict__ src, long long ld_src, TO* __restrict__ dst, long long ld_dst,
-                               int rows, int cols) {
+                               int rows, int cols, int* range) {
   const long long total = static_cast<long long>(rows) * cols;
   for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<long long>(gridDim.x) * blockDim.x) {
@@ -880,7 +891,7 @@ __global__ void convert_kernel(const TI* __restrict__ src, long long ld_src, TO*
     float v;
     if constexpr (std::is_same<TI, float>::value) v = src[r * ld_src + c];
     else v = __bfloat162float(src[r * ld_src + c]);
-    dst[r * ld_dst + c] = from_float<TO>(v);
+    dst[r * ld_dst + c] = checked_from_float<TO>(v, range);
   }
 }
 
@@ -925,11 +936,11 @@ __global__ void wait_probe_kernel(int* err, unsigned long long limit_ns) {
 }
 
 template <typename TI, typename TO>
-static int launch_convert(const TI* src, int64_t ld_src, TO* dst, int64_t ld_dst, int rows, int cols,
+static int launch_convert(const TI* src, int64_t ld_src, TO* dst, int64_t ld_dst, int rows, int cols, int* range,
                           cudaStream_t s) {
   const int64_t total = static_cast<int64_t>(rows) * cols;
   const unsigned blocks = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(cdiv(total, 256), 148 * 16)));
-  convert_kernel<TI, TO><<<blocks, 256, 0, s>>>(src, ld_src, dst, ld_dst, rows, cols);
+  convert_kernel<TI, TO><<<blocks, 256, 0, s>>>(src, ld_src, dst, ld_dst, rows, cols, range);
   SVD_CUDA(cudaGetLastError());
   g_launches.fetch_add(1);
   return SVDMLP_OK;
@@ -937,12 +948,12 @@ static int launch_convert(const TI* src, int64_t ld_src, TO* dst, int64_t ld_dst
 
 template <typename TO>
 static int launch_tiled_pack(const void* src, int64_t ld_src, int rows, int cols, void* dst, int row0, int64_t k,
-                             cudaStream_t s) {
+                             int* range, cudaStream_t s) {
   if (!src || !dst || rows <= 0 || cols <= 0 || ld_src < cols || row0 % 16 != 0) return SVDMLP_ERR_INVALID_VALUE;
   const int kb = static_cast<int>(cdiv(k, 64));
   dim3 grid(static_cast<unsigned>(cdiv(static_cast<int64_t>(kb) * 64, 32)), static_cast<unsigned>(cdiv(cols, 32)));
   tiled_pack_kernel<TO><<<grid, dim3(32, 8), 0, s>>>(static_cast<const bf16*>(src), ld_src, rows, cols,
-                                                     static_cast<TO*>(dst), row0, kb);
+                                                     static_cast<TO*>(dst), row0, kb, range);
   SVD_CUDA(cudaGetLastError());
   g_launches.fetch_add(1);
   return SVDMLP_OK;
@@ -1343,6 +1354,9 @@ const char* svdmlp_status_string(int status) {
     case SVDMLP_ERR_CUDA: return "CUDA error";
     case SVDMLP_ERR_BUDGET: return "SMEM/TMEM budget exceeds the device";
     case SVDMLP_ERR_DEVICE: return "device is not an sm_100 (B200) GPU";
+    case SVDMLP_ERR_RANGE:
+      return "value out of fp16 range: an intermediate or an fp16-packed weight exceeded 65504 (or was NaN) and was "
+             "saturated";
     default: return "unknown status";
   }
 }
@@ -1375,6 +1389,7 @@ int svdmlp_layout_init(svdmlp_layout* L, int d, int ff, int r_gu, int r_d) {
   L->off_vu = take(tiled_bytes(ff, r_gu));
   L->off_ud = take(tiled_bytes(r_d, ff));             // [r_d, ff]
   L->off_vd = take(tiled_bytes(d, r_d));              // [d, r_d]
+  L->off_status = take(kPackStatusBytes);             // pack status word (fp16 range)
   L->packed_bytes = off;
   return SVDMLP_OK;
 }
@@ -1397,6 +1412,7 @@ int svdmlp_dense_layout_init(svdmlp_layout* L, int d, int ff) {
   L->off_vg = take(tiled_bytes(ff, d));  // [ff, d]
   L->off_vu = take(tiled_bytes(ff, d));
   L->off_ud = take(tiled_bytes(d, ff));  // [d, ff]
+  L->off_status = take(kPackStatusBytes);
   L->packed_bytes = off;
   return SVDMLP_OK;
 }
@@ -1416,23 +1432,24 @@ int svdmlp_pack(const svdmlp_layout* L, const void* u_gate, int64_t ld_ug, const
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* P = static_cast<uint8_t*>(packed);
   SVD_CUDA(cudaMemsetAsync(P, 0, static_cast<size_t>(L->packed_bytes), s));
+  int* range = reinterpret_cast<int*>(P + L->off_status);  // set if an fp16-packed weight saturates
   if (L->r_gu > 0) {
     if (!u_gate || !v_gate || !u_up || !v_up) return SVDMLP_ERR_INVALID_VALUE;
     // w1 [2*rp_gu, d] (bf16: it multiplies the bf16 input X): u_gate^T, then u_up^T
-    SVD_CHECK(launch_tiled_pack<bf16>(u_gate, ld_ug, L->d, L->r_gu, P + L->off_w1, 0, L->d, s));
-    SVD_CHECK(launch_tiled_pack<bf16>(u_up, ld_uu, L->d, L->r_gu, P + L->off_w1, L->rp_gu, L->d, s));
+    SVD_CHECK(launch_tiled_pack<bf16>(u_gate, ld_ug, L->d, L->r_gu, P + L->off_w1, 0, L->d, range, s));
+    SVD_CHECK(launch_tiled_pack<bf16>(u_up, ld_uu, L->d, L->r_gu, P + L->off_w1, L->rp_gu, L->d, range, s));
     // v [r, ff] -> v^T [ff, r] (fp16: it multiplies the fp16 XU)
-    SVD_CHECK(launch_tiled_pack<__half>(v_gate, ld_vg, L->r_gu, L->ff, P + L->off_vg, 0, L->r_gu, s));
-    SVD_CHECK(launch_tiled_pack<__half>(v_up, ld_vu, L->r_gu, L->ff, P + L->off_vu, 0, L->r_gu, s));
+    SVD_CHECK(launch_tiled_pack<__half>(v_gate, ld_vg, L->r_gu, L->ff, P + L->off_vg, 0, L->r_gu, range, s));
+    SVD_CHECK(launch_tiled_pack<__half>(v_up, ld_vu, L->r_gu, L->ff, P + L->off_vu, 0, L->r_gu, range, s));
   }
   if (L->r_d > 0) {
     if (!u_down || !v_down) return SVDMLP_ERR_INVALID_VALUE;
     // u_down [ff, r_d] -> [r_d, ff];  v_down [r_d, d] -> [d, r_d]
     if (L->ud_f16)
-      SVD_CHECK(launch_tiled_pack<__half>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, 0, L->ff, s));
+      SVD_CHECK(launch_tiled_pack<__half>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, 0, L->ff, range, s));
     else
-      SVD_CHECK(launch_tiled_pack<bf16>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, 0, L->ff, s));
-    SVD_CHECK(launch_tiled_pack<__half>(v_down, ld_vd, L->r_d, L->d, P + L->off_vd, 0, L->r_d, s));
+      SVD_CHECK(launch_tiled_pack<bf16>(u_down, ld_ud, L->ff, L->r_d, P + L->off_ud, 0, L->ff, range, s));
+    SVD_CHECK(launch_tiled_pack<__half>(v_down, ld_vd, L->r_d, L->d, P + L->off_vd, 0, L->r_d, range, s));
   }
   return SVDMLP_OK;
 }
@@ -1445,9 +1462,10 @@ int svdmlp_dense_pack(const svdmlp_layout* L, const void* w_gate, int64_t ld_wg,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   uint8_t* P = static_cast<uint8_t*>(packed);
   SVD_CUDA(cudaMemsetAsync(P, 0, static_cast<size_t>(L->packed_bytes), s));
-  SVD_CHECK(launch_tiled_pack<bf16>(w_gate, ld_wg, L->d, L->ff, P + L->off_vg, 0, L->d, s));
-  SVD_CHECK(launch_tiled_pack<bf16>(w_up, ld_wu, L->d, L->ff, P + L->off_vu, 0, L->d, s));
-  SVD_CHECK(launch_tiled_pack<__half>(w_down, ld_wd, L->ff, L->d, P + L->off_ud, 0, L->ff, s));
+  int* range = reinterpret_cast<int*>(P + L->off_status);
+  SVD_CHECK(launch_tiled_pack<bf16>(w_gate, ld_wg, L->d, L->ff, P + L->off_vg, 0, L->d, range, s));
+  SVD_CHECK(launch_tiled_pack<bf16>(w_up, ld_wu, L->d, L->ff, P + L->off_vu, 0, L->d, range, s));
+  SVD_CHECK(launch_tiled_pack<__half>(w_down, ld_wd, L->ff, L->d, P + L->off_ud, 0, L->ff, range, s));
   return SVDMLP_OK;
 }
 
@@ -1464,18 +1482,43 @@ int svdmlp_workspace_init(void* ws, int64_t ws_bytes, void* stream) {
   return SVDMLP_OK;
 }
 
+// Reads the two words of a device error block (wait-timeout site, fp16 range
+// flag) after the stream has drained; a set word maps to its status.
+static int read_error_block(const void* block, cudaStream_t s, int* status) {
+  SVD_CUDA(cudaStreamSynchronize(s));
+  int words[2] = {0, 0};
+  SVD_CUDA(cudaMemcpyAsync(words, block, sizeof(words), cudaMemcpyDeviceToHost, s));
+  SVD_CUDA(cudaStreamSynchronize(s));
+  *status = words[0] != 0 ? SVDMLP_ERR_DEVICE_TIMEOUT : words[1] != 0 ? SVDMLP_ERR_RANGE : SVDMLP_OK;
+  return SVDMLP_OK;
+}
+
 int svdmlp_check_device_status(void* ws, int64_t ws_bytes, void* stream) {
   if (!ws || ws_bytes < kCtlBytes) return SVDMLP_ERR_INVALID_VALUE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  SVD_CUDA(cudaStreamSynchronize(s));
-  int err = 0;
-  SVD_CUDA(cudaMemcpy(&err, ws, sizeof(int), cudaMemcpyDeviceToHost));
-  if (err != 0) {
+  int status = SVDMLP_OK;
+  SVD_CHECK(read_error_block(ws, s, &status));
+  if (status == SVDMLP_ERR_DEVICE_TIMEOUT) {
+    // a wait that gave up may leave counters behind: clear the whole block
     SVD_CHECK(svdmlp_workspace_init(ws, ws_bytes, stream));
     SVD_CUDA(cudaStreamSynchronize(s));
-    return SVDMLP_ERR_DEVICE_TIMEOUT;
+  } else if (status == SVDMLP_ERR_RANGE) {
+    SVD_CUDA(cudaMemsetAsync(static_cast<int*>(ws) + kRangeWord, 0, sizeof(int), s));
+    SVD_CUDA(cudaStreamSynchronize(s));
   }
-  return SVDMLP_OK;
+  return status;
+}
+
+int svdmlp_pack_status(const svdmlp_layout* L, const void* packed, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (!packed) return SVDMLP_ERR_INVALID_VALUE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SVD_CUDA(cudaStreamSynchronize(s));
+  int word = 0;
+  SVD_CUDA(cudaMemcpyAsync(&word, static_cast<const uint8_t*>(packed) + L->off_status, sizeof(int),
+                           cudaMemcpyDeviceToHost, s));
+  SVD_CUDA(cudaStreamSynchronize(s));
+  return word != 0 ? SVDMLP_ERR_RANGE : SVDMLP_OK;
 }
 
 int svdmlp_gate_up(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* h,
@@ -1498,7 +1541,7 @@ int svdmlp_gate_up(const svdmlp_layout* L, const void* packed, const void* x, in
 static int stage_h(const svdmlp_layout* L, const void* h, int64_t ldh, int M, const Workspace& w, const void** ha,
                    int64_t* ldha, cudaStream_t s) {
   if (L->ud_f16) {
-    SVD_CHECK(launch_convert<bf16, __half>(static_cast<const bf16*>(h), ldh, w.h, L->ld_ff, M, L->ff, s));
+    SVD_CHECK(launch_convert<bf16, __half>(static_cast<const bf16*>(h), ldh, w.h, L->ld_ff, M, L->ff, w.err + kRangeWord, s));
     *ha = w.h;
     *ldha = L->ld_ff;
     return SVDMLP_OK;
@@ -1714,7 +1757,7 @@ int svdmlp_down_finish(const svdmlp_layout* L, const void* packed, const float* 
   Workspace w{};
   SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  SVD_CHECK(launch_convert<float, __half>(partial, ldp, w.t, L->rp_d, M, L->r_d, s));
+  SVD_CHECK(launch_convert<float, __half>(partial, ldp, w.t, L->rp_d, M, L->r_d, w.err + kRangeWord, s));
   const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
   const void* res = nullptr;
   int64_t ldr = 0;
@@ -1911,13 +1954,86 @@ int svdmlp_xuv_noalloc(const svdmlp_layout* L, const void* packed, const void* h
   const void* ha = h;
   int64_t ldha = ldh;
   if (L->ud_f16) {
-    SVD_CHECK(launch_convert<bf16, __half>(static_cast<const bf16*>(h), ldh, w.h, L->ld_ff, M, L->ff, s));
+    SVD_CHECK(launch_convert<bf16, __half>(static_cast<const bf16*>(h), ldh, w.h, L->ld_ff, M, L->ff, w.err + kRangeWord, s));
     ha = w.h;
     ldha = L->ld_ff;
   }
   const uint8_t* P = static_cast<const uint8_t*>(packed);
   SVD_CHECK(run_down_u(L, P, ha, ldha, L->ud_f16 != 0, M, nullptr, 0, w, s));
   return run_down_v(L, P, M, y, ldy, nullptr, 0, w, s);
+}
+
+int svdmlp_xuv_noalloc_status(void* stream) {
+  void* base = nullptr;
+  SVD_CHECK(static_scratch_address(&base));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int status = SVDMLP_OK;
+  SVD_CHECK(read_error_block(base, s, &status));
+  if (status != SVDMLP_OK) {
+    // both words; the counters are cleared by the next call's own reset
+    SVD_CUDA(cudaMemsetAsync(base, 0, 2 * sizeof(int), s));
+    SVD_CUDA(cudaStreamSynchronize(s));
+  }
+  return status;
+}
+
+}  // extern "C"
+
+// Compile-time resources of the kernel configuration a stage runs with at M
+// tokens (the per-stage kernels; M <= 128 uses the swapped-operand decode
+// set for its token tile).
+namespace svdmlp {
+template <class Cfg>
+static void pair_tile_info(int* o) {
+  o[0] = Cfg::TILE_M;
+  o[1] = Cfg::EPI == EPI_DUAL_STORE ? 2 * Cfg::BN : Cfg::BN;
+  o[2] = Cfg::BK;
+  o[3] = Cfg::STAGES;
+  o[4] = Cfg::SMEM_BYTES;
+  o[5] = static_cast<int>(Cfg::TMEM_COLS);
+  o[6] = Cfg::THREADS;
+  o[7] = Cfg::CTAS;
+}
+template <class Cfg>
+static void dec_tile_info(int* o) {
+  o[0] = Cfg::TOK;
+  o[1] = Cfg::BM;
+  o[2] = Cfg::BK;
+  o[3] = Cfg::STAGES;
+  o[4] = Cfg::SMEM_BYTES;
+  o[5] = static_cast<int>(Cfg::TMEM_COLS);
+  o[6] = 192;
+  o[7] = 1;
+}
+template <class Set>
+static void dec_set_info(int stage, int* o) {
+  if (stage == ST_XU) dec_tile_info<typename Set::XU>(o);
+  else if (stage == ST_GATEUP) dec_tile_info<typename Set::GU>(o);
+  else if (stage == ST_DOWN_U) dec_tile_info<typename Set::DU>(o);
+  else dec_tile_info<typename Set::DV>(o);
+}
+}  // namespace svdmlp
+
+extern "C" {
+
+int svdmlp_tile_info(int stage, int M, int* out8) {
+  if (!out8 || M <= 0 || stage < 0 || stage > ST_GEMM) return SVDMLP_ERR_INVALID_VALUE;
+  const bool pair = M >= g_pair_min_m;
+  switch (stage) {
+    case ST_XU: pair ? pair_tile_info<CfgXUd>(out8) : void(); break;
+    case ST_GATEUP: pair ? pair_tile_info<CfgGU>(out8) : void(); break;
+    case ST_DOWN_U: pair ? pair_tile_info<CfgDU>(out8) : void(); break;
+    case ST_DOWN_V: pair ? pair_tile_info<CfgDV>(out8) : void(); break;
+    case ST_DENSE_GU: pair ? pair_tile_info<CfgDenseGU>(out8) : pair_tile_info<CfgDenseGU1>(out8); break;
+    case ST_DENSE_D: pair ? pair_tile_info<CfgDV>(out8) : pair_tile_info<CfgDV1>(out8); break;
+    default: pair ? pair_tile_info<CfgGemm>(out8) : pair_tile_info<CfgGemm1>(out8); break;
+  }
+  if (!pair && stage <= ST_DOWN_V) {
+    if (M <= 16) dec_set_info<Dec16>(stage, out8);
+    else if (M <= 64) dec_set_info<Dec64>(stage, out8);
+    else dec_set_info<Dec128>(stage, out8);
+  }
+  return SVDMLP_OK;
 }
 
 int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {

@@ -21,6 +21,7 @@ ERR_DEVICE_TIMEOUT = -6
 ERR_CUDA = -7
 ERR_BUDGET = -8
 ERR_DEVICE = -9
+ERR_RANGE = -10
 
 KIND_SVD = 1
 KIND_DENSE = 2
@@ -48,6 +49,7 @@ class Layout(ctypes.Structure):
         ("off_vu", c_int64),
         ("off_ud", c_int64),
         ("off_vd", c_int64),
+        ("off_status", c_int64),
         ("packed_bytes", c_int64),
     ]
 
@@ -67,6 +69,7 @@ SIGNATURES = {
     "svdmlp_workspace_bytes": (c_int64, [LP, c_int]),
     "svdmlp_workspace_init": (c_int, [V, I64, V]),
     "svdmlp_check_device_status": (c_int, [V, I64, V]),
+    "svdmlp_pack_status": (c_int, [LP, V, V]),
     "svdmlp_gate_up": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_xuv": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_forward": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
@@ -79,6 +82,7 @@ SIGNATURES = {
     "svdmlp_xu_project": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_partial_from_xu_f16": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_xuv_noalloc": (c_int, [LP, V, V, I64, c_int, V, I64, V]),
+    "svdmlp_xuv_noalloc_status": (c_int, [V]),
     "svdmlp_gemm": (c_int, [V, I64, V, I64, V, I64, c_int, c_int, c_int, V, I64, V]),
     "svdmlp_gemm_workspace_bytes": (c_int64, [c_int, c_int, c_int]),
     "svdmlp_transpose_pack": (c_int, [V, I64, c_int, c_int, V, I64, c_int, c_int, V]),
@@ -92,6 +96,7 @@ SIGNATURES = {
     "svdmlp_set_prefill_chain": (c_int, [c_int]),
     "svdmlp_set_trace_buffer": (c_int, [V, I64]),
     "svdmlp_plan_info": (c_int, [c_int, c_int, c_int, c_int, POINTER(c_int)]),
+    "svdmlp_tile_info": (c_int, [c_int, c_int, POINTER(c_int)]),
     "svdmlp_stage_timing": (c_int, [c_int]),
     "svdmlp_stage_times": (c_int, [POINTER(ctypes.c_double), POINTER(c_int64), c_int]),
     "svdmlp_launch_count": (c_int64, []),
@@ -133,6 +138,11 @@ class SvdMlpError(RuntimeError):
     """A device-side or CUDA failure reported by the library."""
 
 
+class SvdMlpRangeError(SvdMlpError, FloatingPointError):
+    """An fp16 intermediate (or an fp16-packed weight) exceeded 65504 or was
+    NaN and was saturated: the result of that call is not trustworthy."""
+
+
 def check(status: int, what: str = "") -> None:
     """Maps a C-ABI status to the exception types the reference raises."""
     if status == OK:
@@ -147,4 +157,6 @@ def check(status: int, what: str = "") -> None:
         raise ValueError(msg)
     if status == ERR_DTYPE:
         raise TypeError(msg)
+    if status == ERR_RANGE:
+        raise SvdMlpRangeError(msg)
     raise SvdMlpError(msg)

@@ -40,8 +40,8 @@ __all__ = [
     "PackedLayer", "pack_svd_layer", "pack_dense_layer", "low_rank_dim", "rank_for_ratio", "silu",
     "fused_gate_up", "fused_xuv", "xuv_matmul", "svd_mlp", "contracted_svd_mlp", "dense_mlp",
     "dense_matmul", "svd_mlp_packed", "dense_mlp_packed", "gate_up_packed", "xuv_packed",
-    "forward_partial_packed", "down_finish_packed", "rmsnorm", "workspace_for", "check_device_status",
-    "launch_count",
+    "forward_partial_packed", "down_partial_packed", "down_finish_packed", "rmsnorm", "workspace_for",
+    "check_device_status", "launch_count",
 ]
 
 
@@ -147,7 +147,9 @@ def workspace_for(device: torch.device, nbytes: int) -> _Workspace:
 
 
 def check_device_status(device: Optional[torch.device] = None) -> None:
-    """Synchronises and raises if a bounded device wait expired on any pooled workspace."""
+    """Synchronises and raises if a bounded device wait expired (SvdMlpError) or
+    an fp16 intermediate saturated (SvdMlpRangeError) on any pooled workspace
+    since the last check."""
     lib = _lib.load()
     with _ws_lock:
         items = list(_ws_pool.items())
@@ -226,6 +228,8 @@ def pack_svd_layer(u_gate=None, v_gate=None, u_up=None, v_up=None, u_down=None, 
     for a in bf:
         args += [_ptr(a), 0 if a is None else _ld(a)]
     _lib.check(lib.svdmlp_pack(ctypes.byref(layout), *args, packed.data_ptr(), _stream(dev)), "pack")
+    # packing is a set-up step: synchronise once to refuse weights fp16 cannot hold
+    _lib.check(lib.svdmlp_pack_status(ctypes.byref(layout), packed.data_ptr(), _stream(dev)), "pack")
     return PackedLayer(layout, packed)
 
 
@@ -245,6 +249,7 @@ def pack_dense_layer(w_gate, w_up, w_down) -> PackedLayer:
     wg, wu, wd = (_bf16(a).contiguous() for a in (w_gate, w_up, w_down))
     _lib.check(lib.svdmlp_dense_pack(ctypes.byref(layout), wg.data_ptr(), _ld(wg), wu.data_ptr(), _ld(wu),
                                      wd.data_ptr(), _ld(wd), packed.data_ptr(), _stream(dev)), "dense_pack")
+    _lib.check(lib.svdmlp_pack_status(ctypes.byref(layout), packed.data_ptr(), _stream(dev)), "dense_pack")
     return PackedLayer(layout, packed)
 
 
@@ -384,6 +389,26 @@ def forward_partial_packed(layer: PackedLayer, x: torch.Tensor, partial: Optiona
     return partial
 
 
+def down_partial_packed(layer: PackedLayer, h: torch.Tensor, partial: Optional[torch.Tensor] = None):
+    """First half of the down operator on an ff-shard: the fp32 [M, r_d]
+    partial h . u_down (h: bf16 [M, ff_shard]), the rank-local term that the
+    tensor-parallel layer all-reduces before down_finish_packed."""
+    if layer.kind != _lib.KIND_SVD or layer.r_d == 0:
+        raise ValueError("down_partial needs down factors")
+    hb = _prep_x(h, layer.ff)
+    m = hb.shape[0]
+    if partial is None:
+        partial = torch.empty((m, layer.r_d + (-layer.r_d) % 4), dtype=torch.float32,
+                              device=hb.device)[:, :layer.r_d]
+    if partial.dtype != torch.float32:
+        raise TypeError("the partial must be fp32 (supported dtypes)")
+    ws = layer.workspace(m)
+    _lib.check(_lib.load().svdmlp_down_partial(
+        ctypes.byref(layer.layout), layer.packed.data_ptr(), hb.data_ptr(), _ld(hb), m, partial.data_ptr(),
+        partial.stride(0), ws.ptr, ws.nbytes, _stream(hb.device)), "down_partial")
+    return partial
+
+
 def xu_project_packed(layer: PackedLayer, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Stage 1 alone: XU = x . [u_g|u_u], fp16 [M, 2*rp_gu] (the layout stages 2-3 read)."""
     xb = _prep_x(x, layer.d)
@@ -447,18 +472,46 @@ def _finish(y: torch.Tensor, x: torch.Tensor) -> torch.Tensor:
     return y if x.dtype == torch.bfloat16 else y.to(x.dtype)
 
 
+class _GateUpSplits:
+    """Applies a block request's split-K count to the SwiGLU GEMM (stage 1)
+    for the duration of one call; tile shapes are compile-time on B200."""
+
+    _lock = threading.Lock()
+
+    def __init__(self, blocks):
+        self.splits = 0
+        if blocks is not None:
+            from . import config
+            blocks = tuple(blocks)
+            config.check_gate_up_blocks(config.GateUpBlocks(*blocks))
+            self.splits = int(blocks[4]) if len(blocks) > 4 else 0
+
+    def __enter__(self):
+        if self.splits:
+            self._lock.acquire()
+            _lib.check(_lib.load().svdmlp_set_split_override(_lib.STAGE_GATE_UP, self.splits), "split override")
+        return self
+
+    def __exit__(self, *exc):
+        if self.splits:
+            _lib.load().svdmlp_set_split_override(_lib.STAGE_GATE_UP, 0)
+            self._lock.release()
+        return False
+
+
 def fused_gate_up(x, u_gate, v_gate, u_up, v_up, *, blocks=None, mixed_precision=True, interpret=False):
     """[S, I] = silu(X.Ug.Vg) * (X.Uu.Vu) (kernels/reference.py:54-72;
-    pallas_ops.fused_gate_up, bench/smoke.py:81-83)."""
+    pallas_ops.fused_gate_up, bench/smoke.py:81-83).  `blocks` (a
+    config.GateUpBlocks) is checked against the on-chip budget; its `splits`
+    sets the SwiGLU GEMM's split-K count for this call."""
     _validate_arrays(x, u_gate, v_gate, u_up, v_up)
     _check_modes(mixed_precision, interpret, x.dtype)
-    if blocks is not None:
-        for name, value in zip(("bs", "bh", "br", "bn"), tuple(blocks)):
-            _positive(name, int(value))
+    guard = _GateUpSplits(blocks)
     if x.shape[1] != u_gate.shape[0]:
         raise ValueError("x/u_gate contraction dimensions do not match")
     layer = _cache.get("gu", (u_gate, v_gate, u_up, v_up), lambda: pack_svd_layer(u_gate, v_gate, u_up, v_up))
-    return _finish(gate_up_packed(layer, x), x)
+    with guard:
+        return _finish(gate_up_packed(layer, x), x)
 
 
 def xuv_matmul(x, u, v, *, mixed_precision=True, interpret=False):
@@ -481,14 +534,13 @@ def svd_mlp(x, u_gate, v_gate, u_up, v_up, u_down, v_down, *, gate_up_blocks=Non
     bench/latency.py:402-404, models/modeling_llama.py:851-862)."""
     _validate_arrays(x, u_gate, v_gate, u_up, v_up, u_down, v_down)
     _check_modes(mixed_precision, interpret, x.dtype)
-    if gate_up_blocks is not None:
-        for name, value in zip(("bs", "bh", "br", "bn"), tuple(gate_up_blocks)):
-            _positive(name, int(value))
+    guard = _GateUpSplits(gate_up_blocks)
     if x.shape[1] != u_gate.shape[0]:
         raise ValueError("x/u_gate contraction dimensions do not match")
     layer = _cache.get("svd", (u_gate, v_gate, u_up, v_up, u_down, v_down),
                        lambda: pack_svd_layer(u_gate, v_gate, u_up, v_up, u_down, v_down))
-    return _finish(svd_mlp_packed(layer, x, residual=residual), x)
+    with guard:
+        return _finish(svd_mlp_packed(layer, x, residual=residual), x)
 
 
 def contracted_svd_mlp(x, u_gate, v_gate, u_up, v_up, u_down, v_down, *, gate_up_blocks=None,

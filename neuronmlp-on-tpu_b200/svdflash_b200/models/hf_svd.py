@@ -31,21 +31,27 @@ FACTOR_SUFFIXES = (
 
 _DTYPES = {"BF16": torch.bfloat16, "F32": torch.float32}
 
+__all__ = ["FACTOR_SUFFIXES", "checkpoint_metadata", "factor_keys", "validate_factor_shapes",
+           "inspect_mlp_checkpoint", "load_mlp_factors", "load_svd_mlps"]
+
+
+def _read_json(path: Path, what: str) -> dict:
+    if not path.is_file():
+        raise FileNotFoundError(f"missing {what}: {path}")
+    return json.loads(path.read_text(encoding="utf-8"))
+
 
 def checkpoint_metadata(model_path: str | Path) -> tuple[dict, dict]:
-    """Reads and minimally validates config.json and the safetensors index."""
-    model_path = Path(model_path)
-    config_path = model_path / "config.json"
-    index_path = model_path / "model.safetensors.index.json"
-    if not config_path.is_file():
-        raise FileNotFoundError(f"missing checkpoint config: {config_path}")
-    if not index_path.is_file():
-        raise FileNotFoundError(f"missing safetensors index: {index_path}")
-    config = json.loads(config_path.read_text(encoding="utf-8"))
-    index = json.loads(index_path.read_text(encoding="utf-8"))
-    if "weight_map" not in index:
-        raise ValueError(f"safetensors index has no weight_map: {index_path}")
-    return config, index
+    """(config.json, model.safetensors.index.json) of a checkpoint directory;
+    the index must carry a weight_map (the reference's checks and errors,
+    models/hf_svd.py:23-37)."""
+    root = Path(model_path)
+    config = _read_json(root / "config.json", "checkpoint config")
+    index_path = root / "model.safetensors.index.json"
+    index = _read_json(index_path, "safetensors index")
+    if "weight_map" in index:
+        return config, index
+    raise ValueError(f"safetensors index has no weight_map: {index_path}")
 
 
 def factor_keys(layer_index: int) -> tuple[str, ...]:
@@ -61,19 +67,22 @@ def _check_mlp_config(config: dict) -> None:
 
 
 def validate_factor_shapes(factors: Sequence, *, hidden_size: int, intermediate_size: int) -> int:
-    """Checks the orientation after the transpose and returns the rank."""
+    """Checks that six transposed factors chain as [d, r] [r, ff] [d, r]
+    [r, ff] [ff, r] [r, d] with one dtype, and returns r (the reference's
+    checks and errors, models/hf_svd.py:47-74)."""
     if len(factors) != 6:
         raise ValueError(f"expected six MLP factors, got {len(factors)}")
-    rank = int(factors[0].shape[1])
-    expected = ((hidden_size, rank), (rank, intermediate_size), (hidden_size, rank), (rank, intermediate_size),
-                (intermediate_size, rank), (rank, hidden_size))
-    actual = tuple(tuple(int(v) for v in f.shape) for f in factors)
-    if actual != expected:
-        raise ValueError(f"invalid transposed MLP factor shapes; expected {expected}, got {actual}")
-    dtypes = {f.dtype for f in factors}
-    if len(dtypes) != 1:
-        raise TypeError(f"MLP factor dtypes differ: {sorted(map(str, dtypes))}")
-    return rank
+    shapes = [tuple(int(n) for n in f.shape) for f in factors]
+    r = shapes[0][1]
+    d, ff = hidden_size, intermediate_size
+    # (rows, cols) of each factor in operator order: a pair chains in -> r -> out
+    want = [(d, r), (r, ff)] * 2 + [(ff, r), (r, d)]
+    if shapes != want:
+        raise ValueError(f"invalid transposed MLP factor shapes; expected {tuple(want)}, got {tuple(shapes)}")
+    kinds = sorted({str(f.dtype) for f in factors})
+    if len(kinds) > 1:
+        raise TypeError(f"MLP factor dtypes differ: {kinds}")
+    return r
 
 
 def _selected(config: dict, layer_indices: Optional[Sequence[int]]) -> tuple[int, ...]:

@@ -110,8 +110,13 @@ class TensorParallelSvdMlp:
             return self.forward(x_rows, residual=residual, out=out)
         m = x_rows.shape[0] * self.world
         if self._use_split(m, x_rows.shape[1]):
-            return gather_rows_forward(lambda x, residual=None: self._forward_split(x, residual, None, own_rows=True),
-                                       x_rows, self.rank, self.world, self.group, residual, out, returns_rows=True)
+            # The split mode only ever reads this rank's rows of X and of the
+            # residual: no all-gather of either, only of XU.
+            y_p = self._split_rows(x_rows, residual)
+            if out is None:
+                return y_p
+            out.copy_(y_p)
+            return out
         return gather_rows_forward(self.forward, x_rows, self.rank, self.world, self.group, residual, out)
 
     # "auto": the split pays once the replicated stages outweigh the fixed cost
@@ -124,24 +129,29 @@ class TensorParallelSvdMlp:
             return self.reduce_dtype == torch.float16 and m * d > self.SPLIT_MIN_ELEMENTS
         return self.mode == "split"
 
-    def _forward_split(self, x: torch.Tensor, residual: Optional[torch.Tensor], out: Optional[torch.Tensor],
-                       own_rows: bool = False):
-        m, d = x.shape
-        rows = m // self.world
-        lo, hi = self.rank * rows, (self.rank + 1) * rows
-        dev = x.device
+    def _split_rows(self, x_rows: torch.Tensor, residual_rows: Optional[torch.Tensor]) -> torch.Tensor:
+        """The split mode from this rank's row block of X (and of the residual)
+        to the same rows of y: X.[u_g|u_u] on the block, all-gather XU, stages
+        2-3 of this ff shard on all rows, reduce-scatter the fp16 partial by
+        rows, . v_down (+ residual) on the block."""
+        rows = x_rows.shape[0]
+        m = rows * self.world
+        dev = x_rows.device
         n1 = 2 * self.layer.layout.rp_gu
-        xu_p = ops.xu_project_packed(self.layer, x[lo:hi])
+        xu_p = ops.xu_project_packed(self.layer, x_rows)
         xu = torch.empty((m, n1), dtype=torch.float16, device=dev)
         dist.all_gather_into_tensor(xu, xu_p, group=self.group)
         ops.partial_from_xu_packed(self.layer, xu, self._partial_buffer(m, dev)[:, :self.r_d])
         full = self._partial[:m]
         t_p = torch.empty((rows, full.shape[1]), dtype=torch.float16, device=dev)
         dist.reduce_scatter_tensor(t_p, full, op=dist.ReduceOp.SUM, group=self.group)
-        y_p = ops.down_finish_packed(self.layer, t_p[:, :self.r_d],
-                                     residual=None if residual is None else residual[lo:hi])
-        if own_rows:
-            return y_p  # rows [lo, hi) of y: the caller needs no others
-        y = out if out is not None else torch.empty((m, d), dtype=torch.bfloat16, device=dev)
+        return ops.down_finish_packed(self.layer, t_p[:, :self.r_d], residual=residual_rows)
+
+    def _forward_split(self, x: torch.Tensor, residual: Optional[torch.Tensor], out: Optional[torch.Tensor]):
+        m, d = x.shape
+        rows = m // self.world
+        lo, hi = self.rank * rows, (self.rank + 1) * rows
+        y_p = self._split_rows(x[lo:hi], None if residual is None else residual[lo:hi])
+        y = out if out is not None else torch.empty((m, d), dtype=torch.bfloat16, device=x.device)
         dist.all_gather_into_tensor(y, y_p, group=self.group)
         return y

@@ -49,9 +49,11 @@ def test_layout_sizes(lib):
         return -(-n // 16) * 16 * (-(-k // 64) * 64) * 2
     # w1 [2*rp_gu, d] + vg, vu [ff, r] + ud [r, ff] + vd [d, r]
     expect = tiled(2 * 2880, 4096) + 2 * tiled(14336, 2867) + tiled(2867, 14336) + tiled(4096, 2867)
-    assert L.packed_bytes == pytest.approx(expect, abs=5 * 256)
-    for off in (L.off_w1, L.off_vg, L.off_vu, L.off_ud, L.off_vd):
+    # plus the 256-byte pack status block, each matrix rounded up to 256 bytes
+    assert L.packed_bytes == pytest.approx(expect + 256, abs=5 * 256)
+    for off in (L.off_w1, L.off_vg, L.off_vu, L.off_ud, L.off_vd, L.off_status):
         assert off % 256 == 0
+    assert L.off_status + 256 == L.packed_bytes
     assert lib.svdmlp_workspace_bytes(ctypes.byref(L), 1024) > 0
     D = _lib.Layout()
     assert lib.svdmlp_dense_layout_init(ctypes.byref(D), 129, 137) == 0
@@ -91,8 +93,9 @@ def test_entry_points_reject_bad_arguments(lib):
 
 def test_status_strings(lib):
     from svdflash_b200 import _lib
-    for code in range(0, -10, -1):
-        assert lib.svdmlp_status_string(code)
+    for code in range(0, -11, -1):
+        assert lib.svdmlp_status_string(code) != b"unknown status"
+    assert b"fp16 range" in lib.svdmlp_status_string(_lib.ERR_RANGE)
     assert b"positive" in lib.svdmlp_status_string(_lib.ERR_INVALID_VALUE)
     assert b"SMEM/TMEM budget" in lib.svdmlp_status_string(_lib.ERR_BUDGET)
 
@@ -129,4 +132,8 @@ def test_status_mapping_to_exceptions():
         _lib.check(_lib.ERR_DTYPE)
     with pytest.raises(_lib.SvdMlpError):
         _lib.check(_lib.ERR_DEVICE_TIMEOUT)
+    with pytest.raises(_lib.SvdMlpRangeError):
+        _lib.check(_lib.ERR_RANGE)
+    with pytest.raises(FloatingPointError):
+        _lib.check(_lib.ERR_RANGE)
     _lib.check(_lib.OK)

@@ -56,15 +56,72 @@ def test_rank_formulas():
 
 
 def test_config_tables_and_budget():
-    assert config.MODELS["llama-3.1-8b"]["rank_at_080"] == 2560
-    b = config.gate_up_block_params(1024)
-    assert isinstance(b, config.GateUpBlocks) and b._asdict()["bn"] == config.GATE_UP_BLOCK_N
-    assert b._replace(bn=256).bn == 256
+    m8 = config.MODELS["llama-3.1-8b"]
+    assert isinstance(m8, config.ModelShape) and m8.hidden_size == 4096 and m8.rank_at_080 == 2560
+    assert config.rank_for(m8, 0.9) == config.rank_for("llama-3.1-8b", 0.9) == 2816
+    b = config.gate_up_block_params(1024, m8, 0.9)
+    # the compiled prefill tile: 256-row CTA pairs, 224 ff columns per branch,
+    # 64-wide K blocks; the split count is the library planner's
+    assert isinstance(b, config.GateUpBlocks) and (b.bs, b.bh, b.br, b.bn) == (256, 64, 64, 224)
+    assert b.splits == config.stage_plan(config.STAGE_GATE_UP, 1024, 14336, 2816).splits
+    assert b._replace(bn=256).bn == 256 and set(b._asdict()) == {"bs", "bh", "br", "bn", "splits"}
+    d = config.gate_up_block_params(1, m8, 0.9)   # decode: 16-token tiles over 128-row weight panels
+    assert (d.bs, d.bn) == (16, 128)
+    assert config.gate_up_block_params(100, m8, 0.9).bs == 128
+    t = config.tile_info(config.STAGE_GATE_UP, 1024)
+    assert config.smem_bytes_gate_up() == t.smem_bytes
+    # the layout formula reproduces the compiled kernel's shared memory
+    assert config._pair_smem(t.tile_cols, 2, False, t.stages, 2, 8, 2) == t.smem_bytes
     assert config.fits_smem(config.smem_bytes_gate_up())
     assert config.fits_vmem(config.vmem_bytes_xuv())
     with pytest.raises(ValueError, match="SMEM/TMEM budget exceeds"):
         config.check_budget(config.SMEM_BUDGET_BYTES + 1)
     assert config.tmem_columns_gate_up() <= config.TMEM_COLUMNS
+    # a tile the SM cannot hold is refused with the reference's budget error
+    with pytest.raises(ValueError, match="SMEM/TMEM budget exceeds"):
+        config.check_gate_up_blocks(b._replace(bn=512))
+    with pytest.raises(ValueError, match="positive integer"):
+        config.check_gate_up_blocks(b._replace(bs=0))
+    config.check_gate_up_blocks(b)
+
+
+def test_tuning_candidates_are_real_split_counts():
+    m8 = config.MODELS["llama-3.1-8b"]
+    cands = config.gate_up_tuning_candidates(1024, m8, 0.9)
+    base = config.gate_up_block_params(1024, m8, 0.9)
+    assert cands[0].splits == max(1, base.splits)
+    k_blocks = -(-2816 // 64)
+    assert all(-(-k_blocks // c.splits) >= 8 for c in cands)   # at least 8 k-blocks per CTA-pair split
+    assert len({c.splits for c in cands}) == len(cands) >= 2
+    assert all((c.bs, c.bn) == (base.bs, base.bn) for c in cands)
+    quick = config.gate_up_tuning_candidates(1024, m8, 0.9, profile="quick")
+    assert 1 <= len(quick) <= 3
+
+
+def test_reference_package_facade_exports():
+    """The import lines of the reference's benches and model resolve to the
+    B200 operators (bench/latency.py:23-42, bench/e2e_block.py:40-48,
+    bench/all_mlp_layers.py:21-31, bench/tune.py:20-27)."""
+    from svdflash_tpu.kernels import config as c
+    from svdflash_tpu.kernels.config import (  # noqa: F401
+        MODELS, XUV_INPUT_TILE, XUV_OUTPUT_TILE, XUV_RANK_TILE, XUV_ROW_TILE, GateUpBlocks, ModelShape, fits_vmem,
+        gate_up_block_params, gate_up_tuning_candidates, rank_for, vmem_bytes_gate_up, vmem_bytes_gate_up_down_u,
+        vmem_bytes_xuv)
+    from svdflash_tpu.kernels.pallas_ops import (contracted_svd_mlp, dense_matmul, dense_mlp, fused_gate_up,
+                                                 svd_mlp, xuv_matmul)
+    from svdflash_tpu.kernels.reference import (dense_mlp_ref, fused_gate_up_ref, fused_xuv_ref, low_rank_dim,
+                                                silu, svd_mlp_ref)  # noqa: F401
+    from svdflash_tpu.models.hf_svd import checkpoint_metadata, load_mlp_factors, validate_factor_shapes  # noqa: F401
+    from svdflash_tpu.test_speedup import (_positive, get_fused_mlp_up_T_params,  # noqa: F401
+                                           get_fused_three_mm_XTUV_params, nki_matmul_fully_optimized_,
+                                           svd_mlp_with_fused_kernel)
+    assert svd_mlp is ops.svd_mlp and contracted_svd_mlp is ops.contracted_svd_mlp and c.MODELS is config.MODELS
+    assert fused_gate_up is ops.fused_gate_up and xuv_matmul is ops.xuv_matmul and dense_mlp is ops.dense_mlp
+    assert dense_matmul is ops.dense_matmul and low_rank_dim(4096, 14336, 0.8) == 2560
+    p = get_fused_mlp_up_T_params(1024)
+    assert (p["tile_rows"], p["tile_cols"]) == (256, 224)
+    with pytest.raises(ValueError, match="positive integer"):
+        get_fused_three_mm_XTUV_params(0)
 
 
 def test_silu_helper_matches_formula():

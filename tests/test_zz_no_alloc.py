@@ -83,3 +83,25 @@ def test_noalloc_rejects_sizes_beyond_the_static_scratch(cuda_device):
                                 y.data_ptr(), y.stride(0), _stream(cuda_device))
     assert st == _lib.ERR_WORKSPACE
     assert b"workspace" in lib.svdmlp_status_string(st)
+
+
+def test_noalloc_status_reports_and_clears(cuda_device):
+    """svdmlp_xuv_noalloc_status reads the error block inside the library's
+    static array (the caller has no workspace to pass): OK after a clean
+    call, SVDMLP_ERR_RANGE after a call whose H holds a value fp16 cannot
+    hold (the full-layer layout converts H to fp16), OK again once read."""
+    from svdflash_b200 import _lib
+    from svdflash_b200.kernels import ops
+    lib = _lib.load()
+    m, d, ff, r = 40, 256, 512, 120
+    x, f = orc.make_inputs(95, m, d, ff, r)
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f])
+    hb = orc.bf16_round(orc.fused_gate_up(x, *f[:4]))
+    y = _run_noalloc(lib, layer, to_dev(hb, cuda_device), cuda_device)
+    assert lib.svdmlp_xuv_noalloc_status(_stream(cuda_device)) == _lib.OK
+    assert_close(to_np(y), orc.fused_xuv(hb, f[4], f[5]), what="clean call")
+    bad = hb.copy()
+    bad[7, 11] = 3.0e5
+    _run_noalloc(lib, layer, to_dev(bad, cuda_device), cuda_device)
+    assert lib.svdmlp_xuv_noalloc_status(_stream(cuda_device)) == _lib.ERR_RANGE
+    assert lib.svdmlp_xuv_noalloc_status(_stream(cuda_device)) == _lib.OK
