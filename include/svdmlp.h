@@ -323,6 +323,12 @@ int svdmlp_debug_wait_timeout(void* workspace, int64_t workspace_bytes, int64_t 
  */
 int svdmlp_set_split_override(int stage, int splits);
 
+/* Split tail of the CTA-pair GEMMs (1, the default): when a stage's tiles
+ * fill whole waves of CTA pairs plus a partial last wave, and the planner
+ * leaves the stage unsplit, the last wave's tiles are split over K across the
+ * pairs that wave would leave idle.  0 turns it off (every tile whole). */
+int svdmlp_set_split_tail(int enable);
+
 /* svdmlp_forward runs layers of M <= max_m tokens as one whole-layer decode
  * kernel and larger ones as four per-stage kernels.  max_m = 0 turns the
  * whole-layer kernel off, a negative value restores the default (16, the
@@ -333,7 +339,7 @@ int svdmlp_set_layer_decode(int max_m);
  * shared-memory slots (two 16 KB weight tiles each): `ahead_slots` beyond the
  * slot being loaded while a unit streams, `wait_slots` beyond the slots
  * already loaded while a unit waits for the previous stage.  0 turns a window
- * off; both are at most 64. */
+ * off (the default for both); both are at most 64. */
 int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots);
 
 /* prefetch_units >= 1 (default 1) launches the whole-layer decode kernel with

@@ -92,6 +92,10 @@ struct GemmParams {
   const __nv_bfloat16* residual;  // EPI_RESID: C = acc + residual (bf16)
   long long ld_residual;
   int m_group;       // M-tiles per group of the unit order (m_tiles: one group, m fastest)
+  // Split tail: units [tail_start, num_units) are the last (partial) wave's
+  // tiles split `tail_splits` ways over K (tail_kb_per_split k-blocks each);
+  // units before it follow `splits`.  tail_start == num_units: no split tail.
+  int tail_start, tail_splits, tail_kb_per_split;
   // Chained stages (null: not chained, wait for the whole previous launch).
   const int* dep;    // previous stage's per-M-tile tile counters
   int dep_target;    // count that marks an M-tile of the previous stage complete
@@ -159,6 +163,8 @@ struct GemmCfg {
 
 struct UnitCoord {
   int m_t, n_t, ks, kb0, kb1, tile;
+  int nsplit;  // splits of this unit's tile
+  int pslot;   // partial slot of split 0 of this tile
 };
 
 SVD_DEV UnitCoord decode_unit(const GemmParams& p, int u) {
@@ -166,17 +172,32 @@ SVD_DEV UnitCoord decode_unit(const GemmParams& p, int u) {
   // splits fastest: the units of one tile are consecutive, so the lowest
   // unfinished tile always has every split running or done (the pair split-K
   // fix-up waits for all splits of its tile).
-  c.ks = u % p.splits;
-  const int v = u / p.splits;
+  int v, kbp;
+  if (u < p.tail_start) {
+    c.nsplit = p.splits;
+    c.ks = u % p.splits;
+    v = u / p.splits;
+    kbp = p.kb_per_split;
+    c.pslot = v * p.splits;
+  } else {
+    // the split tail: tiles after the full waves (whose units are unsplit)
+    const int t = u - p.tail_start;
+    c.nsplit = p.tail_splits;
+    c.ks = t % p.tail_splits;
+    v = p.tail_start / p.splits + t / p.tail_splits;
+    kbp = p.tail_kb_per_split;
+    c.pslot = (t / p.tail_splits) * p.tail_splits;
+  }
   const int group_units = p.m_group * p.n_tiles;
   const int g = v / group_units;
   const int gm = min(p.m_group, p.m_tiles - g * p.m_group);  // M-tiles in this (possibly last, short) group
   const int in_g = v - g * group_units;
   c.m_t = g * p.m_group + in_g % gm;
   c.n_t = in_g / gm;
-  c.kb0 = c.ks * p.kb_per_split;
-  c.kb1 = min(c.kb0 + p.kb_per_split, p.k_blocks);
+  c.kb0 = c.ks * kbp;
+  c.kb1 = min(c.kb0 + kbp, p.k_blocks);
   c.tile = c.n_t * p.m_tiles + c.m_t;
+  if (u < p.tail_start) c.pslot = c.tile * p.splits;
   return c;
 }
 
@@ -544,7 +565,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       const int n0 = c.n_t * Cfg::BN;
       const int y_box = row_base + q * 32;
 
-      if (p.splits == 1) {
+      if (c.nsplit == 1) {
 #pragma unroll 1
         for (int ch = half; ch < NCH; ch += CH_STEP) {
           uint32_t rg[32];
@@ -593,7 +614,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         // the counter lets the last one to finish re-arm it.
         const int ctile = c.tile * Cfg::CTAS + static_cast<int>(rank);
         const size_t tile_elems = static_cast<size_t>(Cfg::NB) * (Cfg::BM * Cfg::BN);
-        float* slot = p.partials + static_cast<size_t>((c.tile * p.splits + c.ks) * Cfg::CTAS + rank) * tile_elems;
+        float* slot = p.partials + static_cast<size_t>((c.pslot + c.ks) * Cfg::CTAS + rank) * tile_elems;
         const bool row_ok = grow < p.M;
 #pragma unroll 1
         for (int ch = half; ch < NCH; ch += CH_STEP) {
@@ -624,18 +645,18 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
         named_barrier_sync(1, EPI_THREADS);
         if (threadIdx.x == 0) {
           const int old = atomicAdd(&p.counters[ctile], 1);
-          int go = PAIR ? 1 : (old == p.splits - 1 ? 1 : 0);
-          if (PAIR && !wait_counter_geq(&p.counters[ctile], p.splits, ctx, SITE_DEPENDENCY)) go = 0;
+          int go = PAIR ? 1 : (old == c.nsplit - 1 ? 1 : 0);
+          if (PAIR && !wait_counter_geq(&p.counters[ctile], c.nsplit, ctx, SITE_DEPENDENCY)) go = 0;
           *fix_flag = go;
         }
         named_barrier_sync(1, EPI_THREADS);
         if (*fix_flag) {
           __threadfence();
-          const float* base = p.partials + static_cast<size_t>(c.tile * p.splits * Cfg::CTAS + rank) * tile_elems;
+          const float* base = p.partials + static_cast<size_t>(c.pslot * Cfg::CTAS + rank) * tile_elems;
           const size_t split_stride = static_cast<size_t>(Cfg::CTAS) * tile_elems;
 #pragma unroll 1
           for (int ch = half; ch < NCH; ch += CH_STEP) {
-            if (PAIR && ch % p.splits != c.ks) continue;  // the same for every lane of the warp
+            if (PAIR && ch % c.nsplit != c.ks) continue;  // the same for every lane of the warp
             float v[32], w[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -644,9 +665,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             }
             if (row_ok) {
 #pragma unroll 1
-              for (int s = 0; s < p.splits; s += 2) {
+              for (int s = 0; s < c.nsplit; s += 2) {
                 // two splits' loads in flight per step; the sum order is the split order
-                const bool two = s + 1 < p.splits;
+                const bool two = s + 1 < c.nsplit;
                 const float* src0 = base + static_cast<size_t>(s) * split_stride + ch * (Cfg::BM * 32);
                 const float* src1 = src0 + split_stride;
 #pragma unroll
@@ -676,7 +697,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             if (*fix_flag) p.counters[ctile] = 0;
           } else {
             const int old = atomicAdd(&p.counters[ctile], 1);
-            if (old == 2 * p.splits - 1) p.counters[ctile] = 0;
+            if (old == 2 * c.nsplit - 1) p.counters[ctile] = 0;
           }
         }
       }

@@ -20,8 +20,12 @@
 // M).  Units are claimed dynamically: the producer takes the next unit index
 // from a global counter and passes it to the MMA and epilogue warps through a
 // small shared-memory queue, so busy and idle CTAs even out at every stage
-// boundary; since units are claimed in order, a unit only ever waits on units
-// that running CTAs have already claimed.
+// boundary.  CTA i starts with unit i and claims from the counter after that,
+// so a unit only ever waits on units of the first wave or claimed before it.
+// The grid is at most one CTA per SM, and the launch waits for the previous
+// grid before any unit is taken, so every CTA of the first wave is resident;
+// were one not (another context holding SMs), the bounded dependency wait
+// would end the launch with a timeout status instead of hanging.
 // A shared-memory slot holds two weight tiles and two token tiles: the
 // two branches (gate, up) of one k-block for the dual stage, or two
 // consecutive k-blocks for the other stages.  The split of a tile that
@@ -289,7 +293,11 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
           mbar_arrive(&q_full[qs]);
           break;
         }
-        const int u = atomicAdd(p.next_unit, 1);
+        // The first unit of every CTA is its own index (no atomic: at launch
+        // the claim would queue behind every CTA's weight prefetches); later
+        // units come from the shared counter, in order after the first wave.
+        const int u = qi == 0 ? static_cast<int>(blockIdx.x)
+                              : static_cast<int>(gridDim.x) + atomicAdd(p.next_unit, 1);
         unit_q[qs] = u < p.total_units ? u : -1;
         mbar_arrive(&q_full[qs]);  // release: the unit id is visible to the waiters
         if (u >= p.total_units) break;

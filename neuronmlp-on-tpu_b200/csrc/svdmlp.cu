@@ -33,7 +33,11 @@ static unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s: far above an
 static constexpr int kLayerDecodeMaxM = 64;        // largest M the whole-layer decode kernel handles
 static constexpr int kLayerDecodeDefaultMaxM = 16; // measured: per-stage kernels are faster above 16 tokens
 static int g_layer_decode_max_m = kLayerDecodeDefaultMaxM;
-static int g_pf_ahead = 1, g_pf_wait = 0;
+// L2 prefetch window of the whole-layer decode kernel's weight stream (slots
+// beyond the one loading).  Off: with weights that are not already in L2 the
+// extra requests only compete with the stage's slowest units (8B layer,
+// three rotated weight copies: M = 1 72.9 us off vs 75.0 us with one slot).
+static int g_pf_ahead = 0, g_pf_wait = 0;
 // Programmatic dependent launch of the whole-layer decode kernel: 0 = off,
 // k >= 1 = on, each CTA prefetching k units' weights before its wait.
 static int g_layer_decode_pdl = 1;
@@ -186,7 +190,12 @@ static int tiled_map(CUtensorMap* map, const void* base, bool f16, int64_t n, in
 // ------------------------------------------------------------------ planner
 struct Plan {
   int m_tiles, n_tiles, k_blocks, splits, kb_per_split, units, grid;
+  // split tail (CTA-pair plans): units [tail_start, units) split the last
+  // wave's tiles `tail_splits` ways; -1: none
+  int tail_start = -1, tail_splits = 1, tail_kb_per_split = 0;
 };
+// Split tail of the CTA-pair plans (on by default; svdmlp_set_split_tail).
+static int g_split_tail = 1;
 
 // One-CTA plans (decode-sized M): chooses the split-K factor that minimises a
 // wave-quantisation cost model in units of one k-block's MMA time: rounds of
@@ -268,6 +277,28 @@ static Plan plan_gemm_pair(int M, int N, int K, int BN, int sms, bool allow_spli
   p.kb_per_split = static_cast<int>(cdiv(p.k_blocks, best_s));
   p.splits = static_cast<int>(cdiv(p.k_blocks, p.kb_per_split));
   p.units = static_cast<int>(tiles) * p.splits;
+  // Split tail: when whole waves are unsplit and the last wave is partial,
+  // its tiles are split over K across the pairs that wave would leave idle
+  // (8B layer at 1024 tokens: the dual gate/up GEMM's 256 tiles are 3 waves
+  // of 74 pairs plus 34 tiles, whose 2-way splits take 68 pairs for half as
+  // long).  Same k-block cost model as above, including the fix-up.
+  if (allow_split && forced_splits <= 0 && g_split_tail && p.splits == 1) {
+    const int64_t waves = tiles / pairs, rem = tiles - waves * pairs;
+    const double plain = static_cast<double>(cdiv(tiles, pairs)) * p.k_blocks;
+    double best_tail = plain * 0.95;
+    for (int st = 2; st <= 4 && waves >= 1 && rem > 0; ++st) {
+      const int kbs = static_cast<int>(cdiv(p.k_blocks, st));
+      if (rem * st > pairs || kbs < 8 || rem * st * 2 * nb * 128 * BN * 4 > kPairPartialBudget) break;
+      const double cost = static_cast<double>(waves) * p.k_blocks + kbs + 10.0;
+      if (cost < best_tail) {
+        best_tail = cost;
+        p.tail_start = static_cast<int>(waves * pairs);
+        p.tail_kb_per_split = kbs;
+        p.tail_splits = static_cast<int>(cdiv(p.k_blocks, kbs));
+      }
+    }
+    if (p.tail_start >= 0) p.units = p.tail_start + static_cast<int>(rem) * p.tail_splits;
+  }
   p.grid = 2 * std::min(p.units, pairs);
   return p;
 }
@@ -403,6 +434,7 @@ static int64_t dec_partial_bytes(const Plan& p) {
 
 // Bytes of split-K partials a plan needs (NB accumulators of BM x BN fp32).
 static int64_t partial_bytes(const Plan& p, int BN, int NB, int ctas = 1) {
+  if (p.tail_start >= 0) return static_cast<int64_t>(p.units - p.tail_start) * ctas * NB * 128 * BN * 4;
   if (p.splits <= 1) return 0;
   return static_cast<int64_t>(p.units) * ctas * NB * 128 * BN * 4;
 }
@@ -575,7 +607,11 @@ static int64_t dec_set_partials(const svdmlp_layout* L, int M, int sms) {
 static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
   const int M = std::min(max_m, kPairMinMDefault - 1);
   int64_t best = 0;
-  for (int mp = kPairMinMLowest; mp <= max_m; mp = mp < 256 ? 256 : mp + 256) {
+  // Partials grow with the M-tiles: every 256-row step below max_m, and
+  // max_m itself (whose last M-tile may be partial).
+  for (int step = kPairMinMLowest;; step = step < 256 ? 256 : step + 256) {
+    const int mp = std::min(step, max_m);
+    if (mp < kPairMinMLowest) break;
     if (L->kind == SVDMLP_KIND_SVD) {
       if (L->r_gu > 0) best = std::max(best, stage_partials<CfgGU>(mp, L->ff, L->r_gu, sms, ST_GATEUP));
       if (L->r_d > 0) {
@@ -587,6 +623,7 @@ static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
       best = std::max(best, stage_partials<CfgDenseGU>(mp, L->ff, L->d, sms, ST_DENSE_GU));
       best = std::max(best, stage_partials<CfgDV>(mp, L->d, L->ff, sms, ST_DENSE_D));
     }
+    if (mp >= max_m) break;
   }
   if (L->kind == SVDMLP_KIND_SVD) {
     if (L->r_gu > 0) {
@@ -678,7 +715,7 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   }
   Plan pl = plan_for<Cfg>(M, N, K, dev->sms, g_split_override[stage]);
   if ((partial_bytes(pl, Cfg::BN, Cfg::NB, Cfg::CTAS) > w.partial_cap && w.unsplit_if_short) ||
-      (w.chain && pl.splits > 1))  // chained stages publish whole tiles: unsplit
+      (w.chain && (pl.splits > 1 || pl.tail_start >= 0)))  // chained stages publish whole tiles: unsplit
     pl = plan_for<Cfg>(M, N, K, dev->sms, 1);
   GemmParams p{};
   p.M = M;
@@ -690,6 +727,9 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   p.splits = pl.splits;
   p.kb_per_split = pl.kb_per_split;
   p.num_units = pl.units;
+  p.tail_start = pl.tail_start >= 0 ? pl.tail_start : pl.units;
+  p.tail_splits = pl.tail_splits;
+  p.tail_kb_per_split = pl.tail_kb_per_split;
   p.partials = w.partials;
   p.counters = w.counters;
   p.err = w.err;
@@ -714,7 +754,8 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   }
   if (w.chain) {
     // Chained stages are CTA-pair, unsplit plans by construction of the caller.
-    if (Cfg::CTAS != 2 || pl.splits != 1 || pl.m_tiles > kChainStride) return SVDMLP_ERR_INVALID_VALUE;
+    if (Cfg::CTAS != 2 || pl.splits != 1 || pl.tail_start >= 0 || pl.m_tiles > kChainStride)
+      return SVDMLP_ERR_INVALID_VALUE;
     p.m_group = std::min(w.chain->m_group, pl.m_tiles);
     p.dep = w.chain->dep;
     p.dep_target = w.chain->dep_target;
@@ -787,6 +828,8 @@ static int launch_gemv(const CUtensorMap& x, const CUtensorMap& x2, const CUtens
   p.splits = pl.splits;
   p.kb_per_split = pl.kb_per_split;
   p.num_units = pl.units;
+  p.tail_start = pl.units;
+  p.tail_splits = 1;
   p.partials = w.partials;
   p.counters = w.counters;
   p.err = w.err;
@@ -1884,6 +1927,12 @@ int svdmlp_set_pair_min_m(int m) {
 int svdmlp_set_prefill_chain(int groups) {
   if (groups < 0 || groups > 64) return SVDMLP_ERR_INVALID_VALUE;
   g_chain_groups = groups;
+  return SVDMLP_OK;
+}
+
+int svdmlp_set_split_tail(int enable) {
+  if (enable != 0 && enable != 1) return SVDMLP_ERR_INVALID_VALUE;
+  g_split_tail = enable;
   return SVDMLP_OK;
 }
 

@@ -89,6 +89,7 @@ SIGNATURES = {
     "svdmlp_rmsnorm": (c_int, [V, I64, V, V, I64, c_int, c_int, c_float, V]),
     "svdmlp_debug_wait_timeout": (c_int, [V, I64, I64, V]),
     "svdmlp_set_split_override": (c_int, [c_int, c_int]),
+    "svdmlp_set_split_tail": (c_int, [c_int]),
     "svdmlp_set_layer_decode": (c_int, [c_int]),
     "svdmlp_set_decode_overlap": (c_int, [c_int]),
     "svdmlp_set_pair_min_m": (c_int, [c_int]),

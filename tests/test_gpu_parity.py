@@ -6,6 +6,8 @@ bf16-grid inputs.
 """
 from __future__ import annotations
 
+import ctypes
+
 import numpy as np
 import pytest
 import torch
@@ -149,3 +151,33 @@ def test_device_wait_timeout_reports_error(cuda_device):
     # re-armed and usable
     assert lib.svdmlp_check_device_status(ws.data_ptr(), ws.numel(), s) == 0
     assert float((torch.ones(4, device=cuda_device) * 2).sum()) == 8.0
+
+
+def test_split_tail_matches_whole_tiles(cuda_device):
+    """The CTA-pair split tail (the last, partial wave's tiles split over K):
+    at a shape whose dual gate/up GEMM has one full wave plus a partial one,
+    the layer with and without the tail matches the oracle, and repeated runs
+    with the tail are bitwise identical."""
+    from svdflash_b200 import _lib
+    lib = _lib.load()
+    s, h, r, i = 512, 1024, 2048, 9184
+    x, f = orc.make_inputs(13, s, h, i, r)
+    ops = _ops()
+    out = (ctypes.c_int * 6)()
+    assert lib.svdmlp_plan_info(1, s, i, r, out) == 0 and out[4] > out[0] * out[1]   # tail units present
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f])
+    xd = to_dev(x, cuda_device)
+    ref = orc.svd_mlp(x, *f)
+    try:
+        lib.svdmlp_set_split_tail(0)
+        y_whole = ops.svd_mlp_packed(layer, xd)
+        lib.svdmlp_set_split_tail(1)
+        y1 = ops.svd_mlp_packed(layer, xd)
+        y2 = ops.svd_mlp_packed(layer, xd)
+        torch.cuda.synchronize()
+    finally:
+        lib.svdmlp_set_split_tail(1)
+    ops.check_device_status(cuda_device)
+    assert torch.equal(y1, y2)
+    assert_close(to_np(y_whole), ref, what="whole tiles")
+    assert_close(to_np(y1), ref, what="split tail")
