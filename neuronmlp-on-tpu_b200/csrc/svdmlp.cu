@@ -442,12 +442,15 @@ static int64_t partial_bytes(const Plan& p, int BN, int NB, int ctas = 1) {
 // ------------------------------------------------------------ kernel configs
 // Tile choices of the prefill kernels (compile-time; the defaults are the
 // tuned values, other values serve tile sweeps).
-// Dual gate/up tile: 256 x 224 per branch (one TMEM buffer of 2 x 256
-// columns) moves 68.6 bytes of operands per MMA cycle per SM against 96 for
-// 256 x 128 (double-buffered); L2-to-SM bandwidth (~11-12 TB/s) bounds these
-// kernels, so the wider tile wins (measured 166 vs 199 us at config 1).
+// Dual gate/up tile: 256 x 256 per branch (one TMEM buffer of 2 x 256
+// columns, 3 pipeline stages in 225 KB of shared memory).  L2-to-SM bandwidth
+// (~11-12 TB/s) bounds these kernels, so the widest tile wins: 7.6 KB of
+// operands per MFLOP against 8.2 for 256 x 224 and 11.4 for 256 x 128
+// (config 1: 256 x 128 double-buffered 199 us, 256 x 224 166 -> 139 us with
+// the tile-major weights; 256 x 256 with the split tail 275 vs 280 us per
+// layer in short runs, 312 vs 317 us sustained).
 #ifndef SVDMLP_GU_BN
-#define SVDMLP_GU_BN 224      // per-branch N of the dual gate/up tile
+#define SVDMLP_GU_BN 256      // per-branch N of the dual gate/up tile
 #endif
 #ifndef SVDMLP_GU_STAGES
 #define SVDMLP_GU_STAGES 3

@@ -103,7 +103,7 @@ def test_status_strings(lib):
 def test_plan_info_is_deterministic(lib):
     out = (ctypes.c_int * 6)()
     assert lib.svdmlp_plan_info(1, 1024, 14336, 2867, out) == 0
-    assert list(out)[:3] == [4, 64, 45]           # 256-row CTA-pair tiles, 224 per branch, 64-wide k-blocks
+    assert list(out)[:3] == [4, 56, 45]           # 256-row CTA-pair tiles, 256 per branch, 64-wide k-blocks
     assert out[3] == 1
     assert lib.svdmlp_plan_info(1, 1, 14336, 2867, out) == 0
     assert out[0] == 1 and out[3] >= 1 and out[4] == out[1] * out[3]

@@ -60,9 +60,9 @@ def test_config_tables_and_budget():
     assert isinstance(m8, config.ModelShape) and m8.hidden_size == 4096 and m8.rank_at_080 == 2560
     assert config.rank_for(m8, 0.9) == config.rank_for("llama-3.1-8b", 0.9) == 2816
     b = config.gate_up_block_params(1024, m8, 0.9)
-    # the compiled prefill tile: 256-row CTA pairs, 224 ff columns per branch,
+    # the compiled prefill tile: 256-row CTA pairs, 256 ff columns per branch,
     # 64-wide K blocks; the split count is the library planner's
-    assert isinstance(b, config.GateUpBlocks) and (b.bs, b.bh, b.br, b.bn) == (256, 64, 64, 224)
+    assert isinstance(b, config.GateUpBlocks) and (b.bs, b.bh, b.br, b.bn) == (256, 64, 64, 256)
     assert b.splits == config.stage_plan(config.STAGE_GATE_UP, 1024, 14336, 2816).splits
     assert b._replace(bn=256).bn == 256 and set(b._asdict()) == {"bs", "bh", "br", "bn", "splits"}
     d = config.gate_up_block_params(1, m8, 0.9)   # decode: 16-token tiles over 128-row weight panels
@@ -119,7 +119,7 @@ def test_reference_package_facade_exports():
     assert fused_gate_up is ops.fused_gate_up and xuv_matmul is ops.xuv_matmul and dense_mlp is ops.dense_mlp
     assert dense_matmul is ops.dense_matmul and low_rank_dim(4096, 14336, 0.8) == 2560
     p = get_fused_mlp_up_T_params(1024)
-    assert (p["tile_rows"], p["tile_cols"]) == (256, 224)
+    assert (p["tile_rows"], p["tile_cols"]) == (256, 256)
     with pytest.raises(ValueError, match="positive integer"):
         get_fused_three_mm_XTUV_params(0)
 

@@ -160,7 +160,7 @@ def test_split_tail_matches_whole_tiles(cuda_device):
     with the tail are bitwise identical."""
     from svdflash_b200 import _lib
     lib = _lib.load()
-    s, h, r, i = 512, 1024, 2048, 9184
+    s, h, r, i = 512, 1024, 2048, 10240
     x, f = orc.make_inputs(13, s, h, i, r)
     ops = _ops()
     out = (ctypes.c_int * 6)()
