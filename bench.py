@@ -431,6 +431,25 @@ def run_sweep(args) -> None:
             torch.cuda.empty_cache()
 
 
+def profile_layer(args) -> None:
+    """A short, fixed sequence of layer calls for ncu captures: the config-1
+    factors (seed --seed), then three svd_mlp_packed calls on M tokens; a
+    capture that skips the first call's launches sees warm code paths."""
+    import torch
+
+    from svdflash_b200.kernels import ops
+    dev = torch.device("cuda", 0)
+    d, ff, ratio = 4096, 14336, 0.9
+    layer = ops.pack_svd_layer(*make_factors(d, ff, rank_for(d, ff, ratio), args.seed, dev))
+    x = torch.randn(args.profile_layer, d, device=dev).to(torch.bfloat16)
+    y = torch.empty_like(x)
+    for _ in range(3):
+        ops.svd_mlp_packed(layer, x, out=y)
+    torch.cuda.synchronize()
+    ops.check_device_status(dev)
+    print(json.dumps({"profile_layer": args.profile_layer, "calls": 3}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -441,6 +460,8 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="N=1: leave out the decode (config 2) sub-record")
+    ap.add_argument("--profile-layer", type=int, default=0, metavar="M",
+                    help="profiling target: pack the 8B layer, run it three times on M tokens, exit")
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--tp-mode", choices=("auto", "allreduce", "split"), default="auto",
                     help="N>1: one all-reduce of the partial (default) or the all-gather split of the replicated stages")
@@ -451,6 +472,9 @@ def main():
         ap.error("--warmup must be >= 3")
     if args.sweep:
         run_sweep(args)
+        return
+    if args.profile_layer:
+        profile_layer(args)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":
