@@ -184,6 +184,28 @@ int svdmlp_forward(const svdmlp_layout* layout, const void* packed, const void* 
                    int64_t workspace_bytes, void* stream);
 
 /*
+ * The contracted layer: the same y = xuv(gate_up(x)) (+ residual), with the
+ * gate/up operator fused through . u_down as the reference's contracted path
+ * does (pallas_ops.contracted_svd_mlp, models/modeling_llama.py:865-886,
+ * bench/all_mlp_layers.py:491-503).  At M <= 16 tokens (the whole-layer decode
+ * kernel) each SwiGLU tile of H stays in shared memory and is multiplied by
+ * its slice of u_down at once, so H is never written: T = H . u_down is
+ * summed from fp32 per-tile partials in a fixed order (deterministic) and
+ * rounded to fp16 once.  Above 16 tokens it runs the two-operator path: a
+ * prefill contraction would move r / 256 (~11 at r = 2867) times more partial
+ * sums than the H it saves, and H stays in L2 between the kernels anyway.
+ */
+int svdmlp_forward_contracted(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x, int m,
+                              void* y, int64_t ld_y, const void* residual, int64_t ld_residual, void* workspace,
+                              int64_t workspace_bytes, void* stream);
+
+/* svdmlp_forward runs layers of M <= max_m tokens on the contracted schedule
+ * above and other decode sizes on four GEMM stages.  Default 1 (measured on
+ * B200: the contracted schedule is faster at one token, slower from four);
+ * 0 turns it off, a negative value restores the default; at most 16. */
+int svdmlp_set_decode_contract(int max_m);
+
+/*
  * Dense SwiGLU layer y = (SiLU(x.w_gate) * (x.w_up)) . w_down from the same
  * kernels.  Replaces kernels/reference.py:96-106 (dense_mlp_ref), nki_baseline
  * (test_speedup.py:669-678) and pallas_ops.dense_mlp

@@ -41,8 +41,18 @@
 
 namespace svdmlp {
 
+// Unit kinds of a stage.  GEMM: a 128-row weight panel over a K range (the
+// four stages of the plain schedule).  CONTRACT (the contracted schedule's
+// gate/up stage): one ff tile of the SwiGLU GEMM over the whole rank, its H
+// tile kept in shared memory and multiplied at once by the u_down columns of
+// that ff slice, all rank tiles; the fp32 product is this tile's partial of
+// T = H . u_down.  REDUCE: 32 features of T summed over every CONTRACT tile's
+// partial in tile order (deterministic) and rounded to fp16 once.
+enum DecKind : int { KIND_GEMM = 0, KIND_CONTRACT = 1, KIND_REDUCE = 2 };
+
 struct alignas(64) DecStage {
   CUtensorMap x, x2, w, w2;  // token operand(s) [M, K] (2-D) and packed tiled weight(s) [N, K] (4-D)
+  CUtensorMap w3;            // CONTRACT: packed u_down^T [r, ff], 128-row boxes
   void* out;
   long long ld_out;
   float* partials;   // [tiles][splits][nb][TOK][128] fp32 (token-major)
@@ -52,6 +62,12 @@ struct alignas(64) DecStage {
   int in_f16;        // operand type: fp16 (1) or bf16 (0)
   int epi;           // EPI_PLAIN, EPI_SWIGLU or EPI_RESID
   int out_kind;      // OUT_BF16, OUT_F16 or OUT_F32
+  int kind;          // DecKind
+  // CONTRACT: rank tiles of u_down (128 rows), u_down k-blocks over ff, and the
+  // T partials [ff tile][TOK tokens][t_ld] fp32; REDUCE reads them (t_slots
+  // tiles) and writes fp16 T (out, ld_out; N = rank).
+  int r_tiles, ff_kb, t_ld, t_slots;
+  float* tpart;
 };
 
 struct LayerDecParams {
@@ -97,12 +113,27 @@ struct LayerDecCfg {
   static constexpr int SLOT_BYTES = 2 * W_BYTES + 2 * X_BYTES;
   static constexpr int ACC_BUFS = 2;
   static constexpr int ACC_STRIDE = 2 * TOK;
-  static constexpr uint32_t TMEM_COLS = ACC_BUFS * ACC_STRIDE <= 64 ? 64 : ACC_BUFS * ACC_STRIDE <= 128 ? 128 : 256;
+  // The contracted schedule (16-token tiles only) keeps T accumulators for up
+  // to T_CHUNK rank tiles after the two SwiGLU accumulator buffers: all 512
+  // columns.  64-token tiles run the plain schedule only.
+  static constexpr bool CONTRACT = TOK == 16;
+  static constexpr int T_COL0 = ACC_BUFS * ACC_STRIDE;
+  static constexpr uint32_t TMEM_COLS =
+      CONTRACT ? 512 : ACC_BUFS * ACC_STRIDE <= 64 ? 64 : ACC_BUFS * ACC_STRIDE <= 128 ? 128 : 256;
+  static constexpr int T_CHUNK = CONTRACT ? (512 - T_COL0) / TOK : 0;  // rank tiles per TMEM pass
   static constexpr int OFF_W = 0;                        // [slot][2] weight tiles
   static constexpr int OFF_X = STAGES * 2 * W_BYTES;     // [slot][2] token tiles
-  static constexpr int OFF_BAR = OFF_X + STAGES * 2 * X_BYTES;
+  // CONTRACT: the H tile as the B operand of its u_down product, two
+  // [TOK x 64] K-major 128B-swizzled tiles (ff k-blocks 2f and 2f + 1)
+  static constexpr int OFF_H = OFF_X + STAGES * 2 * X_BYTES;
+  static constexpr int H_BYTES = CONTRACT ? 2 * X_BYTES : 0;
+  // REDUCE: [4 slot groups][TOK tokens][32 features] fp32 partial sums
+  static constexpr int OFF_RED = OFF_H + H_BYTES;
+  static constexpr int RED_BYTES = CONTRACT ? 4 * TOK * 32 * 4 : 0;
+  static constexpr int OFF_BAR = OFF_RED + RED_BYTES;
   static constexpr int QUEUE = 4;  // claimed units in flight per CTA
-  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1 + 2 * QUEUE;
+  // + h_ready, h_empty, t_full, t_empty for CONTRACT units
+  static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1 + 2 * QUEUE + 4;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_MISC + 64 + 4 * QUEUE + 1024;
   static_assert(X_BYTES % 1024 == 0, "token tiles stay 1024-byte aligned");
@@ -129,10 +160,15 @@ SVD_DEV LdUnit layer_dec_unit(const LayerDecParams& p, int u) {
 }
 
 // Shared-memory slots a unit occupies: one per k-block for the dual stage
-// (two branches), one per pair of k-blocks otherwise.
+// (two branches), one per pair of k-blocks otherwise; a CONTRACT unit adds one
+// slot per rank tile (the two u_down k-blocks of its ff slice); REDUCE units
+// load nothing.
 SVD_DEV int unit_slots(const LayerDecParams& p, const LdUnit& c) {
+  const DecStage& st = p.st[c.s];
+  if (st.kind == KIND_REDUCE) return 0;
   const int nk = c.kb1 - c.kb0;
-  return p.st[c.s].nb == 2 ? nk : (nk + 1) / 2;
+  if (st.kind == KIND_CONTRACT) return nk + st.r_tiles;
+  return st.nb == 2 ? nk : (nk + 1) / 2;
 }
 
 template <int TOK>
@@ -168,6 +204,13 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
   uint64_t* drain = acc_empty + Cfg::ACC_BUFS;
   uint64_t* q_full = drain + 1;            // [QUEUE] producer -> MMA, epilogue
   uint64_t* q_empty = q_full + Cfg::QUEUE; // [QUEUE] MMA + 4 epilogue warps -> producer
+  // CONTRACT units: H tile written (epilogue -> MMA), H tile read (MMA ->
+  // epilogue), T accumulators of a rank-tile chunk full (MMA -> epilogue) and
+  // drained (4 epilogue warps -> MMA)
+  uint64_t* h_ready = q_empty + Cfg::QUEUE;
+  uint64_t* h_empty = h_ready + 1;
+  uint64_t* t_full = h_ready + 2;
+  uint64_t* t_empty = h_ready + 3;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Cfg::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   volatile int* fix_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
@@ -195,6 +238,10 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
       mbar_init(&q_full[i], 1);
       mbar_init(&q_empty[i], 5);
     }
+    mbar_init(h_ready, 1);
+    mbar_init(h_empty, 1);
+    mbar_init(t_full, 1);
+    mbar_init(t_empty, 4);
     *abort_flag = 0;
     *fix_flag = 0;
     *epi_abort = 0;
@@ -202,12 +249,14 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
   }
   if (warp == 4 && lane == 0) {
     for (int s = 0; s < p.num_stages; ++s) {
+      if (p.st[s].kind == KIND_REDUCE) continue;  // no tensor maps
       prefetch_tensormap(&p.st[s].x);
       prefetch_tensormap(&p.st[s].w);
       if (p.st[s].nb == 2) {
         prefetch_tensormap(&p.st[s].x2);
         prefetch_tensormap(&p.st[s].w2);
       }
+      if (p.st[s].kind == KIND_CONTRACT) prefetch_tensormap(&p.st[s].w3);
     }
   }
   if (warp == 5) {
@@ -231,7 +280,12 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         uint8_t* w1 = w0 + Cfg::W_BYTES;
         // weights: packed tile-major layout, 4-D loads at (k-block, 16-row group)
         const int grp = c.n_t * Cfg::BM / 16;
-        if (st.nb == 2) {
+        if (st.kind == KIND_CONTRACT && i >= c.kb1 - c.kb0) {
+          // u_down^T rows of rank tile j, the two k-blocks of this ff slice
+          const int j = i - (c.kb1 - c.kb0), kbu = 2 * c.n_t;
+          tma_load_4d(&st.w3, &full[sl], w0, kbu, j * (Cfg::BM / 16));
+          if (kbu + 1 < st.ff_kb) tma_load_4d(&st.w3, &full[sl], w1, kbu + 1, j * (Cfg::BM / 16));
+        } else if (st.nb == 2) {
           tma_load_4d(&st.w, &full[sl], w0, c.kb0 + i, grp);
           tma_load_4d(&st.w2, &full[sl], w1, c.kb0 + i, grp);
         } else {
@@ -243,6 +297,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         const DecStage& st = p.st[c.s];
         uint8_t* x0 = smem + Cfg::OFF_X + (sl * 2) * Cfg::X_BYTES;
         uint8_t* x1 = x0 + Cfg::X_BYTES;
+        if (st.kind == KIND_CONTRACT && i >= c.kb1 - c.kb0) return;  // the H tile is already in shared memory
         if (st.nb == 2) {
           tma_load_2d(&st.x, &full[sl], x0, (c.kb0 + i) * Cfg::BK, 0);
           tma_load_2d(&st.x2, &full[sl], x1, (c.kb0 + i) * Cfg::BK, 0);
@@ -254,7 +309,11 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
       auto slot_pf = [&](const LdUnit& c, int i) {
         const DecStage& st = p.st[c.s];
         const int grp = c.n_t * Cfg::BM / 16;
-        if (st.nb == 2) {
+        if (st.kind == KIND_CONTRACT && i >= c.kb1 - c.kb0) {
+          const int j = i - (c.kb1 - c.kb0), kbu = 2 * c.n_t;
+          tma_prefetch_4d(&st.w3, kbu, j * (Cfg::BM / 16));
+          if (kbu + 1 < st.ff_kb) tma_prefetch_4d(&st.w3, kbu + 1, j * (Cfg::BM / 16));
+        } else if (st.nb == 2) {
           tma_prefetch_4d(&st.w, c.kb0 + i, grp);
           tma_prefetch_4d(&st.w2, c.kb0 + i, grp);
         } else {
@@ -263,7 +322,10 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         }
       };
       auto slot_bytes = [&](const LdUnit& c, int i) -> uint32_t {
-        const bool two = p.st[c.s].nb == 2 || c.kb0 + 2 * i + 1 < c.kb1;
+        const DecStage& st = p.st[c.s];
+        if (st.kind == KIND_CONTRACT && i >= c.kb1 - c.kb0)
+          return (2 * c.n_t + 1 < st.ff_kb ? 2u : 1u) * Cfg::W_BYTES;
+        const bool two = st.nb == 2 || c.kb0 + 2 * i + 1 < c.kb1;
         return (two ? 2u : 1u) * (Cfg::W_BYTES + Cfg::X_BYTES);
       };
       int it = 0;  // slot index over the whole run
@@ -304,6 +366,17 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         if (ntr < 40) trace_event(p, ntr, TR_CLAIM, u);
         const LdUnit c = layer_dec_unit(p, u);
         const int ns = unit_slots(p, c);
+        // REDUCE units load nothing, but the producer still waits for the
+        // CONTRACT stage before it claims again: CTAs with nothing else to do
+        // would otherwise queue several reduce units each and run them one
+        // after another at the end.
+        if (p.st[c.s].kind == KIND_REDUCE) {
+          if (c.s > ready_stage) {
+            if (!wait_counter_geq(&p.done[c.s - 1], p.st[c.s - 1].n_tiles, ctx, SITE_DEPENDENCY)) ok = false;
+            ready_stage = c.s;
+          }
+          continue;
+        }
         int i = 0;
         int pf = 0;  // slots of this unit requested so far (to L2 or shared memory)
         if (c.s > ready_stage) {
@@ -365,6 +438,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
       const uint32_t idesc_bf = make_idesc_16bit(Cfg::BM, TOK, false);
       const uint32_t idesc_h = make_idesc_16bit(Cfg::BM, TOK, true);
       int it = 0, acc_it = 0;
+      int cu = 0, tc = 0;  // CONTRACT units and T chunks issued by this CTA
       bool ok = true;
       for (int qi = 0; ok; ++qi) {
         const int qs = qi % Cfg::QUEUE;
@@ -374,8 +448,10 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         if (u < 0) break;
         const LdUnit c = layer_dec_unit(p, u);
         const DecStage& st = p.st[c.s];
+        if (st.kind == KIND_REDUCE) continue;  // no MMA: the epilogue sums partials
         const uint32_t idesc = st.in_f16 ? idesc_h : idesc_bf;
-        const int ns = unit_slots(p, c);
+        // the SwiGLU accumulation over the rank (a CONTRACT unit's first phase)
+        const int ns = st.kind == KIND_CONTRACT ? c.kb1 - c.kb0 : unit_slots(p, c);
         const int b = acc_it % Cfg::ACC_BUFS;
         const uint32_t aph = static_cast<uint32_t>(acc_it / Cfg::ACC_BUFS) & 1u;
         if (!mbar_wait(&acc_empty[b], aph ^ 1u, ctx, SITE_MMA_ACC_EMPTY)) break;
@@ -409,6 +485,51 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         if (!ok) break;
         umma_commit(&acc_full[b]);
         ++acc_it;
+        if constexpr (Cfg::CONTRACT) {
+          if (st.kind == KIND_CONTRACT) {
+            // Second phase: T partial [rank tile x TOK] = u_down^T[tile, ff slice]
+            // . H[ff slice, TOK], for every rank tile, in chunks of T_CHUNK tiles
+            // of TMEM columns; the H tile comes from shared memory.
+            if (!mbar_wait(h_ready, static_cast<uint32_t>(cu) & 1u, ctx, SITE_MMA_FULL)) break;
+            tc_fence_after();
+            const uint32_t hb = smem_addr(smem + Cfg::OFF_H);
+            const bool two = 2 * c.n_t + 1 < st.ff_kb;
+            for (int j0 = 0; j0 < st.r_tiles && ok; j0 += Cfg::T_CHUNK) {
+              const int j1 = min(st.r_tiles, j0 + Cfg::T_CHUNK);
+              if (!mbar_wait(t_empty, (static_cast<uint32_t>(tc) & 1u) ^ 1u, ctx, SITE_MMA_ACC_EMPTY)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              for (int j = j0; j < j1; ++j, ++it) {
+                const int sl = it % STAGES;
+                const uint32_t ph = static_cast<uint32_t>(it / STAGES) & 1u;
+                if (!mbar_wait(&full[sl], ph, ctx, SITE_MMA_FULL)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                const uint32_t w0 = smem_addr(smem + Cfg::OFF_W + (sl * 2) * Cfg::W_BYTES);
+                const uint32_t dT = tmem_base + static_cast<uint32_t>(Cfg::T_COL0 + (j - j0) * TOK);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  if (h == 1 && !two) break;
+#pragma unroll
+                  for (int k = 0; k < Cfg::BK / 16; ++k)
+                    umma_f16kind(dT, make_sw128_desc(w0 + h * Cfg::W_BYTES + k * 32),
+                                 make_sw128_desc(hb + h * Cfg::X_BYTES + k * 32), idesc_h, (h | k) ? 1u : 0u);
+                }
+                umma_commit(&empty[sl]);
+              }
+              if (!ok) break;
+              umma_commit(t_full);
+              ++tc;
+            }
+            if (!ok) break;
+            umma_commit(h_empty);  // the H tile may be overwritten once these MMAs are done
+            ++cu;
+          }
+        }
       }
       umma_commit(drain);
       mbar_wait(drain, 0, ctx, SITE_DRAIN_MMA, false);
@@ -419,6 +540,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
     grid_dependency_wait();
     const int q = warp;
     int acc_it = 0;
+    int ecu = 0, etc = 0;  // CONTRACT units and T chunks drained by this CTA
     int ntr = 40;  // epilogue trace events (slots [40, 64))
     for (int qi = 0;; ++qi) {
       const int qs = qi % Cfg::QUEUE;
@@ -435,6 +557,79 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
       if (u < 0) break;
       const LdUnit c = layer_dec_unit(p, u);
       const DecStage& st = p.st[c.s];
+      if constexpr (Cfg::CONTRACT) {
+        if (st.kind == KIND_REDUCE) {
+          // 32 features of T: wait (bounded) for every CONTRACT tile, sum its
+          // partials in tile order -- four slot groups (one per warp), then the
+          // groups in order -- round once to fp16 and publish.
+          if (threadIdx.x == 0) {
+            if (ntr < kTraceEvents - 1) trace_event(p, ntr, TR_DEP_BEGIN, u);
+            *fix_flag = wait_counter_geq(&p.done[c.s - 1], p.st[c.s - 1].n_tiles, ctx, SITE_DEPENDENCY) ? 1 : 0;
+            if (ntr < kTraceEvents - 1) trace_event(p, ntr, TR_DEP_END, u);
+          }
+          // thread 0's acquire load saw every CONTRACT tile's release; the
+          // CTA barrier orders the other threads' reads after it
+          named_barrier_sync(1, 128);
+          if (!*fix_flag) break;  // the same for all four warps
+          const int tv = min(p.M, TOK);
+          const int feat = c.n_t * 32 + static_cast<int>(lane);
+          const int S = st.t_slots, g0 = q * S / 4, g1 = (q + 1) * S / 4;
+          const float* base = st.tpart + feat;
+          const size_t slot_stride = static_cast<size_t>(TOK) * st.t_ld;
+          // Each thread sums its group's slots in slot order, in registers:
+          // one token with 32 loads in flight, more tokens four at a time with
+          // 8 slots x 4 tokens in flight (the reduction is latency-bound).
+          float* red = reinterpret_cast<float*>(smem + Cfg::OFF_RED);
+          if (tv == 1) {
+            float acc = 0.f;
+            for (int b0 = g0; b0 < g1; b0 += 32) {
+              float l[32];
+#pragma unroll
+              for (int k = 0; k < 32; ++k) l[k] = b0 + k < g1 ? __ldcg(base + (b0 + k) * slot_stride) : 0.f;
+#pragma unroll
+              for (int k = 0; k < 32; ++k) acc += l[k];
+            }
+            red[q * TOK * 32 + lane] = acc;
+          } else {
+            for (int t0 = 0; t0 < tv; t0 += 4) {
+              float acc[4] = {0.f, 0.f, 0.f, 0.f};
+              for (int b0 = g0; b0 < g1; b0 += 8) {
+                float l[8][4];
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+#pragma unroll
+                  for (int t = 0; t < 4; ++t)
+                    l[k][t] = (b0 + k < g1 && t0 + t < tv)
+                                  ? __ldcg(base + (b0 + k) * slot_stride + static_cast<size_t>(t0 + t) * st.t_ld)
+                                  : 0.f;
+#pragma unroll
+                for (int k = 0; k < 8; ++k)
+#pragma unroll
+                  for (int t = 0; t < 4; ++t) acc[t] += l[k][t];
+              }
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+                if (t0 + t < tv) red[(q * TOK + t0 + t) * 32 + lane] = acc[t];
+            }
+          }
+          named_barrier_sync(1, 128);
+          if (q == 0 && feat < st.N) {
+            __half* o = static_cast<__half*>(st.out);
+            for (int t = 0; t < tv; ++t) {
+              float sum = red[(0 * TOK + t) * 32 + lane];
+              sum += red[(1 * TOK + t) * 32 + lane];
+              sum += red[(2 * TOK + t) * 32 + lane];
+              sum += red[(3 * TOK + t) * 32 + lane];
+              if (f16_out_of_range(sum)) flag_range(p.err);
+              o[static_cast<long long>(t) * st.ld_out + feat] = __float2half_rn(fminf(fmaxf(sum, -65504.f), 65504.f));
+            }
+          }
+          named_barrier_sync(1, 128);  // stores before the release; the buffer free for the next unit
+          if (threadIdx.x == 0) red_add_release_gpu(&p.done[c.s], 1);
+          if (threadIdx.x == 0 && ntr < kTraceEvents - 1) trace_event(p, ntr, TR_UNIT_DONE, u);
+          continue;
+        }
+      }
       const int b = acc_it % Cfg::ACC_BUFS;
       const uint32_t aph = static_cast<uint32_t>(acc_it / Cfg::ACC_BUFS) & 1u;
       bool ok = mbar_wait(&acc_full[b], aph, ctx, SITE_EPI_ACC_FULL);
@@ -475,7 +670,30 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = silu_mul(v[j], w[j]);
           }
-          ld_store_chunk<TOK>(p, st, f, 16 * ch, v);
+          if (Cfg::CONTRACT && st.kind == KIND_CONTRACT) {
+            // H tile -> shared memory, as the B operand [TOK tokens x 128 ff]
+            // of this unit's u_down product: two K-major [TOK x 64] tiles in
+            // the 128-byte swizzle (16-byte chunk c of row t at c ^ (t % 8)).
+            // The previous CONTRACT unit's MMAs must be done reading it.
+            bool hok = ecu == 0 || mbar_wait(h_empty, static_cast<uint32_t>(ecu - 1) & 1u, ctx, SITE_EPI_ACC_FULL);
+            hok = __all_sync(0xffffffffu, hok);
+            if (!hok && lane == 0) *epi_abort = 1;
+            bool bad = false;
+            uint8_t* ht = smem + Cfg::OFF_H + (row >> 6) * Cfg::X_BYTES;
+            const int col = row & 63;
+#pragma unroll
+            for (int t = 0; t < 16; ++t) {
+              if (t < tv) bad |= f16_out_of_range(v[t]);
+              const __half hv = __float2half_rn(fminf(fmaxf(v[t], -65504.f), 65504.f));
+              *reinterpret_cast<__half*>(ht + t * 128 + (((col >> 3) ^ (t & 7)) << 4) + (col & 7) * 2) = hv;
+            }
+            if (bad) flag_range(p.err);
+            fence_proxy_async_smem();
+            named_barrier_sync(1, 128);
+            if (threadIdx.x == 0 && !*epi_abort) mbar_arrive(h_ready);
+          } else {
+            ld_store_chunk<TOK>(p, st, f, 16 * ch, v);
+          }
         } else {
 #pragma unroll
           for (int j = 0; j < 16; ++j) {
@@ -485,6 +703,42 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
             }
           }
         }
+      }
+      if (Cfg::CONTRACT && st.kind == KIND_CONTRACT) {
+        if (*epi_abort) break;
+        // Second phase: this ff tile's partial of T, rank tile by rank tile,
+        // token-major [TOK][t_ld] fp32 in the tile's slot (a warp's 32
+        // features of one token are one 128-byte line).
+        const int tv2 = min(p.M, TOK);
+        float* dst = st.tpart + static_cast<size_t>(c.n_t) * TOK * st.t_ld;
+        bool tok = true;
+        for (int j0 = 0; j0 < st.r_tiles && tok; j0 += Cfg::T_CHUNK) {
+          const int j1 = min(st.r_tiles, j0 + Cfg::T_CHUNK);
+          tok = mbar_wait(t_full, static_cast<uint32_t>(etc) & 1u, ctx, SITE_EPI_ACC_FULL);
+          tok = __all_sync(0xffffffffu, tok);
+          if (!tok) break;
+          tc_fence_after();
+          for (int j = j0; j < j1; ++j) {
+            uint32_t r16[16];
+            tmem_ld_x16(tmem_base + (static_cast<uint32_t>(q * 32) << 16) +
+                            static_cast<uint32_t>(Cfg::T_COL0 + (j - j0) * TOK), r16);
+            tmem_ld_wait();
+            const int fr = j * Cfg::BM + row;
+            if (fr < st.N) {
+#pragma unroll
+              for (int t = 0; t < 16; ++t)
+                if (t < tv2) __stcg(dst + static_cast<size_t>(t) * st.t_ld + fr, __uint_as_float(r16[t]));
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(t_empty);
+          ++etc;
+        }
+        if (!tok && lane == 0) *epi_abort = 1;
+        named_barrier_sync(2, 128);
+        if (*epi_abort) break;
+        ++ecu;
       }
       bool finished = st.splits == 1;  // this unit completed its tile
       if (st.splits > 1) {

@@ -413,17 +413,33 @@ static constexpr int kLayerDecodeCtasPerSm = 1;
 #endif
 
 // Partial bytes of the whole-layer decode kernel (all four stages at once).
+// The contracted decode schedule (16-token tiles): the gate/up stage's units
+// also multiply their H tile by u_down, writing fp32 partials of T per ff tile.
+// svdmlp_forward uses it for M <= g_decode_contract tokens.  Measured on B200
+// (8B layer, three rotated weight copies): M = 1 74.4 vs 76.0 us at r = 2867
+// and 58.0 vs 62.1 us at r = 1911; at 2 tokens 79.4 vs 77.8 and 63.0 vs 64.3;
+// from 4 tokens on slower (the partials grow with the tokens).
+static constexpr int kDecodeContractDefault = 1;
+static int g_decode_contract = kDecodeContractDefault;
+static int64_t contract_partials(const svdmlp_layout* L) {
+  return round_up(cdiv(L->ff, 128) * 16 * round_up(L->r_d, 128) * 4, 256);
+}
+
+// Partial bytes of the whole-layer decode kernel (all four stages at once),
+// the larger of the plain and the contracted schedule.
 static int64_t layer_decode_partials(const svdmlp_layout* L, int M, int sms) {
   const int tok = M <= 16 ? 16 : 64;
   const int slots = kLayerDecodeCtasPerSm * sms;
   const int shapes[4][3] = {{2 * L->rp_gu, L->d, 1}, {L->ff, L->r_gu, 2}, {L->r_d, L->ff, 1}, {L->d, L->r_d, 1}};
-  int64_t total = 0;
+  int64_t by_stage[4] = {0, 0, 0, 0};
   for (int st = 0; st < 4; ++st) {
     const Plan pl =
         plan_layer_stage(M, tok, shapes[st][0], shapes[st][1], shapes[st][2], slots, g_split_override[st]);
-    if (pl.splits > 1) total += round_up(static_cast<int64_t>(pl.units) * 2 * 128 * tok * 4, 256);
+    if (pl.splits > 1) by_stage[st] = round_up(static_cast<int64_t>(pl.units) * 2 * 128 * tok * 4, 256);
   }
-  return total;
+  const int64_t plain = by_stage[0] + by_stage[1] + by_stage[2] + by_stage[3];
+  const int64_t contracted = tok == 16 ? by_stage[0] + by_stage[3] + contract_partials(L) : 0;
+  return std::max(plain, contracted);
 }
 
 template <class Cfg>
@@ -1286,11 +1302,17 @@ static int launch_layer_decode(LayerDecParams& prm, cudaStream_t s, int sms) {
   return SVDMLP_OK;
 }
 
+// `contract`: the contracted schedule (16-token tiles, full layers with fp16
+// u_down): stage 1 runs CONTRACT units (SwiGLU tile -> shared memory ->
+// . u_down, fp32 T partials per ff tile), stage 2 REDUCE units (T summed in
+// tile order, rounded to fp16 once), stage 3 T . v_down as usual.
 static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void* x, int64_t ldx, int M, void* y,
-                            int64_t ldy, const void* residual, int64_t ld_res, const Workspace& w, cudaStream_t s) {
+                            int64_t ldy, const void* residual, int64_t ld_res, const Workspace& w, cudaStream_t s,
+                            bool contract = false) {
   DeviceInfo* dev = nullptr;
   SVD_CHECK(device_info(&dev));
   const int tok = M <= 16 ? 16 : 64;
+  contract = contract && tok == 16 && L->ud_f16 != 0;
   const int slots = kLayerDecodeCtasPerSm * dev->sms;  // the planning grid; the launch checks that it fits
   LayerDecParams prm;
   std::memset(&prm, 0, sizeof(prm));
@@ -1333,20 +1355,51 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
   for (int st = 0; st < 4; ++st) {
     DecStage& d = prm.st[st];
     const Spec& sp = spec[st];
+    d.kind = KIND_GEMM;
+    if (contract && st == 2) {
+      // REDUCE: 32 features of T per unit, reading stage 1's partials
+      const DecStage& c1 = prm.st[1];
+      d.kind = KIND_REDUCE;
+      d.out = w.t;
+      d.ld_out = L->rp_d;
+      d.N = L->r_d;
+      d.n_tiles = static_cast<int>(cdiv(L->r_d, 32));
+      d.splits = 1;
+      d.units = d.n_tiles;
+      d.unit_base = base;
+      d.t_slots = c1.n_tiles;
+      d.t_ld = c1.t_ld;
+      d.tpart = c1.tpart;
+      d.out_kind = OUT_F16;
+      base += d.units;
+      continue;
+    }
     SVD_CHECK(operand_map(&d.x, sp.x, sp.xf16, sp.xk, M, sp.xld, tok));
     SVD_CHECK(operand_map(&d.x2, sp.x2, sp.xf16, sp.xk, M, sp.xld, tok));
     SVD_CHECK(tiled_map(&d.w, sp.w, sp.xf16, sp.wrows, sp.xk, 128));
     SVD_CHECK(tiled_map(&d.w2, sp.w2, sp.xf16, sp.wrows, sp.xk, 128));
     const int N = static_cast<int>(st == 0 ? n1 : sp.wrows);
     const int K = static_cast<int>(sp.xk);
-    Plan pl = plan_layer_stage(M, tok, N, K, sp.nb, slots, g_split_override[st]);
+    const bool con = contract && st == 1;
+    // CONTRACT units hold a whole ff tile (the SwiGLU needs full sums)
+    Plan pl = plan_layer_stage(M, tok, N, K, sp.nb, slots, con ? 1 : g_split_override[st]);
     int64_t pb = pl.splits > 1 ? round_up(static_cast<int64_t>(pl.units) * 2 * 128 * tok * 4, 256) : 0;
+    if (con) {
+      d.kind = KIND_CONTRACT;
+      SVD_CHECK(tiled_map(&d.w3, P + L->off_ud, true, L->r_d, L->ff, 128));
+      d.r_tiles = static_cast<int>(cdiv(L->r_d, 128));
+      d.ff_kb = static_cast<int>(cdiv(L->ff, 64));
+      d.t_ld = static_cast<int>(round_up(L->r_d, 128));
+      pb = contract_partials(L);
+      if (pb > part_left) return SVDMLP_ERR_WORKSPACE;
+      d.tpart = part;
+    }
     if (pb > part_left) {
       if (!w.unsplit_if_short) return SVDMLP_ERR_WORKSPACE;
       pl = plan_layer_stage(M, tok, N, K, sp.nb, slots, 1);
       pb = 0;
     }
-    d.out = sp.out;
+    d.out = con ? nullptr : sp.out;
     d.ld_out = sp.ld_out;
     d.partials = part;
     d.tile_counters = w.counters + st * 65536;
@@ -1613,8 +1666,32 @@ int svdmlp_xuv(const svdmlp_layout* L, const void* packed, const void* h, int64_
   return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
 }
 
+static int forward_impl(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* y,
+                        int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes, void* stream,
+                        bool contract);
+
 int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* y,
                    int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes, void* stream) {
+  return forward_impl(L, packed, x, ldx, M, y, ldy, residual, ld_res, ws, ws_bytes, stream, M <= g_decode_contract);
+}
+
+int svdmlp_forward_contracted(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M,
+                              void* y, int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes,
+                              void* stream) {
+  return forward_impl(L, packed, x, ldx, M, y, ldy, residual, ld_res, ws, ws_bytes, stream, true);
+}
+
+int svdmlp_set_decode_contract(int max_m) {
+  if (max_m > 16) return SVDMLP_ERR_INVALID_VALUE;
+  g_decode_contract = max_m < 0 ? kDecodeContractDefault : max_m;
+  return SVDMLP_OK;
+}
+
+}  // extern "C"
+
+static int forward_impl(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* y,
+                        int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes, void* stream,
+                        bool contract) {
   SVD_CHECK(check_layout(L));
   if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || L->r_d <= 0 || !packed || !x || !y || M <= 0 ||
       ldx < L->d || ldy < L->d || (residual && ld_res < L->d))
@@ -1629,7 +1706,7 @@ int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, in
   if (M <= g_layer_decode_max_m) {
     // Decode sizes: the whole layer in one launch; its stores need no TMA
     // alignment, and the residual is read in place (it must not alias y).
-    return run_layer_decode(L, P, xa, ldxa, M, y, ldy, residual, ld_res, w, s);
+    return run_layer_decode(L, P, xa, ldxa, M, y, ldy, residual, ld_res, w, s, contract);
   }
   const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
   const void* res = nullptr;
@@ -1667,6 +1744,8 @@ int svdmlp_forward(const svdmlp_layout* L, const void* packed, const void* x, in
   SVD_CHECK(run_down_v(L, P, M, yt.ptr, yt.ld, res, ldr, w, s));
   return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
 }
+
+extern "C" {
 
 int svdmlp_dense_forward(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* y,
                          int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes,

@@ -74,6 +74,8 @@ SIGNATURES = {
     "svdmlp_xuv": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_forward": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
     "svdmlp_dense_forward": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
+    "svdmlp_forward_contracted": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
+    "svdmlp_set_decode_contract": (c_int, [c_int]),
     "svdmlp_down_partial": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_forward_partial": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_down_finish": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),

@@ -39,7 +39,7 @@ from .. import _lib
 __all__ = [
     "PackedLayer", "pack_svd_layer", "pack_dense_layer", "low_rank_dim", "rank_for_ratio", "silu",
     "fused_gate_up", "fused_xuv", "xuv_matmul", "svd_mlp", "contracted_svd_mlp", "dense_mlp",
-    "dense_matmul", "svd_mlp_packed", "dense_mlp_packed", "gate_up_packed", "xuv_packed",
+    "dense_matmul", "svd_mlp_packed", "contracted_mlp_packed", "dense_mlp_packed", "gate_up_packed", "xuv_packed",
     "forward_partial_packed", "down_partial_packed", "down_finish_packed", "rmsnorm", "workspace_for",
     "check_device_status", "launch_count",
 ]
@@ -330,6 +330,28 @@ def svd_mlp_packed(layer: PackedLayer, x: torch.Tensor, residual: Optional[torch
     return y
 
 
+def contracted_mlp_packed(layer: PackedLayer, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
+                          out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """The contracted layer (svdmlp_forward_contracted): gate/up fused through
+    . u_down at decode sizes, H never written; the two-operator path above 16
+    tokens."""
+    if layer.kind != _lib.KIND_SVD or layer.r_gu == 0 or layer.r_d == 0:
+        raise ValueError("contracted_svd_mlp needs a full SVD layer")
+    xb = _prep_x(x, layer.d)
+    m = xb.shape[0]
+    y = out if out is not None else _out(m, layer.d, xb.device)
+    ws = layer.workspace(m)
+    res = None
+    if residual is not None:
+        res = _bf16(residual)
+        if tuple(res.shape) != (m, layer.d):
+            raise ValueError("residual shape does not match the output")
+    _lib.check(_lib.load().svdmlp_forward_contracted(
+        ctypes.byref(layer.layout), layer.packed.data_ptr(), xb.data_ptr(), _ld(xb), m, y.data_ptr(), _ld(y),
+        _ptr(res), 0 if res is None else _ld(res), ws.ptr, ws.nbytes, _stream(xb.device)), "contracted_svd_mlp")
+    return y
+
+
 def dense_mlp_packed(layer: PackedLayer, x: torch.Tensor, residual: Optional[torch.Tensor] = None,
                      out: Optional[torch.Tensor] = None) -> torch.Tensor:
     if layer.kind != _lib.KIND_DENSE:
@@ -545,12 +567,21 @@ def svd_mlp(x, u_gate, v_gate, u_up, v_up, u_down, v_down, *, gate_up_blocks=Non
 
 def contracted_svd_mlp(x, u_gate, v_gate, u_up, v_up, u_down, v_down, *, gate_up_blocks=None,
                        mixed_precision=True, interpret=False, residual=None):
-    """pallas_ops.contracted_svd_mlp (models/modeling_llama.py:865-886): the
-    same function as svd_mlp.  On B200 the [M, ff] activation H is an fp16
-    workspace intermediate that stays resident in the 126 MB L2 between the
-    gate/up and down kernels for prefill-sized M."""
-    return svd_mlp(x, u_gate, v_gate, u_up, v_up, u_down, v_down, gate_up_blocks=gate_up_blocks,
-                   mixed_precision=mixed_precision, interpret=interpret, residual=residual)
+    """pallas_ops.contracted_svd_mlp (models/modeling_llama.py:865-886,
+    bench/all_mlp_layers.py:491-503): the layer with gate/up fused through
+    . u_down (svdmlp_forward_contracted).  At decode sizes (<= 16 tokens) each
+    SwiGLU tile of H stays in shared memory and is multiplied by its u_down
+    slice in the same unit; above that the two-operator path runs, where H
+    stays in the 126 MB L2 between the kernels."""
+    _validate_arrays(x, u_gate, v_gate, u_up, v_up, u_down, v_down)
+    _check_modes(mixed_precision, interpret, x.dtype)
+    guard = _GateUpSplits(gate_up_blocks)
+    if x.shape[1] != u_gate.shape[0]:
+        raise ValueError("x/u_gate contraction dimensions do not match")
+    layer = _cache.get("svd", (u_gate, v_gate, u_up, v_up, u_down, v_down),
+                       lambda: pack_svd_layer(u_gate, v_gate, u_up, v_up, u_down, v_down))
+    with guard:
+        return _finish(contracted_mlp_packed(layer, x, residual=residual), x)
 
 
 def dense_mlp(x, w_gate, w_up, w_down, *, mixed_precision=True, interpret=False, residual=None):

@@ -86,6 +86,8 @@ def test_entry_points_reject_bad_arguments(lib):
     assert lib.svdmlp_set_pair_min_m(130) == _lib.ERR_INVALID_VALUE
     assert lib.svdmlp_set_decode_prefetch(-1, 0) == _lib.ERR_INVALID_VALUE
     assert lib.svdmlp_set_prefill_chain(-1) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_set_decode_contract(17) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_set_split_tail(2) == _lib.ERR_INVALID_VALUE
     assert lib.svdmlp_rmsnorm(None, 8, None, None, 8, 1, 8, 1e-5, None) == _lib.ERR_INVALID_VALUE
     # misaligned output of the fp32 partial
     assert lib.svdmlp_forward_partial(ctypes.byref(L), 1, 1, 64, 4, 2, 40, 256, 1 << 20, None) == _lib.ERR_ALIGNMENT
