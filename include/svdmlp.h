@@ -131,6 +131,16 @@ int svdmlp_pack(const svdmlp_layout* layout, const void* u_gate, int64_t ld_u_ga
  * Python API calls this after every pack. */
 int svdmlp_pack_status(const svdmlp_layout* layout, const void* packed, void* stream);
 
+/* svdmlp_pack for a decoder block with a fused RMSNorm: the norm's weight
+ * norm_weight [d] (bf16) is folded into the first factors (row k of u_gate
+ * and u_up times norm_weight[k], in fp32, rounded once), since
+ * (x * rstd * w) . u = rstd * (x . diag(w) u).  The layout is svdmlp_layout_init's.
+ * Use the packed layer with svdmlp_forward_block. */
+int svdmlp_pack_block(const svdmlp_layout* layout, const void* norm_weight, const void* u_gate, int64_t ld_u_gate,
+                      const void* v_gate, int64_t ld_v_gate, const void* u_up, int64_t ld_u_up, const void* v_up,
+                      int64_t ld_v_up, const void* u_down, int64_t ld_u_down, const void* v_down, int64_t ld_v_down,
+                      void* packed, void* stream);
+
 /* Packs dense weights w_gate, w_up [d, ff] and w_down [ff, d]. */
 int svdmlp_dense_pack(const svdmlp_layout* layout, const void* w_gate, int64_t ld_w_gate, const void* w_up,
                       int64_t ld_w_up, const void* w_down, int64_t ld_w_down, void* packed, void* stream);
@@ -204,6 +214,27 @@ int svdmlp_forward_contracted(const svdmlp_layout* layout, const void* packed, c
  * B200: the contracted schedule is faster at one token, slower from four);
  * 0 turns it off, a negative value restores the default; at most 16. */
 int svdmlp_set_decode_contract(int max_m);
+
+/*
+ * One MLP block of a decoder stack with the RMSNorm fused in:
+ *   y = x + mlp(RMSNorm(x)),  RMSNorm(x) = x * rsqrt(mean(x^2) + eps) * w
+ * (models/modeling_llama.py:245-262, 998-1002; bench/e2e_block.py:72-75,
+ * 264-278), `packed` from svdmlp_pack_block.  No separate norm launch: the
+ * first GEMM scales its output rows by rsqrt(sum(x_stats[row]) / d + eps),
+ * and the last GEMM's residual epilogue writes y_stats, the same statistics of
+ * y for the next block.  x_stats / y_stats: fp32 [M, ld_stats], one sum of
+ * squares per 128-column slice of the row (ld_stats >= ceil(d / 128));
+ * svdmlp_row_sumsq computes them for the stack's input; y_stats may be NULL.
+ * x must be 16-byte aligned (it is read in place as the residual) and must
+ * not alias y.
+ */
+int svdmlp_forward_block(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x, int m,
+                         void* y, int64_t ld_y, const float* x_stats, int64_t ld_stats, float* y_stats, float eps,
+                         void* workspace, int64_t workspace_bytes, void* stream);
+
+/* stats[row * ld_stats + s] = sum of squares of x[row, 128 s : 128 (s + 1)]
+ * (bf16 x [M, n]); ld_stats >= ceil(n / 128). */
+int svdmlp_row_sumsq(const void* x, int64_t ld_x, int m, int n, float* stats, int64_t ld_stats, void* stream);
 
 /*
  * Dense SwiGLU layer y = (SiLU(x.w_gate) * (x.w_up)) . w_down from the same

@@ -96,6 +96,17 @@ struct GemmParams {
   // tiles split `tail_splits` ways over K (tail_kb_per_split k-blocks each);
   // units before it follow `splits`.  tail_start == num_units: no split tail.
   int tail_start, tail_splits, tail_kb_per_split;
+  // Fused RMSNorm of a decoder block.  norm_stats (the block's first GEMM,
+  // whose weights carry the norm's column weights): output row i is scaled
+  // by rsqrt(sum_j norm_stats[i * stats_ld + j] / norm_dim + norm_eps), the
+  // sum over j < norm_parts in order.  out_stats (an EPI_RESID stage): for
+  // each row, the sum of squares of its bf16 outputs in every 128-column
+  // slice, stored at out_stats[row * stats_ld + slice] -- the next block's
+  // norm_stats.
+  const float* norm_stats;
+  int norm_parts, norm_dim, stats_ld;
+  float norm_eps;
+  float* out_stats;
   // Chained stages (null: not chained, wait for the whole previous launch).
   const int* dep;    // previous stage's per-M-tile tile counters
   int dep_target;    // count that marks an M-tile of the previous stage complete
@@ -566,6 +577,13 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       const int y_box = row_base + q * 32;
 
       if (c.nsplit == 1) {
+        float rscale = 1.0f;  // RMSNorm row scale (1 without a fused norm)
+        if (p.norm_stats != nullptr && grow < p.M) {
+          float ssum = 0.0f;
+          for (int j = 0; j < p.norm_parts; ++j) ssum += p.norm_stats[static_cast<long long>(grow) * p.stats_ld + j];
+          rscale = rsqrtf(ssum / static_cast<float>(p.norm_dim) + p.norm_eps);
+        }
+        float slice_ss[Cfg::BN / 128 > 0 ? Cfg::BN / 128 : 1] = {};
 #pragma unroll 1
         for (int ch = half; ch < NCH; ch += CH_STEP) {
           uint32_t rg[32];
@@ -589,9 +607,34 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
             w[j] = Cfg::NB == 2 ? __uint_as_float(ru[j]) : 0.0f;
           }
           epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
+          if (p.norm_stats != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              v[j] *= rscale;
+              w[j] *= rscale;
+            }
+          }
+          if constexpr (Cfg::EPI == EPI_RESID && Cfg::BN % 128 == 0 && CH_STEP == 1) {
+            if (p.out_stats != nullptr) {
+              float ss = 0.0f;
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const float r = __bfloat162float(__float2bfloat16(v[j]));  // the value the next block reads
+                ss += r * r;
+              }
+              slice_ss[ch / 4] += ss;
+            }
+          }
           store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
           if constexpr (Cfg::EPI == EPI_DUAL_STORE)
             store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N, p.err);
+        }
+        if constexpr (Cfg::EPI == EPI_RESID && Cfg::BN % 128 == 0 && CH_STEP == 1) {
+          if (p.out_stats != nullptr && grow < p.M) {
+#pragma unroll
+            for (int sl = 0; sl < Cfg::BN / 128; ++sl)
+              if (n0 + sl * 128 < p.N) p.out_stats[static_cast<long long>(grow) * p.stats_ld + n0 / 128 + sl] = slice_ss[sl];
+          }
         }
         if (p.pub != nullptr) {
           // Publish this CTA's rows of the tile: each warp's output boxes are

@@ -65,7 +65,8 @@ struct DecCfg {
   static constexpr int OFF_BAR = OFF_STG + STG_BYTES;
   static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
-  static constexpr int SMEM_BYTES = OFF_MISC + 64 + 1024;
+  static constexpr int OFF_RSTD = OFF_MISC + 64;  // fused RMSNorm: the row scale of each token
+  static constexpr int SMEM_BYTES = OFF_RSTD + TOK * 4 + 1024;
   static_assert(SMEM_BYTES <= 232448, "shared memory budget exceeded");
   static_assert(!TWO_PER_SM || SMEM_BYTES <= 113 * 1024, "two CTAs per SM need <= 113 KB of shared memory each");
 };
@@ -86,9 +87,11 @@ SVD_DEV DecUnit decode_dec_unit(const GemmParams& p, int u) {
 // Writes four consecutive features [f, f + 4) of token t: epilogue residual,
 // conversion and a vector store when all four are inside N (scalar tail
 // otherwise).  Rows and the output base are 16-byte aligned.
+// Returns the sum of squares of the bf16 values it stored (0 for other
+// output types), for the fused RMSNorm statistics of the next block.
 template <class Cfg>
-SVD_DEV void dec_store4(const GemmParams& p, void* out, long long ld_out, int t, int f, float4 v) {
-  if (t >= p.M || f >= p.N) return;
+SVD_DEV float dec_store4(const GemmParams& p, void* out, long long ld_out, int t, int f, float4 v) {
+  if (t >= p.M || f >= p.N) return 0.0f;
   float x[4] = {v.x, v.y, v.z, v.w};
   const bool full = f + 4 <= p.N;
   if constexpr (Cfg::EPI == EPI_RESID) {
@@ -136,7 +139,21 @@ SVD_DEV void dec_store4(const GemmParams& p, void* out, long long ld_out, int t,
       for (int j = 0; j < 4; ++j)
         if (f + j < p.N) o[j] = __float2bfloat16(x[j]);
     }
+    float ss = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float r = f + j < p.N ? __bfloat162float(__float2bfloat16(x[j])) : 0.0f;
+      ss += r * r;
+    }
+    return ss;
   }
+  return 0.0f;
+}
+
+SVD_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
 }
 
 template <class Cfg>
@@ -293,6 +310,18 @@ __global__ void __launch_bounds__(192)
     // ------------------------------------------------------------ epilogue
     const int q = warp;
     int acc_it = 0;
+    float* rstd = reinterpret_cast<float*>(smem + Cfg::OFF_RSTD);
+    if (p.norm_stats != nullptr) {
+      // fused RMSNorm: the row scale of each token, from the previous
+      // block's per-slice sums of squares (written by the previous kernel)
+      grid_dependency_wait();
+      for (int t = threadIdx.x; t < min(p.M, TOK); t += 128) {
+        float ssum = 0.0f;
+        for (int j = 0; j < p.norm_parts; ++j) ssum += p.norm_stats[static_cast<long long>(t) * p.stats_ld + j];
+        rstd[t] = rsqrtf(ssum / static_cast<float>(p.norm_dim) + p.norm_eps);
+      }
+      named_barrier_sync(1, 128);
+    }
     for (int u = blockIdx.x; u < p.num_units; u += gridDim.x) {
       const DecUnit c = decode_dec_unit(p, u);
       const int b = acc_it % Cfg::ACC_BUFS;
@@ -336,6 +365,10 @@ __global__ void __launch_bounds__(192)
 #pragma unroll
             for (int j = 0; j < 16; ++j) v[j] = silu_mul(v[j], w[j]);
           }
+          if (p.norm_stats != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) v[j] *= rstd[min(16 * ch + j, TOK - 1)];
+          }
           // column `row` of the fp32 [16 tokens][128 features] staging tile
 #pragma unroll
           for (int j = 0; j < 16; ++j) stg[j * Cfg::BM + row] = v[j];
@@ -346,7 +379,10 @@ __global__ void __launch_bounds__(192)
             const int idx = static_cast<int>(threadIdx.x) + 128 * i;
             const int rr = idx >> 5, c4 = idx & 31;
             const float4 x = *reinterpret_cast<const float4*>(stg + rr * Cfg::BM + 4 * c4);
-            dec_store4<Cfg>(p, out, ld_out, 16 * ch + rr, f0 + 4 * c4, x);
+            const float ss = warp_sum(dec_store4<Cfg>(p, out, ld_out, 16 * ch + rr, f0 + 4 * c4, x));
+            // one warp holds one token's 128 features: its slice sum of squares
+            if (p.out_stats != nullptr && lane == 0 && 16 * ch + rr < p.M)
+              p.out_stats[static_cast<long long>(16 * ch + rr) * p.stats_ld + c.n_t] = ss;
           }
           named_barrier_sync(3, 128);  // read before the next chunk overwrites it
         } else {
@@ -439,7 +475,17 @@ __global__ void __launch_bounds__(192)
                 g[i].z = silu_mul(g[i].z, uacc[i].z);
                 g[i].w = silu_mul(g[i].w, uacc[i].w);
               }
-              if (tt[i] < tv) dec_store4<Cfg>(p, out, ld_out, tt[i], f0 + ff[i], g[i]);
+              if (p.norm_stats != nullptr && tt[i] < tv) {
+                const float sc = rstd[tt[i]];
+                g[i].x *= sc;
+                g[i].y *= sc;
+                g[i].z *= sc;
+                g[i].w *= sc;
+              }
+              // a warp's lanes hold one token row (tt is the same across the warp)
+              const float ss = warp_sum(tt[i] < tv ? dec_store4<Cfg>(p, out, ld_out, tt[i], f0 + ff[i], g[i]) : 0.0f);
+              if (p.out_stats != nullptr && lane == 0 && tt[i] < tv)
+                p.out_stats[static_cast<long long>(tt[i]) * p.stats_ld + c.n_t] = ss;
             }
           }
         }

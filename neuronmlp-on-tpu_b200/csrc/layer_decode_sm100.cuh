@@ -68,6 +68,11 @@ struct alignas(64) DecStage {
   // tiles) and writes fp16 T (out, ld_out; N = rank).
   int r_tiles, ff_kb, t_ld, t_slots;
   float* tpart;
+  // fused RMSNorm: `norm` (the first stage) scales each token's outputs by
+  // its row scale; `out_stats` (the EPI_RESID stage) receives each token's
+  // sum of squares of its bf16 outputs per 128-feature tile.
+  int norm;
+  float* out_stats;
 };
 
 struct LayerDecParams {
@@ -88,6 +93,12 @@ struct LayerDecParams {
   int pdl_units;
   const __nv_bfloat16* residual;
   long long ld_residual;
+  // Fused RMSNorm of a decoder block: the previous block's per-slice sums of
+  // squares of this block's input, [M][stats_ld], norm_parts slices of the
+  // norm_dim features; also the row stride of the stages' out_stats.
+  const float* norm_stats;
+  int norm_parts, norm_dim, stats_ld;
+  float norm_eps;
   // Optional timeline (null: off): per CTA kTraceEvents pairs of
   // (tag | unit << 8, globaltimer ns).
   unsigned long long* trace;
@@ -130,7 +141,9 @@ struct LayerDecCfg {
   // REDUCE: [4 slot groups][TOK tokens][32 features] fp32 partial sums
   static constexpr int OFF_RED = OFF_H + H_BYTES;
   static constexpr int RED_BYTES = CONTRACT ? 4 * TOK * 32 * 4 : 0;
-  static constexpr int OFF_BAR = OFF_RED + RED_BYTES;
+  static constexpr int OFF_RSTD = OFF_RED + RED_BYTES;     // fused RMSNorm: row scale per token
+  static constexpr int OFF_SS = OFF_RSTD + TOK * 4;        // [4 warps][16 tokens] sums of squares
+  static constexpr int OFF_BAR = OFF_SS + 4 * 16 * 4;
   static constexpr int QUEUE = 4;  // claimed units in flight per CTA
   // + h_ready, h_empty, t_full, t_empty for CONTRACT units
   static constexpr int NUM_BARS = 2 * STAGES + 2 * ACC_BUFS + 1 + 2 * QUEUE + 4;
@@ -171,13 +184,25 @@ SVD_DEV int unit_slots(const LayerDecParams& p, const LdUnit& c) {
   return st.nb == 2 ? nk : (nk + 1) / 2;
 }
 
+// Stores one 16-token chunk of a unit's outputs (thread = feature f of the
+// 128-row tile; all 128 epilogue threads call it together).  The first stage
+// of a fused block scales token t by its RMSNorm row scale; an EPI_RESID
+// stage with out_stats also writes each token's sum of squares of its bf16
+// outputs over the tile's 128 features (summed across the four warps in
+// warp order).
 template <int TOK>
-SVD_DEV void ld_store_chunk(const LayerDecParams& p, const DecStage& st, int f, int t0, const float (&v)[16]) {
-  if (f >= st.N) return;
+SVD_DEV void ld_store_chunk(const LayerDecParams& p, const DecStage& st, int f, int t0, float (&v)[16],
+                            const float* rstd, float* ss_smem, int n_t) {
+  if (st.norm) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] *= rstd[min(t0 + j, TOK - 1)];
+  }
+  float ss[16];
 #pragma unroll
   for (int j = 0; j < 16; ++j) {
+    ss[j] = 0.0f;
     const int t = t0 + j;
-    if (t < p.M) {
+    if (t < p.M && f < st.N) {
       float x = v[j];
       if (st.epi == EPI_RESID) x += __bfloat162float(p.residual[static_cast<long long>(t) * p.ld_residual + f]);
       const long long off = static_cast<long long>(t) * st.ld_out + f;
@@ -185,9 +210,30 @@ SVD_DEV void ld_store_chunk(const LayerDecParams& p, const DecStage& st, int f, 
       else if (st.out_kind == OUT_F16) {
         if (f16_out_of_range(x)) flag_range(p.err);  // reported, never silent
         static_cast<__half*>(st.out)[off] = __float2half_rn(fminf(fmaxf(x, -65504.f), 65504.f));
+      } else {
+        const __nv_bfloat16 b = __float2bfloat16(x);
+        static_cast<__nv_bfloat16*>(st.out)[off] = b;
+        const float r = __bfloat162float(b);
+        ss[j] = r * r;
       }
-      else static_cast<__nv_bfloat16*>(st.out)[off] = __float2bfloat16(x);
     }
+  }
+  if (st.out_stats != nullptr) {
+    const int warp = static_cast<int>(threadIdx.x >> 5), lane = static_cast<int>(threadIdx.x & 31);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float a = ss[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+      if (lane == 0) ss_smem[warp * 16 + j] = a;
+    }
+    named_barrier_sync(5, 128);
+    if (threadIdx.x < 16 && t0 + static_cast<int>(threadIdx.x) < p.M) {
+      const int j = static_cast<int>(threadIdx.x);
+      const float tot = ss_smem[j] + ss_smem[16 + j] + ss_smem[32 + j] + ss_smem[48 + j];
+      st.out_stats[static_cast<long long>(t0 + j) * p.stats_ld + n_t] = tot;
+    }
+    named_barrier_sync(5, 128);  // the buffer is free for the next chunk
   }
 }
 
@@ -541,6 +587,18 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
     const int q = warp;
     int acc_it = 0;
     int ecu = 0, etc = 0;  // CONTRACT units and T chunks drained by this CTA
+    float* rstd = reinterpret_cast<float*>(smem + Cfg::OFF_RSTD);
+    float* ss_smem = reinterpret_cast<float*>(smem + Cfg::OFF_SS);
+    if (p.norm_stats != nullptr) {
+      // fused RMSNorm: each token's row scale, from the previous block's
+      // per-slice sums of squares, summed in slice order
+      for (int t = threadIdx.x; t < min(p.M, TOK); t += 128) {
+        float ssum = 0.0f;
+        for (int j = 0; j < p.norm_parts; ++j) ssum += p.norm_stats[static_cast<long long>(t) * p.stats_ld + j];
+        rstd[t] = rsqrtf(ssum / static_cast<float>(p.norm_dim) + p.norm_eps);
+      }
+      named_barrier_sync(1, 128);
+    }
     int ntr = 40;  // epilogue trace events (slots [40, 64))
     for (int qi = 0;; ++qi) {
       const int qs = qi % Cfg::QUEUE;
@@ -692,7 +750,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
             named_barrier_sync(1, 128);
             if (threadIdx.x == 0 && !*epi_abort) mbar_arrive(h_ready);
           } else {
-            ld_store_chunk<TOK>(p, st, f, 16 * ch, v);
+            ld_store_chunk<TOK>(p, st, f, 16 * ch, v, rstd, ss_smem, c.n_t);
           }
         } else {
 #pragma unroll
@@ -790,7 +848,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
 #pragma unroll
               for (int j = 0; j < 16; ++j) v[j] = silu_mul(v[j], w[j]);
             }
-            ld_store_chunk<TOK>(p, st, f, 16 * ch, v);
+            ld_store_chunk<TOK>(p, st, f, 16 * ch, v, rstd, ss_smem, c.n_t);
           }
           finished = true;
           named_barrier_sync(1, 128);

@@ -581,6 +581,13 @@ struct Workspace {
   // fails the call with SVDMLP_ERR_WORKSPACE, true runs the GEMM unsplit.
   bool unsplit_if_short = false;
   const ChainLink* chain = nullptr;  // set for the stages of a chained prefill layer
+  // Fused RMSNorm of a decoder block (see GemmParams): the stage that reads
+  // the block input scales rows by the norm; the residual stage writes the
+  // next block's statistics.
+  const float* norm_stats = nullptr;
+  int norm_parts = 0, norm_dim = 0, stats_ld = 0;
+  float norm_eps = 0.0f;
+  float* out_stats = nullptr;
 };
 
 static constexpr int64_t kCtlBytes = 256;
@@ -716,6 +723,10 @@ template <class Cfg>
 static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtensorMap& b, const CUtensorMap& b2,
                        const CUtensorMap& out, const CUtensorMap& out2, int M, int N, int K, int stage, const Workspace& w,
                        const bf16* residual, int64_t ld_res, cudaStream_t stream) {
+  // Only a residual stage whose tiles hold whole 128-column slices, one
+  // epilogue thread per row, writes the block statistics.
+  if (w.out_stats != nullptr && !(Cfg::EPI == EPI_RESID && Cfg::BN % 128 == 0 && Cfg::EPI_WARPS == 4))
+    return SVDMLP_ERR_INVALID_VALUE;
   DeviceInfo* dev = nullptr;
   SVD_CHECK(device_info(&dev));
   static std::mutex mu;
@@ -733,8 +744,10 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
     }
   }
   Plan pl = plan_for<Cfg>(M, N, K, dev->sms, g_split_override[stage]);
+  // chained stages publish whole tiles, and the block statistics are written
+  // per tile row by the unsplit epilogue: unsplit
   if ((partial_bytes(pl, Cfg::BN, Cfg::NB, Cfg::CTAS) > w.partial_cap && w.unsplit_if_short) ||
-      (w.chain && (pl.splits > 1 || pl.tail_start >= 0)))  // chained stages publish whole tiles: unsplit
+      ((w.chain || w.out_stats || w.norm_stats) && (pl.splits > 1 || pl.tail_start >= 0)))
     pl = plan_for<Cfg>(M, N, K, dev->sms, 1);
   GemmParams p{};
   p.M = M;
@@ -749,6 +762,12 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   p.tail_start = pl.tail_start >= 0 ? pl.tail_start : pl.units;
   p.tail_splits = pl.tail_splits;
   p.tail_kb_per_split = pl.tail_kb_per_split;
+  p.norm_stats = w.norm_stats;
+  p.norm_parts = w.norm_parts;
+  p.norm_dim = w.norm_dim;
+  p.norm_eps = w.norm_eps;
+  p.stats_ld = w.stats_ld;
+  p.out_stats = w.out_stats;
   p.partials = w.partials;
   p.counters = w.counters;
   p.err = w.err;
@@ -849,6 +868,12 @@ static int launch_gemv(const CUtensorMap& x, const CUtensorMap& x2, const CUtens
   p.num_units = pl.units;
   p.tail_start = pl.units;
   p.tail_splits = 1;
+  p.norm_stats = w.norm_stats;
+  p.norm_parts = w.norm_parts;
+  p.norm_dim = w.norm_dim;
+  p.norm_eps = w.norm_eps;
+  p.stats_ld = w.stats_ld;
+  p.out_stats = w.out_stats;
   p.partials = w.partials;
   p.counters = w.counters;
   p.err = w.err;
@@ -921,15 +946,21 @@ __global__ void transpose_pack_kernel(const bf16* __restrict__ src, long long ld
 // destination is src[k][n - row0], stored at tile (n / 16, k / 64), offset
 // (n % 16) * 64 + k % 64.  `kb_count` is the number of 64-column k-blocks of
 // the destination; destination columns k >= rows are written as zero.
+// `kscale` (nullable): each source row k is multiplied by kscale[k] in fp32
+// before the conversion (a decoder block's RMSNorm weight folded into the
+// first factors).
 template <typename TO>
 __global__ void tiled_pack_kernel(const bf16* __restrict__ src, long long ld_src, int rows, int cols,
-                                  TO* __restrict__ dst, int row0, int kb_count, int* range) {
+                                  TO* __restrict__ dst, int row0, int kb_count, int* range,
+                                  const bf16* __restrict__ kscale) {
   __shared__ float tile[32][33];
   const int k0 = blockIdx.x * 32;  // destination column (k) == source row
   const int n0 = blockIdx.y * 32;  // destination row offset within [0, cols)
   for (int y = threadIdx.y; y < 32; y += blockDim.y) {
     const int k = k0 + y, n = n0 + threadIdx.x;
-    tile[y][threadIdx.x] = (k < rows && n < cols) ? __bfloat162float(src[static_cast<long long>(k) * ld_src + n]) : 0.f;
+    float val = (k < rows && n < cols) ? __bfloat162float(src[static_cast<long long>(k) * ld_src + n]) : 0.f;
+    if (kscale != nullptr && k < rows) val *= __bfloat162float(kscale[k]);
+    tile[y][threadIdx.x] = val;
   }
   __syncthreads();
   for (int y = threadIdx.y; y < 32; y += blockDim.y) {
@@ -981,6 +1012,28 @@ __global__ void rmsnorm_kernel(const bf16* __restrict__ x, long long ld_x, const
     yr[i] = __float2bfloat16(__bfloat162float(xr[i]) * rstd * __bfloat162float(w[i]));
 }
 
+// Per row of x [M, n], the sum of squares of each 128-column slice:
+// stats[row * ld_stats + slice] (the statistics a block's fused RMSNorm reads
+// for the first block of a stack; later blocks get them from the previous
+// block's residual epilogue).  One CTA per row, a warp per slice.
+__global__ void row_sumsq_kernel(const bf16* __restrict__ x, long long ld_x, int n, float* __restrict__ stats,
+                                 long long ld_stats) {
+  const bf16* xr = x + static_cast<long long>(blockIdx.x) * ld_x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const int slices = (n + 127) / 128;
+  for (int sl = warp; sl < slices; sl += nwarps) {
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int c = sl * 128 + j * 32 + lane;
+      const float v = c < n ? __bfloat162float(xr[c]) : 0.f;
+      ss += v * v;
+    }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (lane == 0) stats[static_cast<long long>(blockIdx.x) * ld_stats + sl] = ss;
+  }
+}
+
 // One CTA that waits, bounded, on an mbarrier nothing will complete.
 __global__ void wait_probe_kernel(int* err, unsigned long long limit_ns) {
   __shared__ uint64_t bar;
@@ -1010,12 +1063,13 @@ static int launch_convert(const TI* src, int64_t ld_src, TO* dst, int64_t ld_dst
 
 template <typename TO>
 static int launch_tiled_pack(const void* src, int64_t ld_src, int rows, int cols, void* dst, int row0, int64_t k,
-                             int* range, cudaStream_t s) {
+                             int* range, cudaStream_t s, const void* kscale = nullptr) {
   if (!src || !dst || rows <= 0 || cols <= 0 || ld_src < cols || row0 % 16 != 0) return SVDMLP_ERR_INVALID_VALUE;
   const int kb = static_cast<int>(cdiv(k, 64));
   dim3 grid(static_cast<unsigned>(cdiv(static_cast<int64_t>(kb) * 64, 32)), static_cast<unsigned>(cdiv(cols, 32)));
   tiled_pack_kernel<TO><<<grid, dim3(32, 8), 0, s>>>(static_cast<const bf16*>(src), ld_src, rows, cols,
-                                                     static_cast<TO*>(dst), row0, kb, range);
+                                                     static_cast<TO*>(dst), row0, kb, range,
+                                                     static_cast<const bf16*>(kscale));
   SVD_CUDA(cudaGetLastError());
   g_launches.fetch_add(1);
   return SVDMLP_OK;
@@ -1329,6 +1383,11 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
   prm.pf_ahead = g_pf_ahead;
   prm.pf_wait = g_pf_wait;
   prm.pdl_units = g_layer_decode_pdl;
+  prm.norm_stats = w.norm_stats;
+  prm.norm_parts = w.norm_parts;
+  prm.norm_dim = w.norm_dim;
+  prm.norm_eps = w.norm_eps;
+  prm.stats_ld = w.stats_ld;
   const int64_t n1 = 2LL * L->rp_gu;
   // stage operands: token tiles (box TOK rows) and weight panels (box 128 rows)
   struct Spec {
@@ -1400,6 +1459,8 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
       pb = 0;
     }
     d.out = con ? nullptr : sp.out;
+    d.norm = (st == 0 && w.norm_stats != nullptr) ? 1 : 0;
+    d.out_stats = st == 3 ? w.out_stats : nullptr;
     d.ld_out = sp.ld_out;
     d.partials = part;
     d.tile_counters = w.counters + st * 65536;
@@ -1522,9 +1583,33 @@ int svdmlp_transpose_pack(const void* src, int64_t ld_src, int rows, int cols, v
                                 static_cast<cudaStream_t>(stream));
 }
 
+static int pack_impl(const svdmlp_layout* L, const void* u_gate, int64_t ld_ug, const void* v_gate, int64_t ld_vg,
+                     const void* u_up, int64_t ld_uu, const void* v_up, int64_t ld_vu, const void* u_down,
+                     int64_t ld_ud, const void* v_down, int64_t ld_vd, void* packed, void* stream,
+                     const void* norm_w);
+
 int svdmlp_pack(const svdmlp_layout* L, const void* u_gate, int64_t ld_ug, const void* v_gate, int64_t ld_vg,
                 const void* u_up, int64_t ld_uu, const void* v_up, int64_t ld_vu, const void* u_down, int64_t ld_ud,
                 const void* v_down, int64_t ld_vd, void* packed, void* stream) {
+  return pack_impl(L, u_gate, ld_ug, v_gate, ld_vg, u_up, ld_uu, v_up, ld_vu, u_down, ld_ud, v_down, ld_vd, packed,
+                   stream, nullptr);
+}
+
+int svdmlp_pack_block(const svdmlp_layout* L, const void* norm_weight, const void* u_gate, int64_t ld_ug,
+                      const void* v_gate, int64_t ld_vg, const void* u_up, int64_t ld_uu, const void* v_up,
+                      int64_t ld_vu, const void* u_down, int64_t ld_ud, const void* v_down, int64_t ld_vd,
+                      void* packed, void* stream) {
+  if (!norm_weight) return SVDMLP_ERR_INVALID_VALUE;
+  return pack_impl(L, u_gate, ld_ug, v_gate, ld_vg, u_up, ld_uu, v_up, ld_vu, u_down, ld_ud, v_down, ld_vd, packed,
+                   stream, norm_weight);
+}
+
+}  // extern "C"
+
+static int pack_impl(const svdmlp_layout* L, const void* u_gate, int64_t ld_ug, const void* v_gate, int64_t ld_vg,
+                     const void* u_up, int64_t ld_uu, const void* v_up, int64_t ld_vu, const void* u_down,
+                     int64_t ld_ud, const void* v_down, int64_t ld_vd, void* packed, void* stream,
+                     const void* norm_w) {
   SVD_CHECK(check_layout(L));
   if (L->kind != SVDMLP_KIND_SVD || !packed) return SVDMLP_ERR_INVALID_VALUE;
   if ((reinterpret_cast<uintptr_t>(packed) & 255u) != 0) return SVDMLP_ERR_ALIGNMENT;
@@ -1535,8 +1620,8 @@ int svdmlp_pack(const svdmlp_layout* L, const void* u_gate, int64_t ld_ug, const
   if (L->r_gu > 0) {
     if (!u_gate || !v_gate || !u_up || !v_up) return SVDMLP_ERR_INVALID_VALUE;
     // w1 [2*rp_gu, d] (bf16: it multiplies the bf16 input X): u_gate^T, then u_up^T
-    SVD_CHECK(launch_tiled_pack<bf16>(u_gate, ld_ug, L->d, L->r_gu, P + L->off_w1, 0, L->d, range, s));
-    SVD_CHECK(launch_tiled_pack<bf16>(u_up, ld_uu, L->d, L->r_gu, P + L->off_w1, L->rp_gu, L->d, range, s));
+    SVD_CHECK(launch_tiled_pack<bf16>(u_gate, ld_ug, L->d, L->r_gu, P + L->off_w1, 0, L->d, range, s, norm_w));
+    SVD_CHECK(launch_tiled_pack<bf16>(u_up, ld_uu, L->d, L->r_gu, P + L->off_w1, L->rp_gu, L->d, range, s, norm_w));
     // v [r, ff] -> v^T [ff, r] (fp16: it multiplies the fp16 XU)
     SVD_CHECK(launch_tiled_pack<__half>(v_gate, ld_vg, L->r_gu, L->ff, P + L->off_vg, 0, L->r_gu, range, s));
     SVD_CHECK(launch_tiled_pack<__half>(v_up, ld_vu, L->r_gu, L->ff, P + L->off_vu, 0, L->r_gu, range, s));
@@ -1552,6 +1637,8 @@ int svdmlp_pack(const svdmlp_layout* L, const void* u_gate, int64_t ld_ug, const
   }
   return SVDMLP_OK;
 }
+
+extern "C" {
 
 int svdmlp_dense_pack(const svdmlp_layout* L, const void* w_gate, int64_t ld_wg, const void* w_up, int64_t ld_wu,
                       const void* w_down, int64_t ld_wd, void* packed, void* stream) {
@@ -1746,6 +1833,48 @@ static int forward_impl(const svdmlp_layout* L, const void* packed, const void* 
 }
 
 extern "C" {
+
+int svdmlp_row_sumsq(const void* x, int64_t ldx, int M, int n, float* stats, int64_t ld_stats, void* stream) {
+  if (!x || !stats || M <= 0 || n <= 0 || ldx < n || ld_stats < cdiv(n, 128)) return SVDMLP_ERR_INVALID_VALUE;
+  row_sumsq_kernel<<<static_cast<unsigned>(M), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const bf16*>(x), ldx, n, stats, ld_stats);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+int svdmlp_forward_block(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* y,
+                         int64_t ldy, const float* x_stats, int64_t ld_stats, float* y_stats, float eps, void* ws,
+                         int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || L->r_d <= 0 || !packed || !x || !y || !x_stats || M <= 0 ||
+      ldx < L->d || ldy < L->d || ld_stats < cdiv(L->d, 128) || !(eps >= 0.0f) || x == y)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if (!aligned16(x, ldx)) return SVDMLP_ERR_ALIGNMENT;  // x is also the residual, read in place
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  Workspace wn = w, wo = w;  // the first stage (norm) and the residual stage (statistics)
+  wn.norm_stats = x_stats;
+  wn.norm_parts = static_cast<int>(cdiv(L->d, 128));
+  wn.norm_dim = L->d;
+  wn.norm_eps = eps;
+  wn.stats_ld = static_cast<int>(ld_stats);
+  wo.stats_ld = static_cast<int>(ld_stats);
+  wo.out_stats = y_stats;
+  if (M <= g_layer_decode_max_m) {
+    Workspace wb = wn;
+    wb.out_stats = y_stats;
+    return run_layer_decode(L, P, x, ldx, M, y, ldy, x, ldx, wb, s, M <= g_decode_contract);
+  }
+  const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
+  SVD_CHECK(run_xu(L, P, x, ldx, M, wn, s));
+  SVD_CHECK(run_gu(L, P, M, w.h, L->ld_ff, false, w, s));
+  SVD_CHECK(run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, 0, w, s));
+  SVD_CHECK(run_down_v(L, P, M, yt.ptr, yt.ld, x, ldx, wo, s));
+  return finish_output(y, ldy, yt.ptr, yt.ld, M, L->d, s);
+}
 
 int svdmlp_dense_forward(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M, void* y,
                          int64_t ldy, const void* residual, int64_t ld_res, void* ws, int64_t ws_bytes,

@@ -75,6 +75,9 @@ SIGNATURES = {
     "svdmlp_forward": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
     "svdmlp_dense_forward": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
     "svdmlp_forward_contracted": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, I64, V]),
+    "svdmlp_forward_block": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V, c_float, V, I64, V]),
+    "svdmlp_row_sumsq": (c_int, [V, I64, c_int, c_int, V, I64, V]),
+    "svdmlp_pack_block": (c_int, [LP, V, V, I64, V, I64, V, I64, V, I64, V, I64, V, I64, V, V]),
     "svdmlp_set_decode_contract": (c_int, [c_int]),
     "svdmlp_down_partial": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),
     "svdmlp_forward_partial": (c_int, [LP, V, V, I64, c_int, V, I64, V, I64, V]),

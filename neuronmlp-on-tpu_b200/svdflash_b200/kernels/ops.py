@@ -40,7 +40,8 @@ __all__ = [
     "PackedLayer", "pack_svd_layer", "pack_dense_layer", "low_rank_dim", "rank_for_ratio", "silu",
     "fused_gate_up", "fused_xuv", "xuv_matmul", "svd_mlp", "contracted_svd_mlp", "dense_mlp",
     "dense_matmul", "svd_mlp_packed", "contracted_mlp_packed", "dense_mlp_packed", "gate_up_packed", "xuv_packed",
-    "forward_partial_packed", "down_partial_packed", "down_finish_packed", "rmsnorm", "workspace_for",
+    "forward_partial_packed", "down_partial_packed", "down_finish_packed", "rmsnorm", "row_sumsq",
+    "svd_block_packed", "workspace_for",
     "check_device_status", "launch_count",
 ]
 
@@ -190,10 +191,13 @@ class PackedLayer:
         return int(self.layout.packed_bytes)
 
 
-def pack_svd_layer(u_gate=None, v_gate=None, u_up=None, v_up=None, u_down=None, v_down=None) -> PackedLayer:
+def pack_svd_layer(u_gate=None, v_gate=None, u_up=None, v_up=None, u_down=None, v_down=None,
+                   norm_weight=None) -> PackedLayer:
     """Packs factor pairs in the reference layouts (u [in, r], v [r, out]).
 
-    Either half may be omitted (gate/up-only or down-only layers)."""
+    Either half may be omitted (gate/up-only or down-only layers).  With
+    `norm_weight` ([d]) the layer is packed for svd_block_packed: the decoder
+    block's RMSNorm weight is folded into u_gate and u_up."""
     have_gu = u_gate is not None
     have_d = u_down is not None
     if not have_gu and not have_d:
@@ -227,10 +231,21 @@ def pack_svd_layer(u_gate=None, v_gate=None, u_up=None, v_up=None, u_down=None, 
     args = []
     for a in bf:
         args += [_ptr(a), 0 if a is None else _ld(a)]
-    _lib.check(lib.svdmlp_pack(ctypes.byref(layout), *args, packed.data_ptr(), _stream(dev)), "pack")
+    if norm_weight is not None:
+        if not (have_gu and have_d):
+            raise ValueError("a block's norm needs a full SVD layer")
+        nw = _bf16(norm_weight).reshape(-1).contiguous()
+        if nw.numel() != d or nw.device != dev:
+            raise ValueError("norm_weight must be [d] on the factors' device: dimensions do not match")
+        _lib.check(lib.svdmlp_pack_block(ctypes.byref(layout), nw.data_ptr(), *args, packed.data_ptr(),
+                                         _stream(dev)), "pack_block")
+    else:
+        _lib.check(lib.svdmlp_pack(ctypes.byref(layout), *args, packed.data_ptr(), _stream(dev)), "pack")
     # packing is a set-up step: synchronise once to refuse weights fp16 cannot hold
     _lib.check(lib.svdmlp_pack_status(ctypes.byref(layout), packed.data_ptr(), _stream(dev)), "pack")
-    return PackedLayer(layout, packed)
+    layer = PackedLayer(layout, packed)
+    layer.normed = norm_weight is not None
+    return layer
 
 
 def pack_dense_layer(w_gate, w_up, w_down) -> PackedLayer:
@@ -327,6 +342,48 @@ def svd_mlp_packed(layer: PackedLayer, x: torch.Tensor, residual: Optional[torch
     _lib.check(_lib.load().svdmlp_forward(
         ctypes.byref(layer.layout), layer.packed.data_ptr(), xb.data_ptr(), _ld(xb), m, y.data_ptr(), _ld(y),
         _ptr(res), 0 if res is None else _ld(res), ws.ptr, ws.nbytes, _stream(xb.device)), "svd_mlp")
+    return y
+
+
+def row_sumsq(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per row of x [M, d], the sum of squares of each 128-column slice, fp32
+    [M, ceil(d / 128)]: the statistics the first block of a stack reads."""
+    xb = _bf16(x)
+    if xb.stride(1) != 1:
+        xb = xb.contiguous()
+    m, d = xb.shape
+    parts = -(-d // 128)
+    if out is None:
+        out = torch.empty((m, parts), dtype=torch.float32, device=xb.device)
+    if out.dtype != torch.float32 or out.shape[0] < m or out.shape[1] < parts or out.stride(1) != 1:
+        raise ValueError("stats must be fp32 [M, ceil(d / 128)]")
+    _lib.check(_lib.load().svdmlp_row_sumsq(xb.data_ptr(), _ld(xb), m, d, out.data_ptr(), out.stride(0),
+                                            _stream(xb.device)), "row_sumsq")
+    return out
+
+
+def svd_block_packed(layer: PackedLayer, x: torch.Tensor, x_stats: torch.Tensor,
+                     y_stats: Optional[torch.Tensor] = None, eps: float = 1e-5,
+                     out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One decoder-stack block y = x + mlp(rmsnorm(x)) with the norm fused
+    (svdmlp_forward_block): `layer` packed with its norm weight, `x_stats` the
+    per-slice sums of squares of x (row_sumsq, or the previous block's
+    y_stats); y_stats, when given, receives the same statistics of y."""
+    if not getattr(layer, "normed", False):
+        raise ValueError("svd_block_packed needs a layer packed with norm_weight")
+    xb = _prep_x(x, layer.d)
+    m = xb.shape[0]
+    y = out if out is not None else _out(m, layer.d, xb.device)
+    for st in (x_stats, y_stats):
+        if st is not None and (st.dtype != torch.float32 or st.stride(1) != 1 or st.shape[0] < m):
+            raise ValueError("block statistics must be fp32 [M, ceil(d / 128)] row-major")
+    if y_stats is not None and y_stats.stride(0) != x_stats.stride(0):
+        raise ValueError("x_stats and y_stats must share their row stride")
+    ws = layer.workspace(m)
+    _lib.check(_lib.load().svdmlp_forward_block(
+        ctypes.byref(layer.layout), layer.packed.data_ptr(), xb.data_ptr(), _ld(xb), m, y.data_ptr(), _ld(y),
+        x_stats.data_ptr(), x_stats.stride(0), _ptr(y_stats), float(eps), ws.ptr, ws.nbytes,
+        _stream(xb.device)), "svd_block")
     return y
 
 
