@@ -341,15 +341,16 @@ def run_sweep(args) -> None:
             the three factor pairs once + x and y, against the measured copy bandwidth.
     shapes  config 5: ratio {0.4, 0.6, 0.8, 0.9, 1.0 = dense} x seq {512..8192} x batch
             {1, 4}; SVD/dense speed-up and tensor roofline fraction.
-    stack   config 3: 32 blocks of x + mlp(rmsnorm(x)) at seq {1024, 4096}, SVD (0.9) and
-            dense arms, each captured as one CUDA graph.
+    stack   config 3: 32 blocks of x + mlp(rmsnorm(x)) at seq {1, 16, 1024, 4096}: SVD (0.9)
+            with a separate RMSNorm kernel per block, SVD with the norm fused into the
+            block (svd_fused) and dense arms, each captured as one CUDA graph.
     Weights are synthetic seeded draws of the named shapes; every point streams factor
     matrices larger than L2 per call, so no flush is needed between calls."""
     import torch
 
     from svdflash_b200 import _lib
     from svdflash_b200.kernels import ops
-    from svdflash_b200.models import DenseLlamaMLP, MlpBlockStack, SvdLlamaMLP
+    from svdflash_b200.models import DenseLlamaMLP, MlpBlockStack, SvdLlamaMLP, SvdMlpBlock
     _lib.load()
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -412,18 +413,22 @@ def run_sweep(args) -> None:
         gn = torch.Generator(device=dev)
         gn.manual_seed(args.seed + 99)
         norms = [(1 + 0.02 * torch.randn(d, generator=gn, device=dev)).to(torch.bfloat16) for _ in range(n_layers)]
-        for arm in ("svd", "dense"):
+        for arm in ("svd", "svd_fused", "dense"):
             if arm == "svd":
                 mlps = [SvdLlamaMLP(*make_factors(d, ff, r, args.seed + 1000 + l, dev)) for l in range(n_layers)]
+            elif arm == "svd_fused":
+                mlps = [SvdMlpBlock(*make_factors(d, ff, r, args.seed + 1000 + l, dev), norms[l])
+                        for l in range(n_layers)]
             else:
                 mlps = [DenseLlamaMLP(*dense_w(args.seed + 2000 + l)) for l in range(n_layers)]
             stack = MlpBlockStack(mlps, norms)
-            for seq in (1024, 4096):
+            for seq in (1, 16, 1024, 4096):
                 x = torch.randn(seq, d, device=dev).to(torch.bfloat16)
                 stack.capture(seq, d, dev)
                 ms = _time_events(lambda: stack.replay(x), max(3, min(args.steps, 50)), args.warmup)
-                fl = n_layers * 6.0 * seq * (r * (d + ff) if arm == "svd" else d * ff)
-                emit({"sweep": "stack", "arm": arm, "layers": n_layers, "seq": seq, "ratio": ratio if arm == "svd" else 1.0,
+                fl = n_layers * 6.0 * seq * (d * ff if arm == "dense" else r * (d + ff))
+                emit({"sweep": "stack", "arm": arm, "layers": n_layers, "seq": seq,
+                      "ratio": 1.0 if arm == "dense" else ratio, "us_per_block": ms * 1e3 / n_layers,
                       "ms_per_stack": ms, "tokens_per_s": seq / (ms * 1e-3), "tflops": fl / (ms * 1e-3) / 1e12,
                       "graph": True})
                 stack._graph = None
@@ -450,6 +455,40 @@ def profile_layer(args) -> None:
     print(json.dumps({"profile_layer": args.profile_layer, "calls": 3}), flush=True)
 
 
+def profile_stack(args) -> None:
+    """A fixed sequence for the launch list of config 3: 32 blocks of the 8B
+    layer (r = 2867) on M tokens, first with the RMSNorm fused into each block
+    (SvdMlpBlock), then with a separate RMSNorm kernel per block (SvdLlamaMLP);
+    each stack is captured as one CUDA graph (one eager warm-up pass inside
+    capture()) and replayed twice."""
+    import torch
+
+    from svdflash_b200.kernels import ops
+    from svdflash_b200.models import MlpBlockStack, SvdLlamaMLP, SvdMlpBlock
+    dev = torch.device("cuda", 0)
+    d, ff, n_layers = 4096, 14336, 32
+    r = rank_for(d, ff, 0.9)
+    gn = torch.Generator(device=dev)
+    gn.manual_seed(args.seed + 99)
+    norms = [(1 + 0.02 * torch.randn(d, generator=gn, device=dev)).to(torch.bfloat16) for _ in range(n_layers)]
+    x = torch.randn(args.profile_stack, d, device=dev).to(torch.bfloat16)
+    for arm in ("svd_fused", "svd"):
+        if arm == "svd_fused":
+            mlps = [SvdMlpBlock(*make_factors(d, ff, r, args.seed + 1000 + l, dev), norms[l]) for l in range(n_layers)]
+        else:
+            mlps = [SvdLlamaMLP(*make_factors(d, ff, r, args.seed + 1000 + l, dev)) for l in range(n_layers)]
+        stack = MlpBlockStack(mlps, norms)
+        stack.capture(args.profile_stack, d, dev)
+        for _ in range(2):
+            stack.replay(x)
+        torch.cuda.synchronize()
+        stack._graph = None
+        del mlps, stack
+        torch.cuda.empty_cache()
+    ops.check_device_status(dev)
+    print(json.dumps({"profile_stack": args.profile_stack, "layers": n_layers, "replays": 2}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
@@ -462,6 +501,9 @@ def main():
     ap.add_argument("--no-decode", action="store_true", help="N=1: leave out the decode (config 2) sub-record")
     ap.add_argument("--profile-layer", type=int, default=0, metavar="M",
                     help="profiling target: pack the 8B layer, run it three times on M tokens, exit")
+    ap.add_argument("--profile-stack", type=int, default=0, metavar="M",
+                    help="profiling target: the 32-block stack (fused and unfused RMSNorm) on M tokens, "
+                         "captured and replayed twice each, exit")
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--tp-mode", choices=("auto", "allreduce", "split"), default="auto",
                     help="N>1: one all-reduce of the partial (default) or the all-gather split of the replicated stages")
@@ -475,6 +517,9 @@ def main():
         return
     if args.profile_layer:
         profile_layer(args)
+        return
+    if args.profile_stack:
+        profile_stack(args)
         return
     wl = WORKLOADS[args.workload]
     if args.impl == "reference":

@@ -272,6 +272,22 @@ SVD_DEV float silu_mul(float g, float u) {
   return __fdividef(g, 1.0f + __expf(-g)) * u;
 }
 
+// Fused RMSNorm row scale rsqrt(sum_j stats[row, j] / dim + eps).  The sum
+// runs in j order (every kernel computes the same value from the same
+// statistics), with sixteen loads in flight at a time.
+SVD_DEV float norm_row_scale(const float* stats, long long ld, int parts, int dim, float eps, int row) {
+  const float* s = stats + static_cast<long long>(row) * ld;
+  float sum = 0.0f;
+  for (int j0 = 0; j0 < parts; j0 += 16) {
+    float v[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) v[j] = j0 + j < parts ? s[j0 + j] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) sum += v[j];  // + 0.0f past the end leaves the sum as it is
+  }
+  return rsqrtf(sum / static_cast<float>(dim) + eps);
+}
+
 // Applies the epilogue to one 32-column chunk of this thread's row.
 template <class Cfg>
 SVD_DEV void epilogue_math(const GemmParams& p, float (&v)[32], const float (&u)[32], int row, int col) {
@@ -557,10 +573,20 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     constexpr int EPI_THREADS = 32 * Cfg::EPI_WARPS;
     int stg_buf = 0;
     int acc_it = 0;
+    // The fused norm's statistics come from the previous launch: wait for it
+    // (as the producer does) so that each unit's row scale can be read before
+    // its accumulator is ready.
+    if (p.norm_stats != nullptr) grid_dependency_wait();
     for (int u = unit0; u < p.num_units; u += unit_step) {
       const UnitCoord c = decode_unit(p, u);
       const int b = acc_it % Cfg::ACC_BUFS;
       const uint32_t aph = static_cast<uint32_t>(acc_it / Cfg::ACC_BUFS) & 1u;
+      const int row_base = c.m_t * Cfg::TILE_M + static_cast<int>(rank) * Cfg::BM;  // this CTA's first row
+      const int row_in_tile = q * 32 + static_cast<int>(lane);
+      const int grow = row_base + row_in_tile;
+      float rscale = 1.0f;  // RMSNorm row scale (1 without a fused norm)
+      if (p.norm_stats != nullptr && c.nsplit == 1 && grow < p.M)
+        rscale = norm_row_scale(p.norm_stats, p.stats_ld, p.norm_parts, p.norm_dim, p.norm_eps, grow);
       bool ok = mbar_wait(&acc_full[b], aph, ctx, SITE_EPI_ACC_FULL);
       ok = __all_sync(0xffffffffu, ok);
       // The epilogue warps take the same decision, so that none of them is
@@ -570,19 +596,10 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
       if (*epi_abort) break;
       tc_fence_after();
       const uint32_t tacc = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(b * Cfg::ACC_STRIDE);
-      const int row_base = c.m_t * Cfg::TILE_M + static_cast<int>(rank) * Cfg::BM;  // this CTA's first row
-      const int row_in_tile = q * 32 + static_cast<int>(lane);
-      const int grow = row_base + row_in_tile;
       const int n0 = c.n_t * Cfg::BN;
       const int y_box = row_base + q * 32;
 
       if (c.nsplit == 1) {
-        float rscale = 1.0f;  // RMSNorm row scale (1 without a fused norm)
-        if (p.norm_stats != nullptr && grow < p.M) {
-          float ssum = 0.0f;
-          for (int j = 0; j < p.norm_parts; ++j) ssum += p.norm_stats[static_cast<long long>(grow) * p.stats_ld + j];
-          rscale = rsqrtf(ssum / static_cast<float>(p.norm_dim) + p.norm_eps);
-        }
         float slice_ss[Cfg::BN / 128 > 0 ? Cfg::BN / 128 : 1] = {};
 #pragma unroll 1
         for (int ch = half; ch < NCH; ch += CH_STEP) {

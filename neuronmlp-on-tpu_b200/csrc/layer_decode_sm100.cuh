@@ -592,11 +592,8 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
     if (p.norm_stats != nullptr) {
       // fused RMSNorm: each token's row scale, from the previous block's
       // per-slice sums of squares, summed in slice order
-      for (int t = threadIdx.x; t < min(p.M, TOK); t += 128) {
-        float ssum = 0.0f;
-        for (int j = 0; j < p.norm_parts; ++j) ssum += p.norm_stats[static_cast<long long>(t) * p.stats_ld + j];
-        rstd[t] = rsqrtf(ssum / static_cast<float>(p.norm_dim) + p.norm_eps);
-      }
+      for (int t = threadIdx.x; t < min(p.M, TOK); t += 128)
+        rstd[t] = norm_row_scale(p.norm_stats, p.stats_ld, p.norm_parts, p.norm_dim, p.norm_eps, t);
       named_barrier_sync(1, 128);
     }
     int ntr = 40;  // epilogue trace events (slots [40, 64))
