@@ -507,6 +507,9 @@ def main():
     ap.add_argument("--cpu-reps", type=int, default=3)
     ap.add_argument("--tp-mode", choices=("auto", "allreduce", "split"), default="auto",
                     help="N>1: one all-reduce of the partial (default) or the all-gather split of the replicated stages")
+    ap.add_argument("--tp-collectives", choices=("auto", "nccl", "peer"), default="auto",
+                    help="N>1: the library's peer-memory collectives over NVLink (auto, when every GPU can "
+                         "address every other) or NCCL")
     ap.add_argument("--sweep", choices=("decode", "shapes", "stack"), default=None,
                     help="print one JSON line per point of BASELINE configs 2, 5 or 3 instead of the bench line")
     args = ap.parse_args()
@@ -565,7 +568,8 @@ def main():
         def step(inp, out=y):
             return ops.svd_mlp_packed(layer, inp, out=out)
     else:
-        tp = TensorParallelSvdMlp(*factors, rank=rank, world=world, mode=args.tp_mode)
+        tp = TensorParallelSvdMlp(*factors, rank=rank, world=world, mode=args.tp_mode,
+                                  collectives=args.tp_collectives)
         y = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
 
         def step(inp, out=y):
@@ -681,6 +685,8 @@ def main():
         decode = decode_record(dev, args.seed, args.steps, args.warmup, float(pk["hbm_gbs"]), pk_src)
 
     if world > 1:
+        tp.check_peer_status()   # an expired wait or a saturated sum in the peer collectives raises here
+        tp.close()
         dist.barrier(device_ids=[local])
         dist.destroy_process_group()
     if rank != 0:
@@ -737,8 +743,10 @@ def main():
         "data": "synthetic",
         "config": workload_config(args.workload, wl),
         "parallelism": f"tp-ff{world}" if world > 1 else "single-gpu",
-        "collectives": ("split: all-gather XU, reduce-scatter fp16 partial, all-gather y"
-                        if tp._use_split(m, d) else "one NCCL all-reduce of the fp16 [M, r] partial")
+        "collectives": (("split: all-gather XU, reduce-scatter fp16 partial, all-gather y"
+                         if tp._use_split(m, d) else "one all-reduce of the fp16 [M, r] partial")
+                        + (" (the library's kernels over NVLink peer memory)" if tp.peer_collectives()
+                           else " (NCCL)"))
                        if world > 1 else None,
         "us_per_layer": ms_per_step * 1e3,
         "tflops": flops_layer / (ms_per_step * 1e-3) / 1e12,

@@ -15,9 +15,11 @@
  * Conventions
  *  - Every entry point returns an int status: 0 = SVDMLP_OK, negative = error.
  *  - All device buffers are owned by the caller; no entry point allocates
- *    device memory, and none synchronises the stream except the status
+ *    device memory except svdmlp_peer_alloc (the buffer peers map, freed with
+ *    svdmlp_peer_free), and none synchronises the stream except the status
  *    reads (svdmlp_check_device_status, svdmlp_pack_status,
- *    svdmlp_xuv_noalloc_status).
+ *    svdmlp_xuv_noalloc_status, svdmlp_peer_check_status) and
+ *    svdmlp_peer_alloc.
  *  - Matrices are row-major bf16 (uint16 storage) with an explicit leading
  *    dimension in elements; `void*` pointers are device pointers.
  *  - Work is enqueued on `stream` (a cudaStream_t passed as void*; NULL is the
@@ -444,6 +446,59 @@ int svdmlp_stage_times(double* ms_out, int64_t* counts_out, int n);
 
 /* Number of kernel launches the library has enqueued since load (all entry points). */
 int64_t svdmlp_launch_count(void);
+
+/*
+ * Collectives of the ff-sharded layer over NVLink peer memory, one process per
+ * GPU.  The reference has no multi-device path (models/README.md:26-27); these
+ * are the exchanges of the tensor-parallel layer (the all-reduce of the
+ * [M, r_down] partial, and the all-gather / reduce-scatter of its split form),
+ * done by the library's own kernels with plain stores between GPUs (NVLink).
+ *
+ * Every rank allocates one peer buffer of the same size and layout
+ * (svdmlp_peer_alloc, zeroed; its first svdmlp_peer_signal_bytes() bytes are
+ * the group's signal area), sends the 64-byte handle to the other ranks, and
+ * maps theirs (svdmlp_peer_open; not its own).  A collective gets `bases`, the
+ * `world` buffers as mapped in this process in rank order (bases[rank] = its
+ * own), and a matrix at byte offset `off` of every buffer (off >= the signal
+ * area, 16-byte aligned; rows of 16-byte multiples).  Row blocks: rank q owns
+ * rows [q R, min(M, (q + 1) R)), R = ceil(M / world).  Every rank must make the
+ * same collective calls in the same order on its own stream; each call waits
+ * (bounded) for the others.  A wait that expires leaves the group in error:
+ * svdmlp_peer_check_status reports SVDMLP_ERR_DEVICE_TIMEOUT from then on, and
+ * the buffers must be freed and allocated again.  world <= 8.
+ */
+int64_t svdmlp_peer_signal_bytes(void);
+int svdmlp_peer_alloc(int64_t bytes, void** ptr, void* handle);
+int svdmlp_peer_open(const void* handle, void** peer_ptr);
+int svdmlp_peer_close(void* peer_ptr);
+int svdmlp_peer_free(void* ptr);
+
+/* In-place sum of the fp16 [M, c] matrix (row stride ld elements; c and ld
+ * multiples of 8) over the ranks: the reduced rows replace every rank's copy.
+ * Every rank stores its partial rows of each owner into that owner's scratch
+ * (at byte offset off_scratch, svdmlp_peer_scratch_bytes(world, m, c) bytes,
+ * not overlapping the matrix); each owner sums its rows in rank order in fp32,
+ * rounds once to fp16 (every rank gets the same bits) and stores them into
+ * every rank's matrix.  A sum beyond fp16's range sets the range flag that
+ * svdmlp_peer_check_status reports. */
+int64_t svdmlp_peer_scratch_bytes(int world, int m, int c);
+int svdmlp_peer_allreduce_f16(void* const* bases, int world, int rank, int64_t off, int m, int c, int64_t ld,
+                              int64_t off_scratch, void* stream);
+
+/* This rank's rows of the same sum into `out` (a local fp16 [R, c] matrix,
+ * row stride ld_out). */
+int svdmlp_peer_reduce_scatter_f16(void* const* bases, int world, int rank, int64_t off, int m, int c, int64_t ld,
+                                   int64_t off_scratch, void* out, int64_t ld_out, void* stream);
+
+/* Each rank has written its own rows of an [M, row_bytes] matrix (row stride
+ * ld_bytes) in its buffer; stores them into every other rank's copy. */
+int svdmlp_peer_allgather(void* const* bases, int world, int rank, int64_t off, int m, int64_t row_bytes,
+                          int64_t ld_bytes, void* stream);
+
+/* Reads this rank's group error block (synchronises the stream): an expired
+ * wait (SVDMLP_ERR_DEVICE_TIMEOUT, sticky) or a saturated fp16 sum
+ * (SVDMLP_ERR_RANGE, cleared by the read). */
+int svdmlp_peer_check_status(void* own_base, void* stream);
 
 #ifdef __cplusplus
 }

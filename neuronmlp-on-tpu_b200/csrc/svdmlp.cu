@@ -20,6 +20,7 @@
 #include "gemm_sm100.cuh"
 #include "gemv_sm100.cuh"
 #include "layer_decode_sm100.cuh"
+#include "peer_sm100.cuh"
 
 using bf16 = __nv_bfloat16;
 
@@ -2324,6 +2325,143 @@ int svdmlp_plan_info(int stage, int M, int N, int K, int* out6) {
   out6[4] = p.units;
   out6[5] = p.grid;
   return SVDMLP_OK;
+}
+
+}  // extern "C"
+
+// ----------------------------------------------------------------------------
+// Collectives over NVLink peer memory (peer_sm100.cuh).
+namespace svdmlp {
+static int make_peer_args(void* const* bases, int world, int rank, PeerArgs* a) {
+  if (!bases || world < 1 || world > kPeerMaxRanks || rank < 0 || rank >= world) return SVDMLP_ERR_INVALID_VALUE;
+  std::memset(a, 0, sizeof(*a));
+  for (int i = 0; i < world; ++i) {
+    if (!bases[i] || (reinterpret_cast<uintptr_t>(bases[i]) & 255u) != 0) return SVDMLP_ERR_ALIGNMENT;
+    a->base[i] = static_cast<unsigned char*>(bases[i]);
+  }
+  a->world = world;
+  a->rank = rank;
+  a->limit_ns = g_wait_limit_ns;
+  return SVDMLP_OK;
+}
+
+static int peer_grid(unsigned* grid) {
+  DeviceInfo* dev = nullptr;
+  SVD_CHECK(device_info(&dev));
+  *grid = static_cast<unsigned>(std::min(kPeerMaxCtas, dev->sms));
+  return SVDMLP_OK;
+}
+
+static bool peer_matrix_ok(int64_t off, int m, int64_t row_bytes, int64_t ld_bytes) {
+  return m > 0 && row_bytes > 0 && row_bytes % 16 == 0 && ld_bytes >= row_bytes && ld_bytes % 16 == 0 &&
+         off >= kPeerSignalBytes && off % 16 == 0;
+}
+}  // namespace svdmlp
+
+extern "C" {
+
+int64_t svdmlp_peer_signal_bytes(void) { return kPeerSignalBytes; }
+
+int svdmlp_peer_alloc(int64_t bytes, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes <= kPeerSignalBytes) return SVDMLP_ERR_INVALID_VALUE;
+  void* p = nullptr;
+  SVD_CUDA(cudaMalloc(&p, static_cast<size_t>(bytes)));
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();  // zeroed before any peer maps it
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return SVDMLP_ERR_CUDA;
+  }
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle, &h, sizeof(h));
+  *ptr = p;
+  return SVDMLP_OK;
+}
+
+int svdmlp_peer_open(const void* handle, void** peer_ptr) {
+  if (!handle || !peer_ptr) return SVDMLP_ERR_INVALID_VALUE;
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  SVD_CUDA(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return SVDMLP_OK;
+}
+
+int svdmlp_peer_close(void* peer_ptr) {
+  if (!peer_ptr) return SVDMLP_ERR_INVALID_VALUE;
+  SVD_CUDA(cudaIpcCloseMemHandle(peer_ptr));
+  return SVDMLP_OK;
+}
+
+int svdmlp_peer_free(void* ptr) {
+  if (!ptr) return SVDMLP_ERR_INVALID_VALUE;
+  SVD_CUDA(cudaFree(ptr));
+  return SVDMLP_OK;
+}
+
+int64_t svdmlp_peer_scratch_bytes(int world, int m, int c) {
+  if (world < 1 || world > kPeerMaxRanks || m <= 0 || c <= 0) return 0;
+  return 2LL * world * cdiv(m, world) * c * 2;
+}
+
+int svdmlp_peer_allreduce_f16(void* const* bases, int world, int rank, int64_t off, int m, int c, int64_t ld,
+                              int64_t off_scratch, void* stream) {
+  PeerArgs a;
+  SVD_CHECK(make_peer_args(bases, world, rank, &a));
+  if (c <= 0 || c % 8 != 0 || !peer_matrix_ok(off, m, 2LL * c, 2 * ld) || off_scratch < kPeerSignalBytes ||
+      off_scratch % 16 != 0)
+    return SVDMLP_ERR_INVALID_VALUE;
+  unsigned grid = 0;
+  SVD_CHECK(peer_grid(&grid));
+  peer_allreduce_f16_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, off, m, c, ld,
+                                                                                         off_scratch);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+int svdmlp_peer_reduce_scatter_f16(void* const* bases, int world, int rank, int64_t off, int m, int c, int64_t ld,
+                                   int64_t off_scratch, void* out, int64_t ld_out, void* stream) {
+  PeerArgs a;
+  SVD_CHECK(make_peer_args(bases, world, rank, &a));
+  if (c <= 0 || c % 8 != 0 || !peer_matrix_ok(off, m, 2LL * c, 2 * ld) || off_scratch < kPeerSignalBytes ||
+      off_scratch % 16 != 0 || !out || ld_out < c || ld_out % 8 != 0)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) return SVDMLP_ERR_ALIGNMENT;
+  unsigned grid = 0;
+  SVD_CHECK(peer_grid(&grid));
+  peer_reduce_scatter_f16_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, off, m, c, ld, off_scratch, static_cast<unsigned char*>(out), ld_out);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+int svdmlp_peer_allgather(void* const* bases, int world, int rank, int64_t off, int m, int64_t row_bytes,
+                          int64_t ld_bytes, void* stream) {
+  PeerArgs a;
+  SVD_CHECK(make_peer_args(bases, world, rank, &a));
+  if (!peer_matrix_ok(off, m, row_bytes, ld_bytes)) return SVDMLP_ERR_INVALID_VALUE;
+  unsigned grid = 0;
+  SVD_CHECK(peer_grid(&grid));
+  peer_allgather_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, off, m, row_bytes,
+                                                                                     ld_bytes);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+int svdmlp_peer_check_status(void* own_base, void* stream) {
+  if (!own_base) return SVDMLP_ERR_INVALID_VALUE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  int status = SVDMLP_OK;
+  SVD_CHECK(read_error_block(own_base, s, &status));
+  if (status == SVDMLP_ERR_RANGE) {
+    SVD_CUDA(cudaMemsetAsync(static_cast<int*>(own_base) + kRangeWord, 0, sizeof(int), s));
+    SVD_CUDA(cudaStreamSynchronize(s));
+  }
+  return status;
 }
 
 }  // extern "C"

@@ -106,6 +106,18 @@ SIGNATURES = {
     "svdmlp_stage_timing": (c_int, [c_int]),
     "svdmlp_stage_times": (c_int, [POINTER(ctypes.c_double), POINTER(c_int64), c_int]),
     "svdmlp_launch_count": (c_int64, []),
+    "svdmlp_peer_signal_bytes": (c_int64, []),
+    "svdmlp_peer_alloc": (c_int, [c_int64, POINTER(c_void_p), c_void_p]),
+    "svdmlp_peer_open": (c_int, [c_void_p, POINTER(c_void_p)]),
+    "svdmlp_peer_close": (c_int, [c_void_p]),
+    "svdmlp_peer_free": (c_int, [c_void_p]),
+    "svdmlp_peer_scratch_bytes": (c_int64, [c_int, c_int, c_int]),
+    "svdmlp_peer_allreduce_f16": (c_int, [POINTER(c_void_p), c_int, c_int, c_int64, c_int, c_int, c_int64, c_int64,
+                                          c_void_p]),
+    "svdmlp_peer_reduce_scatter_f16": (c_int, [POINTER(c_void_p), c_int, c_int, c_int64, c_int, c_int, c_int64,
+                                               c_int64, c_void_p, c_int64, c_void_p]),
+    "svdmlp_peer_allgather": (c_int, [POINTER(c_void_p), c_int, c_int, c_int64, c_int, c_int64, c_int64, c_void_p]),
+    "svdmlp_peer_check_status": (c_int, [c_void_p, c_void_p]),
 }
 
 _lock = threading.Lock()

@@ -17,6 +17,13 @@ split): X.[u_g|u_u] on this rank's M/P rows, all-gather XU, stages 2-3 on all
 rows of this rank's ff shard, reduce-scatter the fp16 partial by rows,
 .v_down on this rank's rows, all-gather y.  Three collectives instead of one,
 but X.[u_g|u_u] and .v_down cost 1/P each.
+
+collectives="peer" (chosen by "auto" when every GPU can address every other)
+runs the exchanges with the library's own kernels over NVLink peer memory
+(svdflash_b200.peer): the partial, XU and y live in a buffer every rank maps,
+and each collective is one kernel of plain loads and stores between GPUs.  The
+fp16 sums are taken in rank order in fp32 and rounded once, so every rank
+gets the same bits.  collectives="nccl" uses torch.distributed (NCCL).
 """
 from __future__ import annotations
 
@@ -25,7 +32,9 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from . import _lib
 from .kernels import ops
+from .peer import PeerBuffer, layout, peer_access_everywhere
 
 
 def shard_bounds(ff: int, rank: int, world: int) -> tuple[int, int]:
@@ -64,7 +73,7 @@ class TensorParallelSvdMlp:
     """One ff-sharded SVD MLP layer on this rank's GPU."""
 
     def __init__(self, u_gate, v_gate, u_up, v_up, u_down, v_down, rank: int, world: int, group=None,
-                 reduce_dtype: torch.dtype = torch.float16, mode: str = "auto"):
+                 reduce_dtype: torch.dtype = torch.float16, mode: str = "auto", collectives: str = "auto"):
         ff = v_gate.shape[1]
         lo, hi = shard_bounds(ff, rank, world)
         if reduce_dtype not in (torch.float16, torch.float32):
@@ -73,11 +82,62 @@ class TensorParallelSvdMlp:
             raise ValueError("mode must be 'auto', 'allreduce' or 'split'")
         if mode == "split" and reduce_dtype != torch.float16:
             raise TypeError("the split mode reduces an fp16 partial")
+        if collectives not in ("auto", "nccl", "peer"):
+            raise ValueError("collectives must be 'auto', 'nccl' or 'peer'")
+        if collectives == "peer" and reduce_dtype != torch.float16:
+            raise TypeError("the peer collectives reduce an fp16 partial")
         self.rank, self.world, self.group, self.reduce_dtype, self.mode = rank, world, group, reduce_dtype, mode
+        self.collectives = collectives
         self.layer = ops.pack_svd_layer(u_gate, v_gate[:, lo:hi].contiguous(), u_up, v_up[:, lo:hi].contiguous(),
                                         u_down[lo:hi].contiguous(), v_down)
         self.r_d = u_down.shape[1]
         self._partial: Optional[torch.Tensor] = None
+        self._peer: Optional[PeerBuffer] = None
+        self._peer_m = 0
+        self._t_rows: Optional[torch.Tensor] = None
+
+    # ---------------------------------------------------------- peer memory
+    def peer_collectives(self) -> bool:
+        """Whether the exchanges run on the library's peer-memory kernels
+        (decided once, collectively, on the first call that needs it)."""
+        if self.world == 1 or self.reduce_dtype != torch.float16 or self.collectives == "nccl":
+            return False
+        if self.collectives == "auto":
+            self.collectives = "peer" if peer_access_everywhere(self.group) else "nccl"
+        return self.collectives == "peer"
+
+    def _ensure_peer(self, m: int, d: int) -> PeerBuffer:
+        """The peer buffer for m rows (collective when it has to grow):
+        partial [m, cols] fp16, the reduction's scratch, XU [m, 2 rp_gu] fp16,
+        y [m, d] bf16."""
+        if self._peer is not None and self._peer_m >= m:
+            return self._peer
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+        cols = (self.r_d + 7) // 8 * 8
+        n1 = 2 * self.layer.layout.rp_gu
+        lib = _lib.load()
+        signal = int(lib.svdmlp_peer_signal_bytes())
+        scratch = int(lib.svdmlp_peer_scratch_bytes(self.world, m, cols))
+        (self._off_part, self._off_scr, self._off_xu, self._off_y), total = layout(
+            [m * cols * 2, scratch, m * n1 * 2, m * d * 2], signal)
+        self._cols, self._n1 = cols, n1
+        self._peer = PeerBuffer(total, self.rank, self.world, self.group)
+        self._peer_m = m
+        return self._peer
+
+    def close(self) -> None:
+        """Frees the peer buffer (collective: every rank calls it)."""
+        if self._peer is not None:
+            self._peer.close()
+            self._peer = None
+            self._peer_m = 0
+
+    def check_peer_status(self) -> None:
+        """Raises if a peer collective's wait expired or an fp16 sum saturated."""
+        if self._peer is not None:
+            self._peer.check_status()
 
     def _partial_buffer(self, m: int, device) -> torch.Tensor:
         align = 4 if self.reduce_dtype == torch.float32 else 8
@@ -91,6 +151,12 @@ class TensorParallelSvdMlp:
         m = x.shape[0]
         if self.world > 1 and m % self.world == 0 and self._use_split(m, x.shape[1]):
             return self._forward_split(x, residual, out)
+        if self.peer_collectives():
+            pb = self._ensure_peer(m, x.shape[1])
+            part = pb.view(self._off_part, (m, self._cols), torch.float16)
+            ops.forward_partial_packed(self.layer, x, part[:, :self.r_d])
+            pb.allreduce_f16(self._off_part, m, self._cols, self._cols, self._off_scr)
+            return ops.down_finish_packed(self.layer, part[:, :self.r_d], residual=residual, out=out)
         buf = self._partial_buffer(m, x.device)
         ops.forward_partial_packed(self.layer, x, buf[:, :self.r_d])
         if self.world > 1:
@@ -138,6 +204,8 @@ class TensorParallelSvdMlp:
         m = rows * self.world
         dev = x_rows.device
         n1 = 2 * self.layer.layout.rp_gu
+        if self.peer_collectives():
+            return self._split_rows_peer(x_rows, residual_rows)
         xu_p = ops.xu_project_packed(self.layer, x_rows)
         xu = torch.empty((m, n1), dtype=torch.float16, device=dev)
         dist.all_gather_into_tensor(xu, xu_p, group=self.group)
@@ -147,10 +215,37 @@ class TensorParallelSvdMlp:
         dist.reduce_scatter_tensor(t_p, full, op=dist.ReduceOp.SUM, group=self.group)
         return ops.down_finish_packed(self.layer, t_p[:, :self.r_d], residual=residual_rows)
 
+    def _split_rows_peer(self, x_rows: torch.Tensor, residual_rows: Optional[torch.Tensor],
+                         y_out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """_split_rows over peer memory: XU rows are written into the shared
+        buffer and gathered there; the partial is reduce-scattered from it."""
+        rows, d = x_rows.shape
+        m = rows * self.world
+        lo = self.rank * rows
+        pb = self._ensure_peer(m, d)
+        xu = pb.view(self._off_xu, (m, self._n1), torch.float16)
+        ops.xu_project_packed(self.layer, x_rows, out=xu[lo:lo + rows])
+        pb.allgather(self._off_xu, m, self._n1 * 2, self._n1 * 2)
+        part = pb.view(self._off_part, (m, self._cols), torch.float16)
+        ops.partial_from_xu_packed(self.layer, xu, part[:, :self.r_d])
+        if self._t_rows is None or self._t_rows.shape[0] < rows or self._t_rows.device != x_rows.device:
+            self._t_rows = torch.empty((rows, self._cols), dtype=torch.float16, device=x_rows.device)
+        t_p = self._t_rows[:rows]
+        pb.reduce_scatter_f16(self._off_part, m, self._cols, self._cols, self._off_scr, t_p)
+        return ops.down_finish_packed(self.layer, t_p[:, :self.r_d], residual=residual_rows, out=y_out)
+
     def _forward_split(self, x: torch.Tensor, residual: Optional[torch.Tensor], out: Optional[torch.Tensor]):
         m, d = x.shape
         rows = m // self.world
         lo, hi = self.rank * rows, (self.rank + 1) * rows
+        if self.peer_collectives():
+            pb = self._ensure_peer(m, d)
+            y_all = pb.view(self._off_y, (m, d), torch.bfloat16)
+            self._split_rows_peer(x[lo:hi], None if residual is None else residual[lo:hi], y_out=y_all[lo:hi])
+            pb.allgather(self._off_y, m, d * 2, d * 2)
+            y = out if out is not None else torch.empty((m, d), dtype=torch.bfloat16, device=x.device)
+            y.copy_(y_all)
+            return y
         y_p = self._split_rows(x[lo:hi], None if residual is None else residual[lo:hi])
         y = out if out is not None else torch.empty((m, d), dtype=torch.bfloat16, device=x.device)
         dist.all_gather_into_tensor(y, y_p, group=self.group)

@@ -91,6 +91,27 @@ def test_entry_points_reject_bad_arguments(lib):
     assert lib.svdmlp_rmsnorm(None, 8, None, None, 8, 1, 8, 1e-5, None) == _lib.ERR_INVALID_VALUE
     # misaligned output of the fp32 partial
     assert lib.svdmlp_forward_partial(ctypes.byref(L), 1, 1, 64, 4, 2, 40, 256, 1 << 20, None) == _lib.ERR_ALIGNMENT
+    # peer memory: checked before any CUDA call
+    sig = lib.svdmlp_peer_signal_bytes()
+    assert sig >= 16 * 1024 and sig % 256 == 0
+    ptr, handle = ctypes.c_void_p(), (ctypes.c_ubyte * 64)()
+    assert lib.svdmlp_peer_alloc(sig, ctypes.byref(ptr), handle) == _lib.ERR_INVALID_VALUE  # no data area
+    assert lib.svdmlp_peer_open(None, ctypes.byref(ptr)) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_peer_close(None) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_peer_free(None) == _lib.ERR_INVALID_VALUE
+    bases = (ctypes.c_void_p * 2)(4096, 8192)
+    assert lib.svdmlp_peer_allreduce_f16(None, 2, 0, sig, 8, 8, 8, sig, None) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_peer_allreduce_f16(bases, 9, 0, sig, 8, 8, 8, sig, None) == _lib.ERR_INVALID_VALUE   # world > 8
+    assert lib.svdmlp_peer_allreduce_f16(bases, 2, 2, sig, 8, 8, 8, sig, None) == _lib.ERR_INVALID_VALUE   # rank >= world
+    assert lib.svdmlp_peer_allreduce_f16(bases, 2, 0, 0, 8, 8, 8, sig, None) == _lib.ERR_INVALID_VALUE     # in the signal area
+    assert lib.svdmlp_peer_allreduce_f16(bases, 2, 0, sig, 8, 12, 16, sig, None) == _lib.ERR_INVALID_VALUE  # c % 8
+    odd = (ctypes.c_void_p * 2)(4096, 8200)
+    assert lib.svdmlp_peer_allgather(odd, 2, 0, sig, 8, 16, 16, None) == _lib.ERR_ALIGNMENT
+    assert lib.svdmlp_peer_allgather(bases, 2, 0, sig, 8, 24, 32, None) == _lib.ERR_INVALID_VALUE     # 16-byte rows
+    assert lib.svdmlp_peer_reduce_scatter_f16(bases, 2, 0, sig, 8, 8, 8, sig, None, 8, None) == _lib.ERR_INVALID_VALUE
+    assert lib.svdmlp_peer_allreduce_f16(bases, 2, 0, sig, 8, 8, 8, 8, None) == _lib.ERR_INVALID_VALUE  # scratch
+    assert lib.svdmlp_peer_scratch_bytes(2, 37, 24) == 2 * 2 * 19 * 24 * 2
+    assert lib.svdmlp_peer_check_status(None, None) == _lib.ERR_INVALID_VALUE
 
 
 def test_status_strings(lib):

@@ -46,7 +46,7 @@ def _worker(rank, world, port, q):
         rows = M // world
         mine = slice(rank * rows, (rank + 1) * rows)
         for mode in ("allreduce", "split"):
-            tp = TensorParallelSvdMlp(*fd, rank=rank, world=world, mode=mode)
+            tp = TensorParallelSvdMlp(*fd, rank=rank, world=world, mode=mode, collectives="nccl")
             full = tp.forward(xd)
             full_res = tp.forward(xd, residual=rd)
             got = tp.forward_rows(xd[mine].contiguous())
