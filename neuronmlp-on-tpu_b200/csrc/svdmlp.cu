@@ -2345,10 +2345,15 @@ static int make_peer_args(void* const* bases, int world, int rank, PeerArgs* a) 
   return SVDMLP_OK;
 }
 
-static int peer_grid(unsigned* grid) {
+// CTAs of a collective: enough for `vectors` 16-byte elements at four per
+// thread, at most one per SM.  Small exchanges (decode sizes) then run on a few
+// CTAs and wait on a few barriers instead of one per SM.  The grid depends only
+// on the sizes, so every rank launches the same one.
+static int peer_grid(int64_t vectors, unsigned* grid) {
   DeviceInfo* dev = nullptr;
   SVD_CHECK(device_info(&dev));
-  *grid = static_cast<unsigned>(std::min(kPeerMaxCtas, dev->sms));
+  const int64_t want = cdiv(vectors, static_cast<int64_t>(kPeerThreads) * kPeerUnroll);
+  *grid = static_cast<unsigned>(std::max<int64_t>(1, std::min<int64_t>(want, std::min(kPeerMaxCtas, dev->sms))));
   return SVDMLP_OK;
 }
 
@@ -2413,7 +2418,7 @@ int svdmlp_peer_allreduce_f16(void* const* bases, int world, int rank, int64_t o
       off_scratch % 16 != 0)
     return SVDMLP_ERR_INVALID_VALUE;
   unsigned grid = 0;
-  SVD_CHECK(peer_grid(&grid));
+  SVD_CHECK(peer_grid(static_cast<int64_t>(m) * (c / 8), &grid));
   peer_allreduce_f16_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, off, m, c, ld,
                                                                                          off_scratch);
   SVD_CUDA(cudaGetLastError());
@@ -2430,7 +2435,7 @@ int svdmlp_peer_reduce_scatter_f16(void* const* bases, int world, int rank, int6
     return SVDMLP_ERR_INVALID_VALUE;
   if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) return SVDMLP_ERR_ALIGNMENT;
   unsigned grid = 0;
-  SVD_CHECK(peer_grid(&grid));
+  SVD_CHECK(peer_grid(static_cast<int64_t>(m) * (c / 8), &grid));
   peer_reduce_scatter_f16_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       a, off, m, c, ld, off_scratch, static_cast<unsigned char*>(out), ld_out);
   SVD_CUDA(cudaGetLastError());
@@ -2444,7 +2449,7 @@ int svdmlp_peer_allgather(void* const* bases, int world, int rank, int64_t off, 
   SVD_CHECK(make_peer_args(bases, world, rank, &a));
   if (!peer_matrix_ok(off, m, row_bytes, ld_bytes)) return SVDMLP_ERR_INVALID_VALUE;
   unsigned grid = 0;
-  SVD_CHECK(peer_grid(&grid));
+  SVD_CHECK(peer_grid(static_cast<int64_t>(m) * (row_bytes / 16), &grid));
   peer_allgather_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, off, m, row_bytes,
                                                                                      ld_bytes);
   SVD_CUDA(cudaGetLastError());
