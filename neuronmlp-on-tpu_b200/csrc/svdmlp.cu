@@ -545,6 +545,7 @@ struct DecSet {
   using DUf32 = DecCfg<TOK, 1, PST, EPI_PLAIN, true, OUT_F32>;
   using DV = DecCfg<TOK, 1, PST, EPI_PLAIN, true, OUT_BF16>;
   using DVres = DecCfg<TOK, 1, PST, EPI_RESID, true, OUT_BF16>;
+  using DGU = DecCfg<TOK, 2, DST, EPI_SWIGLU, false, OUT_F16>;  // dense X.[w_g|w_u] (bf16 operands)
 };
 using Dec16 = DecSet<16>;
 using Dec64 = DecSet<64>;
@@ -611,6 +612,12 @@ static int64_t stage_partials(int M, int N, int K, int sms, int stage) {
 template <class Set>
 static int64_t dec_set_partials(const svdmlp_layout* L, int M, int sms) {
   int64_t b = 0;
+  if (L->kind == SVDMLP_KIND_DENSE) {
+    b = std::max(b, dec_partial_bytes<typename Set::DGU>(
+                        plan_dec<typename Set::DGU>(M, L->ff, L->d, sms, g_split_override[ST_DENSE_GU])));
+    return std::max(b, dec_partial_bytes<typename Set::DV>(
+                           plan_dec<typename Set::DV>(M, L->d, L->ff, sms, g_split_override[ST_DENSE_D])));
+  }
   if (L->r_gu > 0) {
     b = std::max(b, dec_partial_bytes<typename Set::XU>(
                         plan_dec<typename Set::XU>(M, 2 * L->rp_gu, L->d, sms, g_split_override[ST_XU])));
@@ -661,9 +668,6 @@ static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
       best = std::max(best, stage_partials<CfgDU1>(M, L->r_d, L->ff, sms, ST_DOWN_U));
       best = std::max(best, stage_partials<CfgDV1>(M, L->d, L->r_d, sms, ST_DOWN_V));
     }
-  } else {
-    best = std::max(best, stage_partials<CfgDenseGU1>(M, L->ff, L->d, sms, ST_DENSE_GU));
-    best = std::max(best, stage_partials<CfgDV1>(M, L->d, L->ff, sms, ST_DENSE_D));
   }
   if (L->kind == SVDMLP_KIND_SVD && L->r_gu > 0 && L->r_d > 0) {
     for (int m : {1, 16, 17, 64}) {
@@ -671,7 +675,7 @@ static int64_t max_partials(const svdmlp_layout* L, int max_m, int sms) {
       best = std::max(best, layer_decode_partials(L, m, sms));
     }
   }
-  if (L->kind == SVDMLP_KIND_SVD) {
+  {
     for (int m : {1, 16, 17, 64, 65, 128}) {
       if (m > max_m) break;
       if (m <= 16) best = std::max(best, dec_set_partials<Dec16>(L, m, sms));
@@ -1200,6 +1204,7 @@ template <class S> using PickDU = typename S::DU;
 template <class S> using PickDUf32 = typename S::DUf32;
 template <class S> using PickDV = typename S::DV;
 template <class S> using PickDVres = typename S::DVres;
+template <class S> using PickDGU = typename S::DGU;
 
 // Stage 1 + 2: h = silu(X.u_g.v_g) * (X.u_u.v_u); `h_bf16` selects the
 // caller-facing bf16 output instead of the internal fp16 H.
@@ -1288,14 +1293,17 @@ static int run_dense(const svdmlp_layout* L, const uint8_t* packed, const void* 
   const Operand xa{x, false, L->d, M, ldx};
   const Operand bg{packed + L->off_vg, false, L->d, L->ff, L->ld_d};
   const Operand bu{packed + L->off_vu, false, L->d, L->ff, L->ld_d};
-  SVD_CHECK(gemm_stage<CfgDenseGU, CfgDenseGU1>(xa, xa, bg, bu, Output{w.h, L->ff, M, L->ld_ff}, M, L->ff, L->d,
-                                                ST_DENSE_GU, w, s));
+  // below the CTA-pair threshold both stages stream their weights on the
+  // swapped-operand decode kernels, as the SVD layer's stages do
+  SVD_CHECK(gemm_stage_dec<CfgDenseGU, PickDGU>(xa, xa, bg, bu, Output{w.h, L->ff, M, L->ld_ff}, M, L->ff, L->d,
+                                               ST_DENSE_GU, w, s));
   const Operand ha{w.h, true, L->ff, M, L->ld_ff};
   const Operand bd{packed + L->off_ud, true, L->ff, L->d, L->ld_ff};
   const Output yo{y, L->d, M, ldy};
   if (residual)
-    return gemm_stage<CfgDVres, CfgDVres1>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s, residual, ld_res);
-  return gemm_stage<CfgDV, CfgDV1>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s);
+    return gemm_stage_dec<CfgDVres, PickDVres>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s, residual,
+                                               ld_res);
+  return gemm_stage_dec<CfgDV, PickDV>(ha, ha, bd, bd, yo, M, L->d, L->ff, ST_DENSE_D, w, s);
 }
 
 // The whole layer for M <= 64 in one persistent launch (layer_decode_sm100.cuh).
@@ -2271,6 +2279,7 @@ static void dec_set_info(int stage, int* o) {
   if (stage == ST_XU) dec_tile_info<typename Set::XU>(o);
   else if (stage == ST_GATEUP) dec_tile_info<typename Set::GU>(o);
   else if (stage == ST_DOWN_U) dec_tile_info<typename Set::DU>(o);
+  else if (stage == ST_DENSE_GU) dec_tile_info<typename Set::DGU>(o);
   else dec_tile_info<typename Set::DV>(o);
 }
 }  // namespace svdmlp
@@ -2289,7 +2298,7 @@ int svdmlp_tile_info(int stage, int M, int* out8) {
     case ST_DENSE_D: pair ? pair_tile_info<CfgDV>(out8) : pair_tile_info<CfgDV1>(out8); break;
     default: pair ? pair_tile_info<CfgGemm>(out8) : pair_tile_info<CfgGemm1>(out8); break;
   }
-  if (!pair && stage <= ST_DOWN_V) {
+  if (!pair && stage <= ST_DENSE_D) {
     if (M <= 16) dec_set_info<Dec16>(stage, out8);
     else if (M <= 64) dec_set_info<Dec64>(stage, out8);
     else dec_set_info<Dec128>(stage, out8);
