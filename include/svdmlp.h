@@ -385,9 +385,11 @@ int svdmlp_set_split_override(int stage, int splits);
 int svdmlp_set_split_tail(int enable);
 
 /* svdmlp_forward runs layers of M <= max_m tokens as one whole-layer decode
- * kernel and larger ones as four per-stage kernels.  max_m = 0 turns the
- * whole-layer kernel off, a negative value restores the default (16, the
- * measured crossover on B200); at most 64. */
+ * kernel and larger ones as four per-stage kernels (the contracted schedule,
+ * svdmlp_set_decode_contract, always runs on the whole-layer kernel).  max_m = 0
+ * turns the plain whole-layer schedule off, a negative value restores the
+ * default (1: measured on B200 the whole-layer kernel wins at one token, ties at
+ * two and loses from four tokens on); at most 64. */
 int svdmlp_set_layer_decode(int max_m);
 
 /* L2 prefetch window of the whole-layer decode kernel's weight stream, in

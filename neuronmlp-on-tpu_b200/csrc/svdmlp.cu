@@ -32,7 +32,11 @@ static std::atomic<int64_t> g_launches{0};
 static int g_split_override[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 static unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s: far above any legal wait
 static constexpr int kLayerDecodeMaxM = 64;        // largest M the whole-layer decode kernel handles
-static constexpr int kLayerDecodeDefaultMaxM = 16; // measured: per-stage kernels are faster above 16 tokens
+// Measured on B200 (8B layer, three rotated weight copies, with and without a
+// residual): the whole-layer kernel wins at one token (its contracted schedule,
+// 77.2 vs 83.6 us at r = 2867, 61.0 vs 65.6 at r = 1911), ties at two and
+// loses from four on (16 tokens: 100.8 vs 90.7 us, 87.0 vs 72.5).
+static constexpr int kLayerDecodeDefaultMaxM = 1;
 static int g_layer_decode_max_m = kLayerDecodeDefaultMaxM;
 // L2 prefetch window of the whole-layer decode kernel's weight stream (slots
 // beyond the one loading).  Off: with weights that are not already in L2 the
@@ -1799,9 +1803,10 @@ static int forward_impl(const svdmlp_layout* L, const void* packed, const void* 
   const void* xa;
   int64_t ldxa;
   SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
-  if (M <= g_layer_decode_max_m) {
-    // Decode sizes: the whole layer in one launch; its stores need no TMA
-    // alignment, and the residual is read in place (it must not alias y).
+  if (M <= g_layer_decode_max_m || (contract && M <= 16)) {
+    // Decode sizes: the whole layer in one launch (the contracted schedule
+    // always runs there); its stores need no TMA alignment, and the residual
+    // is read in place (it must not alias y).
     return run_layer_decode(L, P, xa, ldxa, M, y, ldy, residual, ld_res, w, s, contract);
   }
   const OutTarget yt = out_target(y, ldy, w.ys, L->ld_d);
@@ -1872,7 +1877,7 @@ int svdmlp_forward_block(const svdmlp_layout* L, const void* packed, const void*
   wn.stats_ld = static_cast<int>(ld_stats);
   wo.stats_ld = static_cast<int>(ld_stats);
   wo.out_stats = y_stats;
-  if (M <= g_layer_decode_max_m) {
+  if (M <= g_layer_decode_max_m || M <= g_decode_contract) {
     Workspace wb = wn;
     wb.out_stats = y_stats;
     return run_layer_decode(L, P, x, ldx, M, y, ldy, x, ldx, wb, s, M <= g_decode_contract);

@@ -169,3 +169,29 @@ def test_block_argument_errors(cuda_device):
         ops.pack_svd_layer(*fd, norm_weight=torch.ones(d + 1, device=cuda_device))
     with pytest.raises(ValueError):
         ops.svd_block_packed(normed, x, xs[:, :1].contiguous())  # too few slices per row
+
+
+@pytest.mark.parametrize("m", [3, 16])
+def test_block_on_forced_whole_layer_kernel(cuda_device, m):
+    """The plain whole-layer decode schedule (default only at one token, where
+    it is contracted) with the fused norm: forced for 3 and 16 tokens."""
+    from svdflash_b200 import _lib
+    ops = _ops()
+    lib = _lib.load()
+    d, ff, r = 1024, 3584, 700
+    _, f = orc.make_inputs(700 + m, 1, d, ff, r)
+    x = _rows_scaled(710 + m, m, d)
+    w = _norm_weight(720 + m, d)
+    layer = ops.pack_svd_layer(*[to_dev(a, cuda_device) for a in f], norm_weight=to_dev(w, cuda_device))
+    xd = to_dev(x, cuda_device)
+    xs = ops.row_sumsq(xd)
+    ys = torch.full_like(xs, float("nan"))
+    try:
+        assert lib.svdmlp_set_layer_decode(16) == 0
+        y = ops.svd_block_packed(layer, xd, xs, y_stats=ys)
+        torch.cuda.synchronize()
+    finally:
+        lib.svdmlp_set_layer_decode(-1)
+    ops.check_device_status()
+    _assert_rows(to_np(y), orc.mlp_block(x, w, f, eps=1e-5), x, what=f"forced whole-layer block m={m}")
+    np.testing.assert_allclose(to_np(ys), _slice_sumsq(to_np(y)), rtol=3e-5, atol=1e-30)
