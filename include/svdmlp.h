@@ -399,12 +399,13 @@ int svdmlp_set_layer_decode(int max_m);
  * off (the default for both); both are at most 64. */
 int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots);
 
-/* prefetch_units >= 1 (default 1) launches the whole-layer decode kernel with
+/* mode >= 1 (default 1) launches the whole-layer decode kernel with
  * programmatic dependent launch: its CTAs start on SMs that the previous
- * kernel on the stream has left, prefetch the weights of `prefetch_units`
- * units each to L2, and wait for that kernel before touching anything it
- * writes; 0 launches it plainly.  At most 8. */
-int svdmlp_set_decode_overlap(int prefetch_units);
+ * kernel on the stream has left and wait for that kernel before touching
+ * anything it writes; with mode >= 2 each CTA first requests into L2 the
+ * weights of mode - 1 units (measured slower: their requests compete with the
+ * previous kernel's tail).  0 launches it plainly.  At most 8. */
+int svdmlp_set_decode_overlap(int mode);
 
 /* Layers (and svdmlp_gemm calls) of M >= m tokens run on the CTA-pair GEMMs,
  * smaller ones on the decode kernels.  Default 129; values below 17 act as 17;

@@ -45,6 +45,10 @@ static int g_layer_decode_max_m = kLayerDecodeDefaultMaxM;
 static int g_pf_ahead = 0, g_pf_wait = 0;
 // Programmatic dependent launch of the whole-layer decode kernel: 0 = off,
 // k >= 1 = on, each CTA prefetching k units' weights before its wait.
+// Whole-layer decode launches: 0 plain, 1 overlapped (programmatic dependent
+// launch), k >= 2 overlapped and each CTA requests into L2 the weights of k - 1
+// units before it waits.  Measured at one token (8B layer, rotated weights):
+// plain 78.0 us, overlapped 74.7, with one unit requested 77.4.
 static int g_layer_decode_pdl = 1;
 // Prefill stage chaining: M-tile groups per stage (0: off).  Off by default:
 // under the 1 kW power cap that sustained prefill runs at, filling the SMs a
@@ -1395,7 +1399,7 @@ static int run_layer_decode(const svdmlp_layout* L, const uint8_t* P, const void
   prm.trace = g_trace;
   prm.pf_ahead = g_pf_ahead;
   prm.pf_wait = g_pf_wait;
-  prm.pdl_units = g_layer_decode_pdl;
+  prm.pdl_units = std::max(0, g_layer_decode_pdl - 1);
   prm.norm_stats = w.norm_stats;
   prm.norm_parts = w.norm_parts;
   prm.norm_dim = w.norm_dim;
@@ -2137,9 +2141,9 @@ int svdmlp_set_decode_prefetch(int ahead_slots, int wait_slots) {
   return SVDMLP_OK;
 }
 
-int svdmlp_set_decode_overlap(int prefetch_units) {
-  if (prefetch_units < 0 || prefetch_units > 8) return SVDMLP_ERR_INVALID_VALUE;
-  g_layer_decode_pdl = prefetch_units;
+int svdmlp_set_decode_overlap(int mode) {
+  if (mode < 0 || mode > 8) return SVDMLP_ERR_INVALID_VALUE;
+  g_layer_decode_pdl = mode;
   return SVDMLP_OK;
 }
 
