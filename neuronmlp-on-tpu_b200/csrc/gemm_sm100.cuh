@@ -329,6 +329,12 @@ SVD_DEV void add_partials(float (&acc)[32], const float4 (&t0)[8], const float4 
   }
 }
 
+// Weight (B) tiles of the CTA-pair GEMMs are loaded with an L2 evict-first
+// policy (1) or the default policy (0).
+#ifndef SVDMLP_B_EVICT_FIRST
+#define SVDMLP_B_EVICT_FIRST 1
+#endif
+
 template <class Cfg>
 SVD_DEV void issue_stage_loads(const CUtensorMap* tm_a, const CUtensorMap* tm_a2, const CUtensorMap* tm_b,
                                const CUtensorMap* tm_b2, uint8_t* smem, int s, uint64_t* full_local,
@@ -359,8 +365,14 @@ SVD_DEV void issue_stage_loads(const CUtensorMap* tm_a, const CUtensorMap* tm_a2
     }
     if (!do_b) return;
     if constexpr (Cfg::B_TILED) {
+#if SVDMLP_B_EVICT_FIRST
+      const uint64_t pol = l2_policy_evict_first();
+      tma_load_4d_pair_hint(tm_b, full_leader, b, kb, grp, pol);
+      if constexpr (Cfg::NB == 2) tma_load_4d_pair_hint(tm_b2, full_leader, b2, kb, grp, pol);
+#else
       tma_load_4d_pair(tm_b, full_leader, b, kb, grp);
       if constexpr (Cfg::NB == 2) tma_load_4d_pair(tm_b2, full_leader, b2, kb, grp);
+#endif
     } else {
       tma_load_2d_pair(tm_b, full_leader, b, kx, b_row);
       if constexpr (Cfg::NB == 2) tma_load_2d_pair(tm_b2, full_leader, b2, kx, b_row);

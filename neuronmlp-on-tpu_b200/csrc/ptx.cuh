@@ -278,6 +278,24 @@ SVD_DEV void tma_load_4d_pair(const CUtensorMap* map, uint32_t bar_cluster, void
       : "memory");
 }
 
+// The same load with an L2 cache policy (createpolicy): used for weight tiles,
+// which every CTA pair reads once, so that they leave L2 before the
+// activations and split-K partials that are read again.
+SVD_DEV void tma_load_4d_pair_hint(const CUtensorMap* map, uint32_t bar_cluster, void* dst, int c2, int c3,
+                                   uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %3, %4, %5}], [%2], %6;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(0), "r"(c2), "r"(c3), "l"(policy)
+      : "memory");
+}
+
+SVD_DEV uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 SVD_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(dst_smem)),
                "r"(ncols)
