@@ -212,11 +212,15 @@ __global__ void __launch_bounds__(192)
   if (warp == 4) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      // weights: packed tile-major layout, 4-D loads at (k-block, 16-row group)
+      // weights: packed tile-major layout, 4-D loads at (k-block, 16-row group),
+      // read once per call, so evicted from L2 before activations and partials
+      const uint64_t wpol = l2_policy_weight_stream();
       auto w_loads = [&](int s, int kx, int row) {
-        tma_load_4d(&tm_w, &full[s], smem + Cfg::OFF_W + (s * Cfg::NB) * Cfg::W_BYTES, kx / Cfg::BK, row / 16);
+        tma_load_4d_hint(&tm_w, &full[s], smem + Cfg::OFF_W + (s * Cfg::NB) * Cfg::W_BYTES, kx / Cfg::BK, row / 16,
+                         wpol);
         if constexpr (Cfg::NB == 2)
-          tma_load_4d(&tm_w2, &full[s], smem + Cfg::OFF_W + (s * Cfg::NB + 1) * Cfg::W_BYTES, kx / Cfg::BK, row / 16);
+          tma_load_4d_hint(&tm_w2, &full[s], smem + Cfg::OFF_W + (s * Cfg::NB + 1) * Cfg::W_BYTES, kx / Cfg::BK,
+                           row / 16, wpol);
       };
       auto x_loads = [&](int s, int kx) {
         tma_load_2d(&tm_x, &full[s], smem + Cfg::OFF_X + (s * Cfg::NB) * Cfg::X_BYTES, kx, 0);

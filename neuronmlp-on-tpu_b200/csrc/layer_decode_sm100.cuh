@@ -320,6 +320,9 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
     if (lane == 0) {
       // k-blocks of slot i of unit c: dual -> kb0 + i (both branches);
       // otherwise kb0 + 2i and kb0 + 2i + 1 (the second may not exist).
+      // weights are read once per call: evict them from L2 first, before the
+      // activations and split-K partials that are read again
+      const uint64_t wpol = l2_policy_weight_stream();
       auto slot_w = [&](const LdUnit& c, int i, int sl) {
         const DecStage& st = p.st[c.s];
         uint8_t* w0 = smem + Cfg::OFF_W + (sl * 2) * Cfg::W_BYTES;
@@ -329,14 +332,14 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
         if (st.kind == KIND_CONTRACT && i >= c.kb1 - c.kb0) {
           // u_down^T rows of rank tile j, the two k-blocks of this ff slice
           const int j = i - (c.kb1 - c.kb0), kbu = 2 * c.n_t;
-          tma_load_4d(&st.w3, &full[sl], w0, kbu, j * (Cfg::BM / 16));
-          if (kbu + 1 < st.ff_kb) tma_load_4d(&st.w3, &full[sl], w1, kbu + 1, j * (Cfg::BM / 16));
+          tma_load_4d_hint(&st.w3, &full[sl], w0, kbu, j * (Cfg::BM / 16), wpol);
+          if (kbu + 1 < st.ff_kb) tma_load_4d_hint(&st.w3, &full[sl], w1, kbu + 1, j * (Cfg::BM / 16), wpol);
         } else if (st.nb == 2) {
-          tma_load_4d(&st.w, &full[sl], w0, c.kb0 + i, grp);
-          tma_load_4d(&st.w2, &full[sl], w1, c.kb0 + i, grp);
+          tma_load_4d_hint(&st.w, &full[sl], w0, c.kb0 + i, grp, wpol);
+          tma_load_4d_hint(&st.w2, &full[sl], w1, c.kb0 + i, grp, wpol);
         } else {
-          tma_load_4d(&st.w, &full[sl], w0, c.kb0 + 2 * i, grp);
-          if (c.kb0 + 2 * i + 1 < c.kb1) tma_load_4d(&st.w, &full[sl], w1, c.kb0 + 2 * i + 1, grp);
+          tma_load_4d_hint(&st.w, &full[sl], w0, c.kb0 + 2 * i, grp, wpol);
+          if (c.kb0 + 2 * i + 1 < c.kb1) tma_load_4d_hint(&st.w, &full[sl], w1, c.kb0 + 2 * i + 1, grp, wpol);
         }
       };
       auto slot_x = [&](const LdUnit& c, int i, int sl) {

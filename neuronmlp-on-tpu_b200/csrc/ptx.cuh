@@ -116,6 +116,15 @@ SVD_DEV void tma_load_4d(const CUtensorMap* map, uint64_t* bar, void* dst, int c
       : "memory");
 }
 
+// tma_load_4d with an L2 cache policy (see l2_policy_evict_first).
+SVD_DEV void tma_load_4d_hint(const CUtensorMap* map, uint64_t* bar, void* dst, int c2, int c3, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %3, %4, %5}], [%2], %6;" ::"r"(smem_addr(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_addr(bar)), "r"(0), "r"(c2), "r"(c3), "l"(policy)
+      : "memory");
+}
+
 // L2 prefetch of the same 4-D tile (no shared memory, no barrier): pulls the
 // tile's lines into L2 so that a later tma_load_4d of it hits there.
 SVD_DEV void tma_prefetch_4d(const CUtensorMap* map, int c2, int c3) {
@@ -294,6 +303,21 @@ SVD_DEV uint64_t l2_policy_evict_first() {
   uint64_t pol;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
   return pol;
+}
+
+// The policy of the decode kernels' weight stream: evict-first (1) or the
+// normal policy (0).
+#ifndef SVDMLP_W_EVICT_FIRST
+#define SVDMLP_W_EVICT_FIRST 1
+#endif
+SVD_DEV uint64_t l2_policy_weight_stream() {
+#if SVDMLP_W_EVICT_FIRST
+  return l2_policy_evict_first();
+#else
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+#endif
 }
 
 SVD_DEV void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
