@@ -318,9 +318,15 @@ def parity_sample(x, factors, y, nrows=16):
     return orc.error_metrics(y[rows].float().cpu().numpy(), ref)
 
 
-def _time_events(fn, steps: int, warmup: int) -> float:
-    """Milliseconds per call of fn() on the current stream (CUDA events)."""
+def _time_events(fn, steps: int, warmup: int, settle_s: float = 0.0) -> float:
+    """Milliseconds per call of fn() on the current stream (CUDA events).
+    settle_s > 0 leaves the GPU idle that long before the warm-up, so that
+    arms compared against each other start from the same clock and power
+    state instead of inheriting the previous arm's."""
     import torch
+    if settle_s > 0:
+        torch.cuda.synchronize()
+        time.sleep(settle_s)
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -340,7 +346,8 @@ def run_sweep(args) -> None:
     decode  config 2: M in {1, 8, 32, 128} x ratio {0.6, 0.8, 0.9}; HBM-bound, bytes =
             the three factor pairs once + x and y, against the measured copy bandwidth.
     shapes  config 5: ratio {0.4, 0.6, 0.8, 0.9, 1.0 = dense} x seq {512..8192} x batch
-            {1, 4}; SVD/dense speed-up and tensor roofline fraction.
+            {1, 4}; SVD/dense speed-up and tensor roofline fraction; every point starts
+            after 0.5 s idle, so that no arm inherits another's power-capped clocks.
     stack   config 3: 32 blocks of x + mlp(rmsnorm(x)) at seq {1, 16, 1024, 4096}: SVD (0.9)
             with a separate RMSNorm kernel per block, SVD with the norm fused into the
             block (svd_fused) and dense arms, each captured as one CUDA graph.
@@ -393,14 +400,14 @@ def run_sweep(args) -> None:
                 x = torch.randn(m, d, device=dev).to(torch.bfloat16)
                 y = torch.empty_like(x)
                 steps = max(3, min(args.steps, int(2e5 / m)))
-                ms_dense = _time_events(lambda: ops.dense_mlp_packed(dense, x, out=y), steps, args.warmup)
+                ms_dense = _time_events(lambda: ops.dense_mlp_packed(dense, x, out=y), steps, args.warmup, 0.5)
                 fl_dense = 6.0 * m * d * ff
                 emit({"sweep": "shapes", "batch": batch, "seq": seq, "tokens": m, "ratio": 1.0, "arm": "dense",
                       "us_per_layer": ms_dense * 1e3, "tflops": fl_dense / (ms_dense * 1e-3) / 1e12,
                       "frac_of_sustained_peak": fl_dense / (ms_dense * 1e-3) / 1e12 / peak})
                 for ratio, layer in layers.items():
                     r = rank_for(d, ff, ratio)
-                    ms = _time_events(lambda: ops.svd_mlp_packed(layer, x, out=y), steps, args.warmup)
+                    ms = _time_events(lambda: ops.svd_mlp_packed(layer, x, out=y), steps, args.warmup, 0.5)
                     fl = 6.0 * m * r * (d + ff)
                     emit({"sweep": "shapes", "batch": batch, "seq": seq, "tokens": m, "ratio": ratio, "r": r,
                           "arm": "svd", "us_per_layer": ms * 1e3, "tflops": fl / (ms * 1e-3) / 1e12,
