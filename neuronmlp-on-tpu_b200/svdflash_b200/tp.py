@@ -99,7 +99,9 @@ class TensorParallelSvdMlp:
     # ---------------------------------------------------------- peer memory
     def peer_collectives(self) -> bool:
         """Whether the exchanges run on the library's peer-memory kernels
-        (decided once, collectively, on the first call that needs it)."""
+        (decided once, collectively, on the first call that needs it; that
+        call and any call that grows the peer buffer exchange handles over the
+        process group, so they must run eagerly, not under graph capture)."""
         if self.world == 1 or self.reduce_dtype != torch.float16 or self.collectives == "nccl":
             return False
         if self.collectives == "auto":
