@@ -819,6 +819,31 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
               v[j] = 0.f;
               w[j] = 0.f;
             }
+            if (tv <= 4 && st.splits <= 8) {
+              // Few tokens: every split's loads in flight at once (one round
+              // trip instead of one per pair of splits); the sum is in split order.
+              float g[8][4], u[8][4];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const float* src = base + static_cast<size_t>(j * 2) * (Cfg::BM * TOK) + 16 * ch * Cfg::BM;
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  const bool ld = j < st.splits && t < tv;
+                  g[j][t] = ld ? __ldcg(src + t * Cfg::BM) : 0.f;
+                  u[j][t] = ld && dual ? __ldcg(src + Cfg::BM * TOK + t * Cfg::BM) : 0.f;
+                }
+              }
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                if (j < st.splits) {
+#pragma unroll
+                  for (int t = 0; t < 4; ++t) {
+                    v[t] += g[j][t];
+                    w[t] += u[j][t];
+                  }
+                }
+              }
+            } else {
             // Two splits' loads in flight per step (one 128-byte line per warp
             // and token); the sum is in split order.
 #pragma unroll 1
@@ -843,6 +868,7 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
                   w[t] += u[j][t];
                 }
               }
+            }
             }
             if (dual) {
 #pragma unroll
