@@ -18,8 +18,8 @@ rows of this rank's ff shard, reduce-scatter the fp16 partial by rows,
 .v_down on this rank's rows, all-gather y.  Three collectives instead of one,
 but X.[u_g|u_u] and .v_down cost 1/P each.
 
-collectives="peer" (chosen by "auto" when every GPU can address every other)
-runs the exchanges with the library's own kernels over NVLink peer memory
+collectives="peer" (chosen by "auto" for groups of up to four GPUs that can
+all address each other; "peer" selects it for up to eight) runs the exchanges with the library's own kernels over NVLink peer memory
 (svdflash_b200.peer): the partial, XU and y live in a buffer every rank maps,
 and each collective is one kernel of plain loads and stores between GPUs.  The
 fp16 sums are taken in rank order in fp32 and rounded once, so every rank
@@ -105,8 +105,13 @@ class TensorParallelSvdMlp:
         if self.world == 1 or self.reduce_dtype != torch.float16 or self.collectives == "nccl":
             return False
         if self.collectives == "auto":
-            self.collectives = "peer" if peer_access_everywhere(self.group) else "nccl"
+            # measured on 2 and 4 GPUs (level with NCCL at 1024 tokens, ahead at
+            # decode sizes); larger groups keep NCCL by default until measured
+            use = self.world <= self.PEER_AUTO_MAX_WORLD and peer_access_everywhere(self.group)
+            self.collectives = "peer" if use else "nccl"
         return self.collectives == "peer"
+
+    PEER_AUTO_MAX_WORLD = 4
 
     def _ensure_peer(self, m: int, d: int) -> PeerBuffer:
         """The peer buffer for m rows (collective when it has to grow):
