@@ -19,9 +19,10 @@ rows of this rank's ff shard, reduce-scatter the fp16 partial by rows,
 but X.[u_g|u_u] and .v_down cost 1/P each.
 
 collectives="peer" (chosen by "auto" for groups of up to four GPUs that can
-all address each other; "peer" selects it for up to eight) runs the exchanges with the library's own kernels over NVLink peer memory
-(svdflash_b200.peer): the partial, XU and y live in a buffer every rank maps,
-and each collective is one kernel of plain loads and stores between GPUs.  The
+all address each other; "peer" selects it for up to eight) runs the exchanges
+with the library's own kernels over NVLink peer memory (svdflash_b200.peer):
+the partial, XU and y live in a buffer every rank maps, and each collective is
+one kernel of plain stores between GPUs.  The
 fp16 sums are taken in rank order in fp32 and rounded once, so every rank
 gets the same bits.  collectives="nccl" uses torch.distributed (NCCL).
 """
