@@ -61,15 +61,24 @@ class PeerBuffer:
         dist.all_gather_into_tensor(every, mine, group=group)
         handles = every.cpu().reshape(world, 64)
         bases = []
-        for i in range(world):
-            if i == rank:
-                bases.append(self._own)
-                continue
-            h = (ctypes.c_ubyte * 64)(*handles[i].tolist())
-            p = ctypes.c_void_p()
-            _lib.check(self.lib.svdmlp_peer_open(h, ctypes.byref(p)), "peer_open")
-            self._opened.append(p.value)
-            bases.append(p.value)
+        try:
+            for i in range(world):
+                if i == rank:
+                    bases.append(self._own)
+                    continue
+                h = (ctypes.c_ubyte * 64)(*handles[i].tolist())
+                p = ctypes.c_void_p()
+                _lib.check(self.lib.svdmlp_peer_open(h, ctypes.byref(p)), "peer_open")
+                self._opened.append(p.value)
+                bases.append(p.value)
+        except Exception:
+            # undo this rank's part; the other ranks fail at their next
+            # collective (bounded waits) or at the barrier below
+            for q in self._opened:
+                self.lib.svdmlp_peer_close(ctypes.c_void_p(q))
+            self.lib.svdmlp_peer_free(ctypes.c_void_p(self._own))
+            self._opened, self._own = [], None
+            raise
         self.bases = (ctypes.c_void_p * world)(*bases)
         # every rank has mapped every buffer before any collective runs
         dist.barrier(group=group, device_ids=[self.device.index])
