@@ -388,8 +388,8 @@ int svdmlp_set_split_tail(int enable);
  * kernel and larger ones as four per-stage kernels (the contracted schedule,
  * svdmlp_set_decode_contract, always runs on the whole-layer kernel).  max_m = 0
  * turns the plain whole-layer schedule off, a negative value restores the
- * default (1: measured on B200 the whole-layer kernel wins at one token, ties at
- * two and loses from four tokens on); at most 64. */
+ * default (6: measured on B200 the whole-layer kernel wins up to six tokens and
+ * the per-stage kernels from eight); at most 64. */
 int svdmlp_set_layer_decode(int max_m);
 
 /* L2 prefetch window of the whole-layer decode kernel's weight stream, in

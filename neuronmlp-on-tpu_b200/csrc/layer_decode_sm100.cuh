@@ -184,6 +184,37 @@ SVD_DEV int unit_slots(const LayerDecParams& p, const LdUnit& c) {
   return st.nb == 2 ? nk : (nk + 1) / 2;
 }
 
+// Split-K fix-up of the first 16-token chunk with few tokens: this thread's
+// feature row of every split's partial (JM splits and TM tokens at most, all
+// loads in flight at once), summed in split order into v (and w for the dual
+// stage).  `slot` is the element distance between two splits' partials (two
+// branches each).
+template <int JM, int TM, int SLOT>
+SVD_DEV void ld_sum_splits(const float* base, int splits, int tv, bool dual, float (&v)[16], float (&w)[16]) {
+  constexpr int BM = 128;
+  float g[JM][TM], u[JM][TM];
+#pragma unroll
+  for (int j = 0; j < JM; ++j) {
+    const float* src = base + static_cast<size_t>(j * 2) * SLOT;
+#pragma unroll
+    for (int t = 0; t < TM; ++t) {
+      const bool ld = j < splits && t < tv;
+      g[j][t] = ld ? __ldcg(src + t * BM) : 0.f;
+      u[j][t] = ld && dual ? __ldcg(src + SLOT + t * BM) : 0.f;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < JM; ++j) {
+    if (j < splits) {
+#pragma unroll
+      for (int t = 0; t < TM; ++t) {
+        v[t] += g[j][t];
+        w[t] += u[j][t];
+      }
+    }
+  }
+}
+
 // Stores one 16-token chunk of a unit's outputs (thread = feature f of the
 // 128-row tile; all 128 epilogue threads call it together).  The first stage
 // of a fused block scales token t by its RMSNorm row scale; an EPI_RESID
@@ -819,30 +850,12 @@ __global__ void __launch_bounds__(192) layer_decode_kernel(const __grid_constant
               v[j] = 0.f;
               w[j] = 0.f;
             }
+            // Few tokens: every split's loads in flight at once (one round trip
+            // instead of one per pair of splits); the sum is in split order.
             if (tv <= 4 && st.splits <= 8) {
-              // Few tokens: every split's loads in flight at once (one round
-              // trip instead of one per pair of splits); the sum is in split order.
-              float g[8][4], u[8][4];
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                const float* src = base + static_cast<size_t>(j * 2) * (Cfg::BM * TOK) + 16 * ch * Cfg::BM;
-#pragma unroll
-                for (int t = 0; t < 4; ++t) {
-                  const bool ld = j < st.splits && t < tv;
-                  g[j][t] = ld ? __ldcg(src + t * Cfg::BM) : 0.f;
-                  u[j][t] = ld && dual ? __ldcg(src + Cfg::BM * TOK + t * Cfg::BM) : 0.f;
-                }
-              }
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                if (j < st.splits) {
-#pragma unroll
-                  for (int t = 0; t < 4; ++t) {
-                    v[t] += g[j][t];
-                    w[t] += u[j][t];
-                  }
-                }
-              }
+              ld_sum_splits<8, 4, Cfg::BM * TOK>(base, st.splits, tv, dual, v, w);
+            } else if (tv <= 8 && st.splits <= 4) {
+              ld_sum_splits<4, 8, Cfg::BM * TOK>(base, st.splits, tv, dual, v, w);
             } else {
             // Two splits' loads in flight per step (one 128-byte line per warp
             // and token); the sum is in split order.

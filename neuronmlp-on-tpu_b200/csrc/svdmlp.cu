@@ -32,11 +32,11 @@ static std::atomic<int64_t> g_launches{0};
 static int g_split_override[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 static unsigned long long g_wait_limit_ns = 2000000000ull;  // 2 s: far above any legal wait
 static constexpr int kLayerDecodeMaxM = 64;        // largest M the whole-layer decode kernel handles
-// Measured on B200 (8B layer, three rotated weight copies, with and without a
-// residual): the whole-layer kernel wins at one token (its contracted schedule,
-// 77.2 vs 83.6 us at r = 2867, 61.0 vs 65.6 at r = 1911), ties at two and
-// loses from four on (16 tokens: 100.8 vs 90.7 us, 87.0 vs 72.5).
-static constexpr int kLayerDecodeDefaultMaxM = 1;
+// Measured on B200 (8B layer, three rotated weight copies, with a residual;
+// whole-layer kernel / per-stage kernels): 2 tokens 75.3 / 82.5 us, 4 tokens
+// 77.3 / 83.3, 6 tokens 81.6 / 83.6, 8 tokens 91.1 / 84.4, 16 tokens
+// 88.2 / 87.0 (r = 1911 at 8 tokens: 70.1 / 65.9).
+static constexpr int kLayerDecodeDefaultMaxM = 6;
 static int g_layer_decode_max_m = kLayerDecodeDefaultMaxM;
 // L2 prefetch window of the whole-layer decode kernel's weight stream (slots
 // beyond the one loading).  Off: with weights that are not already in L2 the
