@@ -135,3 +135,17 @@ def test_host_pipeline_argument_checks():
     from svdflash_b200.pipeline import HostPipeline
     with pytest.raises(ValueError, match="depth"):
         HostPipeline(lambda x, out: out, (4, 8), (4, 8), device="cuda:0", depth=1)
+
+
+def test_peer_buffer_layout_and_arguments():
+    """Peer-memory layout arithmetic and the argument checks that run before
+    any CUDA call (the collectives themselves are GPU tests)."""
+    from svdflash_b200.peer import PeerBuffer, layout
+    offs, total = layout([100, 0, 4096, 1], 32 * 1024)
+    assert offs[0] == 32 * 1024 and all(o % 256 == 0 for o in offs)
+    assert offs[1] >= offs[0] + 100 and offs[2] >= offs[1] and offs[3] >= offs[2] + 4096
+    assert total % 256 == 0 and total >= offs[3] + 1
+    with pytest.raises(ValueError):
+        PeerBuffer(1 << 20, rank=0, world=9)
+    with pytest.raises(ValueError):
+        PeerBuffer(1 << 20, rank=2, world=2)
