@@ -348,6 +348,8 @@ def run_sweep(args) -> None:
     shapes  config 5: ratio {0.4, 0.6, 0.8, 0.9, 1.0 = dense} x seq {512..8192} x batch
             {1, 4}; SVD/dense speed-up and tensor roofline fraction; every point starts
             after 0.5 s idle, so that no arm inherits another's power-capped clocks.
+    stack70 config 4's stack: 80 fused blocks of the 70B layer (ratio 0.8) at seq {1, 4096},
+            one CUDA graph.
     stack   config 3: 32 blocks of x + mlp(rmsnorm(x)) at seq {1, 16, 1024, 4096}: SVD (0.9)
             with a separate RMSNorm kernel per block, SVD with the norm fused into the
             block (svd_fused) and dense arms, each captured as one CUDA graph.
@@ -441,6 +443,31 @@ def run_sweep(args) -> None:
                 stack._graph = None
             del mlps, stack
             torch.cuda.empty_cache()
+    elif args.sweep == "stack70":
+        # config 4's stack: 80 blocks of the 70B layer (d 8192, ff 28672, ratio 0.8,
+        # r 5097), RMSNorm fused into each block, one CUDA graph, 90 GB of factors
+        d7, ff7, n_layers = 8192, 28672, 80
+        r7 = rank_for(d7, ff7, 0.8)
+        gn = torch.Generator(device=dev)
+        gn.manual_seed(args.seed + 199)
+        blocks = []
+        for l in range(n_layers):
+            wn = (1 + 0.02 * torch.randn(d7, generator=gn, device=dev)).to(torch.bfloat16)
+            blocks.append(SvdMlpBlock(*make_factors(d7, ff7, r7, args.seed + 3000 + l, dev), wn))
+            torch.cuda.empty_cache()
+        stack = MlpBlockStack(blocks)
+        for seq in (1, 4096):
+            x = torch.randn(seq, d7, device=dev).to(torch.bfloat16)
+            stack.capture(seq, d7, dev)
+            ms = _time_events(lambda: stack.replay(x), max(3, min(args.steps, 10)), args.warmup)
+            fl = n_layers * 6.0 * seq * r7 * (d7 + ff7)
+            emit({"sweep": "stack70", "arm": "svd_fused", "layers": n_layers, "seq": seq, "ratio": 0.8, "r": r7,
+                  "us_per_block": ms * 1e3 / n_layers, "ms_per_stack": ms, "tokens_per_s": seq / (ms * 1e-3),
+                  "tflops": fl / (ms * 1e-3) / 1e12, "graph": True})
+            stack._graph = None
+        ops.check_device_status(dev)
+        del blocks, stack
+        torch.cuda.empty_cache()
 
 
 def profile_layer(args) -> None:
@@ -517,7 +544,7 @@ def main():
     ap.add_argument("--tp-collectives", choices=("auto", "nccl", "peer"), default="auto",
                     help="N>1: the library's peer-memory collectives over NVLink (auto, when every GPU can "
                          "address every other) or NCCL")
-    ap.add_argument("--sweep", choices=("decode", "shapes", "stack"), default=None,
+    ap.add_argument("--sweep", choices=("decode", "shapes", "stack", "stack70"), default=None,
                     help="print one JSON line per point of BASELINE configs 2, 5 or 3 instead of the bench line")
     args = ap.parse_args()
     if args.warmup < 3:
