@@ -195,3 +195,33 @@ def test_block_on_forced_whole_layer_kernel(cuda_device, m):
     ops.check_device_status()
     _assert_rows(to_np(y), orc.mlp_block(x, w, f, eps=1e-5), x, what=f"forced whole-layer block m={m}")
     np.testing.assert_allclose(to_np(ys), _slice_sumsq(to_np(y)), rtol=3e-5, atol=1e-30)
+
+
+@pytest.mark.parametrize("m", [1, 4, 1024])
+def test_block_at_the_8b_shape(cuda_device, m):
+    """Config 3's block (Llama-3-8B, ratio 0.9, r = 2867) with the norm fused:
+    one token (contracted whole-layer kernel), four tokens (plain whole-layer
+    kernel) and 1024 tokens (CTA-pair GEMMs), full output, per-row criterion,
+    with the statistics the block writes for the next one."""
+    import math
+    ops = _ops()
+    d, ff, r = 4096, 14336, 2867
+    g = torch.Generator(device=cuda_device)
+    g.manual_seed(800 + m)
+
+    def mat(rows, cols):
+        return (torch.randn(rows, cols, generator=g, device=cuda_device) / math.sqrt(rows)).to(torch.bfloat16)
+
+    fd = [mat(d, r), mat(r, ff), mat(d, r), mat(r, ff), mat(ff, r), mat(r, d)]
+    f = [to_np(t) for t in fd]
+    w = _norm_weight(810 + m, d)
+    x = _rows_scaled(820 + m, m, d)
+    layer = ops.pack_svd_layer(*fd, norm_weight=to_dev(w, cuda_device))
+    del fd
+    xd = to_dev(x, cuda_device)
+    xs = ops.row_sumsq(xd)
+    ys = torch.full_like(xs, float("nan"))
+    y = ops.svd_block_packed(layer, xd, xs, y_stats=ys)
+    ops.check_device_status()
+    _assert_rows(to_np(y), orc.mlp_block(x, w, f, eps=1e-5), x, what=f"8B block m={m}")
+    np.testing.assert_allclose(to_np(ys), _slice_sumsq(to_np(y)), rtol=3e-5, atol=1e-30)
