@@ -468,9 +468,10 @@ static int64_t partial_bytes(const Plan& p, int BN, int NB, int ctas = 1) {
 // Tile choices of the prefill kernels (compile-time; the defaults are the
 // tuned values, other values serve tile sweeps).
 // Dual gate/up tile: 256 x 256 per branch (one TMEM buffer of 2 x 256
-// columns, 3 pipeline stages in 225 KB of shared memory).  L2-to-SM bandwidth
-// (~11-12 TB/s) bounds these kernels, so the widest tile wins: 7.6 KB of
-// operands per MFLOP against 8.2 for 256 x 224 and 11.4 for 256 x 128
+// columns, 3 pipeline stages in 225 KB of shared memory).  The widest tile
+// wins: 7.6 KB of operands per MFLOP against 8.2 for 256 x 224 and 11.4 for
+// 256 x 128, and fewer tiles per launch, although operand traffic is not the
+// bound (with no operand loads at all the stage still takes 0.92 of its time)
 // (config 1: 256 x 128 double-buffered 199 us, 256 x 224 166 -> 139 us with
 // the tile-major weights; 256 x 256 with the split tail 275 vs 280 us per
 // layer in short runs, 312 vs 317 us sustained).
