@@ -544,6 +544,9 @@ def main():
     ap.add_argument("--tp-collectives", choices=("auto", "nccl", "peer"), default="auto",
                     help="N>1: the library's peer-memory collectives over NVLink (auto, when every GPU can "
                          "address every other) or NCCL")
+    ap.add_argument("--tp-exchange", choices=("fused", "separate"), default="fused",
+                    help="N>1, all-reduce mode on the peer collectives: the exchange fused into the H.u_down "
+                         "GEMM's epilogue (default) or a separate all-reduce kernel after it")
     ap.add_argument("--sweep", choices=("decode", "shapes", "stack", "stack70"), default=None,
                     help="print one JSON line per point of BASELINE configs 2, 5 or 3 instead of the bench line")
     args = ap.parse_args()
@@ -603,7 +606,7 @@ def main():
             return ops.svd_mlp_packed(layer, inp, out=out)
     else:
         tp = TensorParallelSvdMlp(*factors, rank=rank, world=world, mode=args.tp_mode,
-                                  collectives=args.tp_collectives)
+                                  collectives=args.tp_collectives, fused_exchange=args.tp_exchange == "fused")
         y = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
 
         def step(inp, out=y):
@@ -782,7 +785,10 @@ def main():
         "config": workload_config(args.workload, wl),
         "parallelism": f"tp-ff{world}" if world > 1 else "single-gpu",
         "collectives": (("split: all-gather XU, reduce-scatter fp16 partial, all-gather y"
-                         if tp._use_split(m, d) else "one all-reduce of the fp16 [M, r] partial")
+                         if tp._use_split(m, d) else
+                         ("one all-reduce of the fp16 [M, r] partial, fused into the H.u_down GEMM"
+                          if tp.peer_collectives() and tp.fused_exchange else
+                          "one all-reduce of the fp16 [M, r] partial"))
                         + (" (the library's kernels over NVLink peer memory)" if tp.peer_collectives()
                            else " (NCCL)"))
                        if world > 1 else None,

@@ -503,6 +503,36 @@ int svdmlp_peer_allgather(void* const* bases, int world, int rank, int64_t off, 
  * (SVDMLP_ERR_RANGE, cleared by the read). */
 int svdmlp_peer_check_status(void* own_base, void* stream);
 
+/* The tensor-parallel all-reduce fused into the GEMM that produces it (the
+ * reference has no multi-device path, models/README.md:26-27; this is the
+ * exchange of the ff-sharded layer, replacing svdmlp_forward_partial_f16 +
+ * svdmlp_peer_allreduce_f16).
+ *
+ * Slots: two sets (alternating from call to call) of one fp16
+ * [slot_rows, ld_slot] slot per rank, svdmlp_peer_slots_bytes(world,
+ * slot_rows, ld_slot) bytes at byte offset off_slots of every rank's buffer
+ * (off_slots >= the signal area, 16-byte aligned; ld_slot a multiple of 8).
+ * A call of M <= slot_rows rows uses the first M rows of each slot; keep
+ * slot_rows fixed for a buffer.
+ *
+ * svdmlp_forward_partial_f16_peer runs stages 1-3 of this rank's ff shard
+ * (as svdmlp_forward_partial_f16) and stores its fp16 partial [M, r_d] into
+ * its slot of every rank's buffer: at CTA-pair sizes (M >= the pair
+ * threshold) the H.u_down GEMM's epilogue stores each row over NVLink as its
+ * tile finishes, so the transfer overlaps the GEMM; below it, one more kernel
+ * copies the finished partial.  The last CTA then publishes this rank's call
+ * count to every peer.  svdmlp_peer_sum_f16 waits (bounded) until every peer
+ * has published the same count and writes the ranks' partials summed in rank
+ * order in fp32, rounded once to fp16, into `out` [m, c] (row stride ld_out):
+ * the same bits as svdmlp_peer_allreduce_f16, on every rank.  Every rank makes
+ * both calls, in this order, on its own stream, for every layer call. */
+int64_t svdmlp_peer_slots_bytes(int world, int slot_rows, int64_t ld_slot);
+int svdmlp_forward_partial_f16_peer(const svdmlp_layout* layout, const void* packed, const void* x, int64_t ld_x,
+                                    int M, void* const* bases, int world, int rank, int64_t off_slots, int slot_rows,
+                                    int64_t ld_slot, void* workspace, int64_t workspace_bytes, void* stream);
+int svdmlp_peer_sum_f16(void* const* bases, int world, int rank, int64_t off_slots, int slot_rows, int m, int c,
+                        int64_t ld_slot, void* out, int64_t ld_out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

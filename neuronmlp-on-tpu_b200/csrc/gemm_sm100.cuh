@@ -80,6 +80,25 @@ enum ErrSite : int {
   SITE_DEPENDENCY = 8,
 };
 
+// Tensor-parallel exchange fused into the epilogue of the H.u_down GEMM
+// (n == 0: none).  Every fp16 output row goes, with 16-byte stores, into
+// this rank's slot of every rank's peer buffer (over NVLink; the own buffer
+// included) instead of through the output tensor map.  The two slot sets
+// alternate from call to call (the parity of this rank's call counter), so a
+// rank one call ahead never overwrites a slot a peer still reads.  When every
+// CTA of the launch is done, the last one publishes the new count into each
+// peer's flag word for this rank (release, system scope).
+constexpr int kPushMaxRanks = 8;
+struct GemmPush {
+  unsigned char* dst[kPushMaxRanks];  // this rank's slot (parity 0) in every rank's buffer
+  unsigned* flag[kPushMaxRanks];      // this rank's flag word in every rank's signal area
+  unsigned* epoch;                    // this rank's call counter
+  unsigned* exit_count;               // CTAs of the launch that are done
+  long long parity_bytes;             // distance between the two slot sets
+  long long ld;                       // row stride of a slot (elements)
+  int n, rank;                        // ranks (0: no exchange), this rank
+};
+
 struct GemmParams {
   int M, N, K;  // N is the per-branch width for dual GEMMs
   int m_tiles, n_tiles, k_blocks;
@@ -113,6 +132,7 @@ struct GemmParams {
   int* pub;          // this stage's per-M-tile counters, bumped by each CTA per tile
   int* reset;        // last stage: counters [3][kChainStride] cleared by the last CTA
   int* exit_count;   // last stage: CTAs that have left
+  GemmPush push;
 };
 
 constexpr int kChainStride = 4096;  // M-tile counters per chained stage
@@ -264,6 +284,61 @@ SVD_DEV void store_box(const CUtensorMap* tm_out, uint8_t* stg_warp, int& stg_bu
     bulk_commit_group();
   }
   stg_buf ^= 1;
+}
+
+// Configurations whose epilogue can run the fused exchange (fp16 rows of a
+// plain GEMM: the tensor-parallel partial of T = H . u_down).  Its blocks are
+// pairs of consecutive 32-column chunks of one warp: four epilogue warps (each
+// walks every chunk of its rows in order) and tiles of whole 64-column pairs.
+template <class Cfg>
+constexpr bool kPushable = Cfg::OUT == OUT_F16 && Cfg::EPI == EPI_PLAIN && Cfg::NB == 1 && Cfg::EPI_WARPS == 4 &&
+                           Cfg::BN % 64 == 0;
+
+// Output boxes of the fused exchange, in pairs: box `half` (0 or 1) of a
+// 32 x 64 block (lane = row y0 + lane, columns col..col+31 of the box) goes,
+// as fp16 with saturation and zeros at or past column N, into half `half` of
+// the warp's two staging buffers; after the second box the block is read back
+// row-wise and stored into every rank's slot, so that each store instruction
+// writes four whole 128-byte row segments (16-byte stores from 32 different
+// rows cost NVLink far more per byte).  All lanes call it together.
+template <class Cfg>
+SVD_DEV void push_box(const GemmParams& p, uint8_t* stg, long long parity_off, const float (&v)[32], int col, int y0,
+                      int half) {
+  const uint32_t lane = lane_id();
+  bool bad = false;
+  uint32_t h[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const float lo = col + 2 * j < p.N ? v[2 * j] : 0.0f;
+    const float hi = col + 2 * j + 1 < p.N ? v[2 * j + 1] : 0.0f;
+    bad |= f16_out_of_range(lo) || f16_out_of_range(hi);
+    h[j] = pack_f16x2_sat(lo, hi);
+  }
+  if (__any_sync(0xffffffffu, bad) && lane == 0) flag_range(p.err);
+  // 64-byte rows per box, 16-byte chunk j of row r at j ^ ((r >> 1) & 3)
+  const uint32_t base = smem_addr(stg);
+  if (half == 0) __syncwarp();  // the previous block's reads of both buffers are done
+  const uint32_t box = base + static_cast<uint32_t>(half) * Cfg::STG_BYTES;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    st_shared_v4(box + lane * 64 + ((static_cast<uint32_t>(j) ^ ((lane >> 1) & 3u)) * 16), h[4 * j], h[4 * j + 1],
+                 h[4 * j + 2], h[4 * j + 3]);
+  if (half == 0) return;
+  __syncwarp();
+  const int c16 = static_cast<int>(lane & 7u);  // 16-byte chunk of the 128-byte row segment
+  const uint32_t src = base + static_cast<uint32_t>(c16 >> 2) * Cfg::STG_BYTES;
+  const int col0 = col - 32 + 8 * c16;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int r = i * 4 + static_cast<int>(lane >> 3);
+    const uint4 val = ld_shared_v4(src + r * 64 + ((static_cast<uint32_t>(c16 & 3) ^ ((static_cast<uint32_t>(r) >> 1) & 3u)) * 16));
+    const int row = y0 + r;
+    if (row < p.M && col0 < p.push.ld) {
+      const long long off = parity_off + (static_cast<long long>(row) * p.push.ld + col0) * 2;
+#pragma unroll 1
+      for (int q = 0; q < p.push.n; ++q) *reinterpret_cast<uint4*>(p.push.dst[q] + off) = val;
+    }
+  }
 }
 
 SVD_DEV float silu_mul(float g, float u) {
@@ -445,6 +520,7 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const WaitCtx ctx{abort_flag, p.err, p.timeout_ns};
+  unsigned push_epoch = 0;  // the fused exchange's call counter, read by the epilogue
 
   if (warp == Cfg::PRODUCER_WARP) {
     // ------------------------------------------------------------ producer
@@ -589,6 +665,17 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     // (as the producer does) so that each unit's row scale can be read before
     // its accumulator is ready.
     if (p.norm_stats != nullptr) grid_dependency_wait();
+    // The fused exchange writes the slot set of this call's parity.  The
+    // counter was moved by the previous exchange's last CTA, in an earlier
+    // launch.
+    long long push_off = 0;
+    if constexpr (kPushable<Cfg>) {
+      if (p.push.n > 0) {
+        grid_dependency_wait();
+        push_epoch = *reinterpret_cast<volatile unsigned*>(p.push.epoch);
+        push_off = (push_epoch & 1u) ? p.push.parity_bytes : 0;
+      }
+    }
     for (int u = unit0; u < p.num_units; u += unit_step) {
       const UnitCoord c = decode_unit(p, u);
       const int b = acc_it % Cfg::ACC_BUFS;
@@ -654,7 +741,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
               slice_ss[ch / 4] += ss;
             }
           }
-          store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
+          if constexpr (kPushable<Cfg>) {
+            if (p.push.n > 0) push_box<Cfg>(p, stg_warp, push_off, v, n0 + ch * 32, y_box, ch & 1);
+            else store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
+          } else {
+            store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
+          }
           if constexpr (Cfg::EPI == EPI_DUAL_STORE)
             store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N, p.err);
         }
@@ -728,7 +820,9 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
           const size_t split_stride = static_cast<size_t>(Cfg::CTAS) * tile_elems;
 #pragma unroll 1
           for (int ch = half; ch < NCH; ch += CH_STEP) {
-            if (PAIR && ch % c.nsplit != c.ks) continue;  // the same for every lane of the warp
+            // the same for every lane of the warp; the fused exchange hands
+            // out whole pairs of chunks (its 128-byte row segments)
+            if (PAIR && (p.push.n > 0 ? (ch >> 1) % c.nsplit : ch % c.nsplit) != c.ks) continue;
             float v[32], w[32];
 #pragma unroll
             for (int j = 0; j < 32; ++j) {
@@ -758,7 +852,12 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
               }
             }
             epilogue_math<Cfg>(p, v, w, grow, n0 + ch * 32);
-            store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
+            if constexpr (kPushable<Cfg>) {
+              if (p.push.n > 0) push_box<Cfg>(p, stg_warp, push_off, v, n0 + ch * 32, y_box, ch & 1);
+              else store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
+            } else {
+              store_box<Cfg>(&tm_out, stg_warp, stg_buf, v, n0 + ch * 32, y_box, p.M, p.N, p.err);
+            }
             if constexpr (Cfg::EPI == EPI_DUAL_STORE)
               store_box<Cfg>(&tm_out2, stg_warp, stg_buf, w, n0 + ch * 32, y_box, p.M, p.N, p.err);
           }
@@ -777,9 +876,29 @@ __global__ void __launch_bounds__(Cfg::THREADS, 1)
     }
     if (lane == 0) bulk_wait_group<0>();  // all output boxes written before exit
     __syncwarp();
+    // This thread's stores into the peers' slots are ordered before the
+    // publish below (system scope: the peers read them).
+    if constexpr (kPushable<Cfg>) {
+      if (p.push.n > 0) __threadfence_system();
+    }
   }
 
   __syncthreads();
+  if constexpr (kPushable<Cfg>) {
+    if (p.push.n > 0 && threadIdx.x == 0) {
+      // thread 0 is an epilogue thread: push_epoch is this launch's count
+      const unsigned done = atom_add_acq_rel_gpu(p.push.exit_count, 1u);
+      if (done == gridDim.x - 1) {
+        // every CTA's rows are out: publish the new count to every peer
+        fence_acq_rel_sys();
+        for (int q = 0; q < p.push.n; ++q)
+          if (q != p.push.rank) st_release_sys(p.push.flag[q], push_epoch + 1u);
+        *p.push.exit_count = 0;
+        *p.push.epoch = push_epoch + 1u;
+        __threadfence();
+      }
+    }
+  }
   if (p.exit_count != nullptr && threadIdx.x == 0) {
     // Last stage of a chain: the last CTA to leave clears the chain's
     // counters (every wait on them has returned by now) for the next launch.

@@ -31,7 +31,15 @@ constexpr int kPeerMaxCtas = 256;
 constexpr int kPeerThreads = 512;
 
 // Sites recorded in the signal area's error word.
-enum PeerSite : int { SITE_PEER_START = 21, SITE_PEER_MID = 22, SITE_PEER_END = 23 };
+enum PeerSite : int { SITE_PEER_START = 21, SITE_PEER_MID = 22, SITE_PEER_END = 23, SITE_PEER_SUM = 24 };
+
+// Words of the signal area's ctl block used by the fused exchange (the
+// H.u_down GEMM or peer_push_slots_kernel fills the slots, then
+// peer_sum_slots_kernel sums them): this rank's call counter, the exit
+// counter of the launch that fills the slots, and from word kPushFlagWord on
+// the count each rank has published into this rank's area.
+constexpr int kPushEpochWord = 8, kPushExitWord = 9, kPushFlagWord = 16;
+static_assert(kPushFlagWord + kPeerMaxRanks <= 64, "ctl words");
 
 struct PeerSignal {
   int ctl[64];                                    // word 0: timeout site; word 1: fp16 range flag
@@ -46,18 +54,6 @@ struct PeerArgs {
   int world, rank;
   unsigned long long limit_ns;
 };
-
-SVD_DEV void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-SVD_DEV unsigned ld_relaxed_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-SVD_DEV void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // The barrier of kind `kind` (0 start, 1 mid, 2 end) for this CTA.  All
 // threads call it; returns false (in every thread) when a wait timed out.
@@ -219,6 +215,148 @@ SVD_DEV void peer_reduce_block(const PeerArgs& a, long long off, int m, int c, l
   }
   // one flag per CTA (a saturated matrix would otherwise send an atomic per thread)
   if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(range_word, 1);
+}
+
+// ------------------------------------------------------------ fused exchange
+// Slots of the fused exchange: [2 parities][world][slot_rows][ld] fp16 at
+// off_s of every rank's buffer; slot [parity][q] holds rank q's partial in its
+// first m rows.  The slot size is fixed by the buffer, not by the call, so
+// calls of different sizes never overlap the other parity's slots.
+SVD_DEV long long push_slot_off(long long off_s, int parity, int world, int src, int slot_rows, long long ld) {
+  return off_s + (static_cast<long long>(parity * world + src) * slot_rows) * ld * 2;
+}
+
+// The last CTA of a launch that filled this rank's slots publishes the new
+// count to every peer and moves this rank's counter (thread 0 calls it after
+// a __syncthreads that follows every thread's system-scope fence).
+SVD_DEV void push_publish(const PeerArgs& a, unsigned epoch) {
+  PeerSignal* me = reinterpret_cast<PeerSignal*>(a.base[a.rank]);
+  unsigned* exit_word = reinterpret_cast<unsigned*>(&me->ctl[kPushExitWord]);
+  if (atom_add_acq_rel_gpu(exit_word, 1u) == gridDim.x - 1) {
+    fence_acq_rel_sys();
+    for (int q = 0; q < a.world; ++q) {
+      if (q == a.rank) continue;
+      PeerSignal* peer = reinterpret_cast<PeerSignal*>(a.base[q]);
+      st_release_sys(reinterpret_cast<unsigned*>(&peer->ctl[kPushFlagWord + a.rank]), epoch + 1u);
+    }
+    *exit_word = 0;
+    me->ctl[kPushEpochWord] = static_cast<int>(epoch + 1u);
+    __threadfence();
+  }
+}
+
+// The fused exchange for a partial that is already in local memory (decode
+// sizes, whose GEMMs are not the CTA-pair kernel): this rank's fp16 partial
+// [m, c_valid] (row stride ld_src) goes into its slot of every rank's buffer,
+// the own included; columns from c_valid up to ld are stored as zeros.
+__global__ void __launch_bounds__(kPeerThreads) peer_push_slots_kernel(PeerArgs a, const unsigned char* src,
+                                                                       long long ld_src, long long off_s, int m,
+                                                                       int slot_rows, int c_valid, long long ld) {
+  PeerSignal* me = reinterpret_cast<PeerSignal*>(a.base[a.rank]);
+  const unsigned epoch = *reinterpret_cast<volatile unsigned*>(&me->ctl[kPushEpochWord]);
+  const int parity = static_cast<int>(epoch & 1u);
+  const long long vpr = ld / 8;
+  const long long n = static_cast<long long>(m) * vpr;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long slot = push_slot_off(off_s, parity, a.world, a.rank, slot_rows, ld);
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+    const long long j = i / vpr;
+    const int v = static_cast<int>(i % vpr);
+    uint4 val = make_uint4(0u, 0u, 0u, 0u);
+    if (v * 8 + 8 <= c_valid) {
+      val = *reinterpret_cast<const uint4*>(src + (j * ld_src + v * 8) * 2);
+    } else if (v * 8 < c_valid) {
+      // the ragged last vector: the columns past c_valid become zeros
+      const unsigned short* h = reinterpret_cast<const unsigned short*>(src) + j * ld_src + v * 8;
+      uint32_t w[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const uint32_t lo = v * 8 + 2 * k < c_valid ? h[2 * k] : 0u;
+        const uint32_t hi = v * 8 + 2 * k + 1 < c_valid ? h[2 * k + 1] : 0u;
+        w[k] = lo | (hi << 16);
+      }
+      val = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+#pragma unroll
+    for (int q = 0; q < kPeerMaxRanks; ++q)
+      if (q < a.world) *reinterpret_cast<uint4*>(a.base[q] + slot + (j * ld + v * 8) * 2) = val;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) push_publish(a, epoch);
+}
+
+// The other half of the fused exchange: once every peer has published this
+// call's count, this rank sums the ranks' slots in rank order in fp32 and
+// rounds once to fp16 (the same arithmetic as the all-reduce above, so every
+// rank gets the same bits) into `out` [m, c] (row stride ld_out).  A peer that
+// does not publish within the limit leaves `out` unwritten and the timeout
+// site in the error word.
+__global__ void __launch_bounds__(kPeerThreads) peer_sum_slots_kernel(PeerArgs a, long long off_s, int m,
+                                                                      int slot_rows, int c, long long ld,
+                                                                      unsigned char* out, long long ld_out) {
+  PeerSignal* me = reinterpret_cast<PeerSignal*>(a.base[a.rank]);
+  __shared__ unsigned s_epoch;
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile unsigned*>(&me->ctl[kPushEpochWord]);
+  __syncthreads();
+  const unsigned epoch = s_epoch;  // moved by this call's fill, in the launch before
+  const int parity = static_cast<int>((epoch - 1u) & 1u);
+  bool ok = true;
+  if (threadIdx.x < static_cast<unsigned>(a.world) && static_cast<int>(threadIdx.x) != a.rank) {
+    const unsigned* f = reinterpret_cast<const unsigned*>(&me->ctl[kPushFlagWord + threadIdx.x]);
+    if (static_cast<int>(ld_relaxed_sys(f) - epoch) < 0) {
+      const unsigned long long t0 = global_timer_ns();
+      for (unsigned i = 1;; ++i) {
+        if (static_cast<int>(ld_relaxed_sys(f) - epoch) >= 0) break;
+        if ((i & 63u) == 0u && global_timer_ns() - t0 > a.limit_ns) {
+          atomicCAS(&me->ctl[0], 0, SITE_PEER_SUM);
+          ok = false;
+          break;
+        }
+      }
+    }
+    fence_acq_rel_sys();
+  }
+  if (!__syncthreads_and(ok)) return;
+  const int vpr = c / 8;
+  const long long n = static_cast<long long>(m) * vpr;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const unsigned char* mine = a.base[a.rank];
+  bool bad = false;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n; i += stride) {
+    const long long j = i / vpr;
+    const int v = static_cast<int>(i % vpr);
+    uint4 in[kPeerMaxRanks];
+#pragma unroll
+    for (int q = 0; q < kPeerMaxRanks; ++q)
+      if (q < a.world)
+        in[q] = __ldcg(reinterpret_cast<const uint4*>(mine + push_slot_off(off_s, parity, a.world, q, slot_rows, ld) +
+                                                     (j * ld + v * 8) * 2));
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+#pragma unroll
+    for (int q = 0; q < kPeerMaxRanks; ++q) {
+      if (q < a.world) {
+        const __half2* h = reinterpret_cast<const __half2*>(&in[q]);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = __half22float2(h[e]);
+          acc[2 * e] += f.x;
+          acc[2 * e + 1] += f.y;
+        }
+      }
+    }
+    uint4 o;
+    uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      bad |= f16_out_of_range(acc[2 * e]) || f16_out_of_range(acc[2 * e + 1]);
+      ow[e] = pack_f16x2_sat(acc[2 * e], acc[2 * e + 1]);
+    }
+    *reinterpret_cast<uint4*>(out + (j * ld_out + v * 8) * 2) = o;
+  }
+  if (__syncthreads_or(bad) && threadIdx.x == 0) atomicOr(&me->ctl[kRangeWord], 1);
 }
 
 // In-place all-reduce (sum) of an fp16 [m, c] matrix at `off` (row stride ld

@@ -414,6 +414,13 @@ SVD_DEV void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uin
                : "memory");
 }
 
+SVD_DEV uint4 ld_shared_v4(uint32_t addr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr)
+               : "memory");
+  return v;
+}
+
 SVD_DEV uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -436,5 +443,25 @@ SVD_DEV bool f16_out_of_range(float v) { return !(fabsf(v) <= 65504.0f); }
 // site.  The host reads both back (svdmlp_check_device_status).
 constexpr int kRangeWord = 1;
 SVD_DEV void flag_range(int* err) { atomicOr(err + kRangeWord, 1); }
+
+// System-scope ordering for flags that other GPUs read (peer memory).
+SVD_DEV void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+SVD_DEV unsigned ld_relaxed_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+SVD_DEV void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+SVD_DEV unsigned atom_add_acq_rel_gpu(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
 
 }  // namespace svdmlp

@@ -599,6 +599,9 @@ struct Workspace {
   int norm_parts = 0, norm_dim = 0, stats_ld = 0;
   float norm_eps = 0.0f;
   float* out_stats = nullptr;
+  // Tensor-parallel exchange fused into the H.u_down epilogue (the CTA-pair
+  // GEMM only; see GemmPush).
+  const GemmPush* push = nullptr;
 };
 
 static constexpr int64_t kCtlBytes = 256;
@@ -788,6 +791,10 @@ static int launch_gemm(const CUtensorMap& a, const CUtensorMap& a2, const CUtens
   p.timeout_ns = g_wait_limit_ns;
   p.residual = residual;
   p.ld_residual = ld_res;
+  if (w.push != nullptr) {
+    if constexpr (kPushable<Cfg> && Cfg::CTAS == 2) p.push = *w.push;
+    else return SVDMLP_ERR_INVALID_VALUE;
+  }
   // Unit raster, from an estimate of HBM traffic.  m-fastest (one group):
   // the weights are read once, A once if it fits in L2, else once per span
   // of N-tiles that one wave of pairs covers.  Grouped: M-tiles in groups
@@ -894,6 +901,7 @@ static int launch_gemv(const CUtensorMap& x, const CUtensorMap& x2, const CUtens
   p.timeout_ns = g_wait_limit_ns;
   p.residual = residual;
   p.ld_residual = ld_res;
+  if (w.push != nullptr) return SVDMLP_ERR_INVALID_VALUE;  // the fused exchange runs on the CTA-pair GEMM only
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(pl.grid));
   cfg.blockDim = dim3(192);
@@ -2471,6 +2479,77 @@ int svdmlp_peer_allgather(void* const* bases, int world, int rank, int64_t off, 
   SVD_CHECK(peer_grid(static_cast<int64_t>(m) * (row_bytes / 16), &grid));
   peer_allgather_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(a, off, m, row_bytes,
                                                                                      ld_bytes);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+int64_t svdmlp_peer_slots_bytes(int world, int slot_rows, int64_t ld_slot) {
+  if (world < 1 || world > kPeerMaxRanks || slot_rows <= 0 || ld_slot <= 0 || ld_slot % 8 != 0) return 0;
+  return 2LL * world * slot_rows * ld_slot * 2;
+}
+
+int svdmlp_forward_partial_f16_peer(const svdmlp_layout* L, const void* packed, const void* x, int64_t ldx, int M,
+                                    void* const* bases, int world, int rank, int64_t off_slots, int slot_rows,
+                                    int64_t ld_slot, void* ws, int64_t ws_bytes, void* stream) {
+  SVD_CHECK(check_layout(L));
+  if (L->kind != SVDMLP_KIND_SVD || L->r_gu <= 0 || L->r_d <= 0 || !packed || !x || M <= 0 || ldx < L->d ||
+      M > slot_rows || ld_slot < L->r_d || ld_slot % 8 != 0 || off_slots < kPeerSignalBytes || off_slots % 16 != 0)
+    return SVDMLP_ERR_INVALID_VALUE;
+  PeerArgs a;
+  SVD_CHECK(make_peer_args(bases, world, rank, &a));
+  Workspace w{};
+  SVD_CHECK(carve(L, M, ws, ws_bytes, &w));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint8_t* P = static_cast<const uint8_t*>(packed);
+  const void* xa;
+  int64_t ldxa;
+  SVD_CHECK(stage_in(x, ldx, M, L->d, w.xs, L->ld_d, &xa, &ldxa, s));
+  SVD_CHECK(run_gate_up(L, P, xa, ldxa, M, w.h, L->ld_ff, false, w, s));
+  if (M >= g_pair_min_m) {
+    // the CTA-pair H.u_down GEMM stores its rows straight into the slots
+    static_assert(kPushMaxRanks == kPeerMaxRanks, "one slot per rank");
+    GemmPush push{};
+    const long long slot_bytes = static_cast<long long>(slot_rows) * ld_slot * 2;
+    for (int q = 0; q < world; ++q) {
+      push.dst[q] = a.base[q] + off_slots + rank * slot_bytes;
+      push.flag[q] = reinterpret_cast<unsigned*>(&reinterpret_cast<PeerSignal*>(a.base[q])->ctl[kPushFlagWord + rank]);
+    }
+    PeerSignal* me = reinterpret_cast<PeerSignal*>(a.base[rank]);
+    push.epoch = reinterpret_cast<unsigned*>(&me->ctl[kPushEpochWord]);
+    push.exit_count = reinterpret_cast<unsigned*>(&me->ctl[kPushExitWord]);
+    push.parity_bytes = world * slot_bytes;
+    push.ld = ld_slot;
+    push.n = world;
+    push.rank = rank;
+    Workspace wp = w;
+    wp.push = &push;
+    // the output map (over the workspace's T) is built but not written
+    return run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, L->rp_d, wp, s, w.t);
+  }
+  // decode sizes: the partial goes to the workspace's T, then into the slots
+  SVD_CHECK(run_down_u(L, P, w.h, L->ld_ff, true, M, nullptr, L->rp_d, w, s, w.t));
+  unsigned grid = 0;
+  SVD_CHECK(peer_grid(static_cast<int64_t>(M) * (ld_slot / 8), &grid));
+  peer_push_slots_kernel<<<grid, kPeerThreads, 0, s>>>(a, reinterpret_cast<const unsigned char*>(w.t), L->rp_d,
+                                                       off_slots, M, slot_rows, L->r_d, ld_slot);
+  SVD_CUDA(cudaGetLastError());
+  g_launches.fetch_add(1);
+  return SVDMLP_OK;
+}
+
+int svdmlp_peer_sum_f16(void* const* bases, int world, int rank, int64_t off_slots, int slot_rows, int m, int c,
+                        int64_t ld_slot, void* out, int64_t ld_out, void* stream) {
+  PeerArgs a;
+  SVD_CHECK(make_peer_args(bases, world, rank, &a));
+  if (m <= 0 || m > slot_rows || c <= 0 || c % 8 != 0 || ld_slot < c || ld_slot % 8 != 0 || off_slots < kPeerSignalBytes ||
+      off_slots % 16 != 0 || !out || ld_out < c || ld_out % 8 != 0)
+    return SVDMLP_ERR_INVALID_VALUE;
+  if ((reinterpret_cast<uintptr_t>(out) & 15u) != 0) return SVDMLP_ERR_ALIGNMENT;
+  unsigned grid = 0;
+  SVD_CHECK(peer_grid(static_cast<int64_t>(m) * (c / 8), &grid));
+  peer_sum_slots_kernel<<<grid, kPeerThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      a, off_slots, m, slot_rows, c, ld_slot, static_cast<unsigned char*>(out), ld_out);
   SVD_CUDA(cudaGetLastError());
   g_launches.fetch_add(1);
   return SVDMLP_OK;

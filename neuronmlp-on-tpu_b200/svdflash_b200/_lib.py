@@ -118,6 +118,11 @@ SIGNATURES = {
                                                c_int64, c_void_p, c_int64, c_void_p]),
     "svdmlp_peer_allgather": (c_int, [POINTER(c_void_p), c_int, c_int, c_int64, c_int, c_int64, c_int64, c_void_p]),
     "svdmlp_peer_check_status": (c_int, [c_void_p, c_void_p]),
+    "svdmlp_peer_slots_bytes": (c_int64, [c_int, c_int, c_int64]),
+    "svdmlp_forward_partial_f16_peer": (c_int, [LP, V, V, I64, c_int, POINTER(c_void_p), c_int, c_int, c_int64,
+                                                c_int, c_int64, V, I64, V]),
+    "svdmlp_peer_sum_f16": (c_int, [POINTER(c_void_p), c_int, c_int, c_int64, c_int, c_int, c_int, c_int64,
+                                    c_void_p, c_int64, c_void_p]),
 }
 
 _lock = threading.Lock()

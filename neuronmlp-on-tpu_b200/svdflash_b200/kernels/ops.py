@@ -40,7 +40,7 @@ __all__ = [
     "PackedLayer", "pack_svd_layer", "pack_dense_layer", "low_rank_dim", "rank_for_ratio", "silu",
     "fused_gate_up", "fused_xuv", "xuv_matmul", "svd_mlp", "contracted_svd_mlp", "dense_mlp",
     "dense_matmul", "svd_mlp_packed", "contracted_mlp_packed", "dense_mlp_packed", "gate_up_packed", "xuv_packed",
-    "forward_partial_packed", "down_partial_packed", "down_finish_packed", "rmsnorm", "row_sumsq",
+    "forward_partial_packed", "forward_partial_peer_packed", "down_partial_packed", "down_finish_packed", "rmsnorm", "row_sumsq",
     "svd_block_packed", "workspace_for",
     "check_device_status", "launch_count",
 ]
@@ -466,6 +466,27 @@ def forward_partial_packed(layer: PackedLayer, x: torch.Tensor, partial: Optiona
     _lib.check(fn(ctypes.byref(layer.layout), layer.packed.data_ptr(), xb.data_ptr(), _ld(xb), m, partial.data_ptr(),
                   partial.stride(0), ws.ptr, ws.nbytes, _stream(xb.device)), "forward_partial")
     return partial
+
+
+def forward_partial_peer_packed(layer: PackedLayer, x: torch.Tensor, peer, off_slots: int, slot_rows: int,
+                                ld_slot: int) -> None:
+    """Stages 1-3 of an ff-shard with the exchange fused in: this rank's fp16
+    [M, r_d] partial goes straight into its slot of every rank's peer buffer
+    (`peer`: a svdflash_b200.peer.PeerBuffer; slots of `slot_rows` rows at
+    byte offset `off_slots`, row stride `ld_slot` elements), written by the
+    H.u_down GEMM's epilogue at prefill sizes; PeerBuffer.sum_f16 then sums
+    them."""
+    if layer.kind != _lib.KIND_SVD or layer.r_d == 0:
+        raise ValueError("the fused exchange needs an SVD layer")
+    xb = _prep_x(x, layer.d)
+    m = xb.shape[0]
+    if ld_slot < layer.r_d:
+        raise ValueError("slot rows must hold r_d columns")
+    peer.check_slots(off_slots, slot_rows, m, ld_slot)
+    ws = layer.workspace(m)
+    _lib.check(_lib.load().svdmlp_forward_partial_f16_peer(
+        ctypes.byref(layer.layout), layer.packed.data_ptr(), xb.data_ptr(), _ld(xb), m, peer.bases, peer.world,
+        peer.rank, off_slots, slot_rows, ld_slot, ws.ptr, ws.nbytes, _stream(xb.device)), "forward_partial_peer")
 
 
 def down_partial_packed(layer: PackedLayer, h: torch.Tensor, partial: Optional[torch.Tensor] = None):

@@ -138,6 +138,32 @@ class PeerBuffer:
         _lib.check(self.lib.svdmlp_peer_allgather(self.bases, self.world, self.rank, offset, m, row_bytes,
                                                   ld_bytes, self._stream()), "peer_allgather")
 
+    # ------------------------------------------------ fused exchange slots
+    def slots_bytes(self, slot_rows: int, ld: int) -> int:
+        """Bytes of the fused exchange's slots: two sets (alternating calls) of
+        one fp16 [slot_rows, ld] slot per rank.  A call of m <= slot_rows rows
+        uses the first m rows of each slot."""
+        return int(self.lib.svdmlp_peer_slots_bytes(self.world, slot_rows, ld))
+
+    def check_slots(self, off_slots: int, slot_rows: int, m: int, ld: int) -> None:
+        n = self.slots_bytes(slot_rows, ld)
+        if n <= 0 or not 0 < m <= slot_rows or off_slots < self.signal_bytes or off_slots % 16 or \
+                off_slots + n > self.nbytes:
+            raise ValueError("exchange slots outside the peer buffer's data area")
+
+    def sum_f16(self, off_slots: int, slot_rows: int, m: int, c: int, ld: int, out: torch.Tensor) -> torch.Tensor:
+        """The receiving half of the fused exchange: waits (bounded) until every
+        peer has filled its slot for this call, then writes the ranks' fp16
+        partials summed in rank order (fp32, rounded once) into `out`, a
+        row-major fp16 [m, >= c] matrix on this GPU."""
+        self.check_slots(off_slots, slot_rows, m, ld)
+        if c <= 0 or c % 8 or c > ld or out.dtype != torch.float16 or out.stride(1) != 1 or \
+                out.device != self.device or out.shape[0] < m or out.shape[1] < c:
+            raise ValueError("out must be a row-major fp16 [m, >= c] matrix on this GPU (c a multiple of 8)")
+        _lib.check(self.lib.svdmlp_peer_sum_f16(self.bases, self.world, self.rank, off_slots, slot_rows, m, c, ld,
+                                                out.data_ptr(), out.stride(0), self._stream()), "peer_sum")
+        return out
+
     def check_status(self) -> None:
         """Raises if a collective's wait expired (SvdMlpError) or an fp16 sum
         saturated (SvdMlpRangeError); synchronises the current stream."""

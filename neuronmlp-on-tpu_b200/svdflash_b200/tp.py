@@ -22,7 +22,11 @@ collectives="peer" (chosen by "auto" for groups of up to four GPUs that can
 all address each other; "peer" selects it for up to eight) runs the exchanges
 with the library's own kernels over NVLink peer memory (svdflash_b200.peer):
 the partial, XU and y live in a buffer every rank maps, and each collective is
-one kernel of plain stores between GPUs.  The
+one kernel of plain stores between GPUs.  In the all-reduce mode the exchange
+is fused into the H.u_down GEMM: its epilogue stores each partial tile into
+this rank's slot of every rank's buffer as the tile finishes, and a small kernel
+sums the slots once the peers' flags arrive (fused_exchange=False keeps the
+separate all-reduce kernel).  The
 fp16 sums are taken in rank order in fp32 and rounded once, so every rank
 gets the same bits.  collectives="nccl" uses torch.distributed (NCCL).
 """
@@ -74,7 +78,8 @@ class TensorParallelSvdMlp:
     """One ff-sharded SVD MLP layer on this rank's GPU."""
 
     def __init__(self, u_gate, v_gate, u_up, v_up, u_down, v_down, rank: int, world: int, group=None,
-                 reduce_dtype: torch.dtype = torch.float16, mode: str = "auto", collectives: str = "auto"):
+                 reduce_dtype: torch.dtype = torch.float16, mode: str = "auto", collectives: str = "auto",
+                 fused_exchange: bool = True):
         ff = v_gate.shape[1]
         lo, hi = shard_bounds(ff, rank, world)
         if reduce_dtype not in (torch.float16, torch.float32):
@@ -89,6 +94,9 @@ class TensorParallelSvdMlp:
             raise TypeError("the peer collectives reduce an fp16 partial")
         self.rank, self.world, self.group, self.reduce_dtype, self.mode = rank, world, group, reduce_dtype, mode
         self.collectives = collectives
+        # all-reduce mode on the peer collectives: the exchange runs inside
+        # the H.u_down GEMM (False: a separate all-reduce kernel after it)
+        self.fused_exchange = fused_exchange
         self.layer = ops.pack_svd_layer(u_gate, v_gate[:, lo:hi].contiguous(), u_up, v_up[:, lo:hi].contiguous(),
                                         u_down[lo:hi].contiguous(), v_down)
         self.r_d = u_down.shape[1]
@@ -117,7 +125,8 @@ class TensorParallelSvdMlp:
     def _ensure_peer(self, m: int, d: int) -> PeerBuffer:
         """The peer buffer for m rows (collective when it has to grow):
         partial [m, cols] fp16, the reduction's scratch, XU [m, 2 rp_gu] fp16,
-        y [m, d] bf16."""
+        y [m, d] bf16, and the fused exchange's slots (two sets of one fp16
+        [m, cols] slot per rank)."""
         if self._peer is not None and self._peer_m >= m:
             return self._peer
         if self._peer is not None:
@@ -128,8 +137,9 @@ class TensorParallelSvdMlp:
         lib = _lib.load()
         signal = int(lib.svdmlp_peer_signal_bytes())
         scratch = int(lib.svdmlp_peer_scratch_bytes(self.world, m, cols))
-        (self._off_part, self._off_scr, self._off_xu, self._off_y), total = layout(
-            [m * cols * 2, scratch, m * n1 * 2, m * d * 2], signal)
+        slots = int(lib.svdmlp_peer_slots_bytes(self.world, m, cols))
+        (self._off_part, self._off_scr, self._off_xu, self._off_y, self._off_slots), total = layout(
+            [m * cols * 2, scratch, m * n1 * 2, m * d * 2, slots], signal)
         self._cols, self._n1 = cols, n1
         self._peer = PeerBuffer(total, self.rank, self.world, self.group)
         self._peer_m = m
@@ -162,8 +172,14 @@ class TensorParallelSvdMlp:
         if self.peer_collectives():
             pb = self._ensure_peer(m, x.shape[1])
             part = pb.view(self._off_part, (m, self._cols), torch.float16)
-            ops.forward_partial_packed(self.layer, x, part[:, :self.r_d])
-            pb.allreduce_f16(self._off_part, m, self._cols, self._cols, self._off_scr)
+            if self.fused_exchange:
+                # H.u_down stores this rank's partial into every rank's slot as
+                # its tiles finish; the sum waits only for the peers' flags
+                ops.forward_partial_peer_packed(self.layer, x, pb, self._off_slots, self._peer_m, self._cols)
+                pb.sum_f16(self._off_slots, self._peer_m, m, self._cols, self._cols, part)
+            else:
+                ops.forward_partial_packed(self.layer, x, part[:, :self.r_d])
+                pb.allreduce_f16(self._off_part, m, self._cols, self._cols, self._off_scr)
             return ops.down_finish_packed(self.layer, part[:, :self.r_d], residual=residual, out=out)
         buf = self._partial_buffer(m, x.device)
         ops.forward_partial_packed(self.layer, x, buf[:, :self.r_d])

@@ -112,6 +112,21 @@ def test_entry_points_reject_bad_arguments(lib):
     assert lib.svdmlp_peer_allreduce_f16(bases, 2, 0, sig, 8, 8, 8, 8, None) == _lib.ERR_INVALID_VALUE  # scratch
     assert lib.svdmlp_peer_scratch_bytes(2, 37, 24) == 2 * 2 * 19 * 24 * 2
     assert lib.svdmlp_peer_check_status(None, None) == _lib.ERR_INVALID_VALUE
+    # the fused exchange: slot geometry and offsets checked before any CUDA call
+    assert lib.svdmlp_peer_slots_bytes(2, 256, 2872) == 2 * 2 * 256 * 2872 * 2
+    assert lib.svdmlp_peer_slots_bytes(2, 256, 2870) == 0 and lib.svdmlp_peer_slots_bytes(9, 256, 8) == 0
+    assert lib.svdmlp_forward_partial_f16_peer(ctypes.byref(L), 1, 1, 64, 8, bases, 2, 0, sig, 4, 40, None, 0,
+                                               None) == _lib.ERR_INVALID_VALUE  # M > slot_rows
+    assert lib.svdmlp_forward_partial_f16_peer(ctypes.byref(L), 1, 1, 64, 4, bases, 2, 0, sig, 4, 36, None, 0,
+                                               None) == _lib.ERR_INVALID_VALUE  # ld_slot < r_d
+    assert lib.svdmlp_forward_partial_f16_peer(ctypes.byref(L), 1, 1, 64, 4, bases, 2, 0, 0, 4, 40, None, 0,
+                                               None) == _lib.ERR_INVALID_VALUE  # slots in the signal area
+    assert lib.svdmlp_peer_sum_f16(bases, 2, 0, sig, 4, 8, 8, 8, ctypes.c_void_p(4096), 8, None) == \
+        _lib.ERR_INVALID_VALUE  # m > slot_rows
+    assert lib.svdmlp_peer_sum_f16(bases, 2, 0, sig, 8, 8, 12, 16, ctypes.c_void_p(4096), 16, None) == \
+        _lib.ERR_INVALID_VALUE  # c % 8
+    assert lib.svdmlp_peer_sum_f16(bases, 2, 0, sig, 8, 8, 8, 8, ctypes.c_void_p(4100), 8, None) == \
+        _lib.ERR_ALIGNMENT
 
 
 def test_status_strings(lib):

@@ -8,7 +8,9 @@ the reduce-scatter against the fp32 sum in rank order rounded once to fp16
 count, padded rows, repeated calls, and an fp16 overflow that must be
 reported.  The layer (both modes, forward and forward_rows, eager and
 captured in a CUDA graph) is checked against the oracle at the north-star
-tolerance and must give the same bits on every rank."""
+tolerance and must give the same bits on every rank; in the all-reduce mode
+the exchange fused into the H.u_down GEMM must give the same bits as the
+separate all-reduce kernel, at prefill, decode and ragged row counts."""
 from __future__ import annotations
 
 import datetime
@@ -133,6 +135,21 @@ def _worker(rank, world, port, q):
             out[mode] = {"full": full.float().cpu().numpy(), "full_res": full_res.float().cpu().numpy(),
                          "rows": got.float().cpu().numpy(), "nccl": nccl.float().cpu().numpy(),
                          "replay_equal": replay_equal, "peer": tp.peer_collectives()}
+            if mode == "allreduce":
+                # the exchange fused into H.u_down against the separate
+                # all-reduce kernel: prefill (CTA-pair GEMM), decode and ragged
+                # row counts on the same slots, one after another
+                unf = TensorParallelSvdMlp(*fd, rank=rank, world=world, mode=mode, collectives="peer",
+                                           fused_exchange=False)
+                pairs = []
+                for m_call in (M, 4, 37, M, 1):
+                    a = tp.forward(xd[:m_call])
+                    b = unf.forward(xd[:m_call])
+                    pairs.append((m_call, a.float().cpu().numpy(), b.float().cpu().numpy()))
+                tp.check_peer_status()
+                unf.check_peer_status()
+                unf.close()
+                out[mode]["fused_vs_unfused"] = pairs
             tp.close()
         q.put((rank, out))
     except Exception as e:  # noqa: BLE001 - reported to the parent
@@ -195,3 +212,9 @@ def test_peer_collectives_and_layer(cuda_device, world):
             assert_close(o["full"], o["nccl"], rel=1e-2, max_abs_rms=4e-2, what=f"{mode} peer vs NCCL rank {r}")
             assert o["replay_equal"], f"{mode}: graph replay differs from eager"
             np.testing.assert_array_equal(o["full"], outs[0][mode]["full"])
+            for m_call, fused, unfused in o.get("fused_vs_unfused", []):
+                # same partials, same rank-order fp32 sums rounded once: the same bits
+                np.testing.assert_array_equal(fused, unfused, err_msg=f"fused exchange, {m_call} rows, rank {r}")
+                assert_close(fused, ref[:m_call], what=f"fused exchange {m_call} rows rank {r}")
+        if mode == "allreduce":
+            assert outs[0][mode]["fused_vs_unfused"], "fused exchange not exercised"
