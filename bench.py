@@ -544,9 +544,9 @@ def main():
     ap.add_argument("--tp-collectives", choices=("auto", "nccl", "peer"), default="auto",
                     help="N>1: the library's peer-memory collectives over NVLink (auto, when every GPU can "
                          "address every other) or NCCL")
-    ap.add_argument("--tp-exchange", choices=("fused", "separate"), default="fused",
+    ap.add_argument("--tp-exchange", choices=("auto", "fused", "separate"), default="auto",
                     help="N>1, all-reduce mode on the peer collectives: the exchange fused into the H.u_down "
-                         "GEMM's epilogue (default) or a separate all-reduce kernel after it")
+                         "GEMM's epilogue or a separate all-reduce kernel after it (auto: fused for two GPUs)")
     ap.add_argument("--sweep", choices=("decode", "shapes", "stack", "stack70"), default=None,
                     help="print one JSON line per point of BASELINE configs 2, 5 or 3 instead of the bench line")
     args = ap.parse_args()
@@ -606,7 +606,8 @@ def main():
             return ops.svd_mlp_packed(layer, inp, out=out)
     else:
         tp = TensorParallelSvdMlp(*factors, rank=rank, world=world, mode=args.tp_mode,
-                                  collectives=args.tp_collectives, fused_exchange=args.tp_exchange == "fused")
+                                  collectives=args.tp_collectives,
+                                  fused_exchange=None if args.tp_exchange == "auto" else args.tp_exchange == "fused")
         y = torch.empty(m, d, dtype=torch.bfloat16, device=dev)
 
         def step(inp, out=y):

@@ -25,8 +25,8 @@ the partial, XU and y live in a buffer every rank maps, and each collective is
 one kernel of plain stores between GPUs.  In the all-reduce mode the exchange
 is fused into the H.u_down GEMM: its epilogue stores each partial tile into
 this rank's slot of every rank's buffer as the tile finishes, and a small kernel
-sums the slots once the peers' flags arrive (fused_exchange=False keeps the
-separate all-reduce kernel).  The
+sums the slots once the peers' flags arrive (the default for two GPUs;
+fused_exchange=True/False forces either).  The
 fp16 sums are taken in rank order in fp32 and rounded once, so every rank
 gets the same bits.  collectives="nccl" uses torch.distributed (NCCL).
 """
@@ -79,7 +79,7 @@ class TensorParallelSvdMlp:
 
     def __init__(self, u_gate, v_gate, u_up, v_up, u_down, v_down, rank: int, world: int, group=None,
                  reduce_dtype: torch.dtype = torch.float16, mode: str = "auto", collectives: str = "auto",
-                 fused_exchange: bool = True):
+                 fused_exchange: Optional[bool] = None):
         ff = v_gate.shape[1]
         lo, hi = shard_bounds(ff, rank, world)
         if reduce_dtype not in (torch.float16, torch.float32):
@@ -95,8 +95,9 @@ class TensorParallelSvdMlp:
         self.rank, self.world, self.group, self.reduce_dtype, self.mode = rank, world, group, reduce_dtype, mode
         self.collectives = collectives
         # all-reduce mode on the peer collectives: the exchange runs inside
-        # the H.u_down GEMM (False: a separate all-reduce kernel after it)
-        self.fused_exchange = fused_exchange
+        # the H.u_down GEMM (False: a separate all-reduce kernel after it;
+        # None: fused for groups of up to FUSED_AUTO_MAX_WORLD, as measured)
+        self.fused_exchange = world <= self.FUSED_AUTO_MAX_WORLD if fused_exchange is None else bool(fused_exchange)
         self.layer = ops.pack_svd_layer(u_gate, v_gate[:, lo:hi].contiguous(), u_up, v_up[:, lo:hi].contiguous(),
                                         u_down[lo:hi].contiguous(), v_down)
         self.r_d = u_down.shape[1]
@@ -121,6 +122,9 @@ class TensorParallelSvdMlp:
         return self.collectives == "peer"
 
     PEER_AUTO_MAX_WORLD = 4
+    # measured on 2 GPUs (8B layer at 1024 tokens: 209 vs 221 us per layer);
+    # larger groups keep the separate all-reduce kernel until measured
+    FUSED_AUTO_MAX_WORLD = 2
 
     def _ensure_peer(self, m: int, d: int) -> PeerBuffer:
         """The peer buffer for m rows (collective when it has to grow):

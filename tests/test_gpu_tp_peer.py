@@ -141,6 +141,10 @@ def _worker(rank, world, port, q):
                 # row counts on the same slots, one after another
                 unf = TensorParallelSvdMlp(*fd, rank=rank, world=world, mode=mode, collectives="peer",
                                            fused_exchange=False)
+                if not tp.fused_exchange:  # larger groups: force the fused path for this comparison
+                    tp.close()
+                    tp = TensorParallelSvdMlp(*fd, rank=rank, world=world, mode=mode, collectives="peer",
+                                              fused_exchange=True)
                 pairs = []
                 for m_call in (M, 4, 37, M, 1):
                     a = tp.forward(xd[:m_call])
