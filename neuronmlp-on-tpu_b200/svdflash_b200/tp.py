@@ -122,8 +122,9 @@ class TensorParallelSvdMlp:
         return self.collectives == "peer"
 
     PEER_AUTO_MAX_WORLD = 4
-    # measured on 2 GPUs (8B layer at 1024 tokens: 209 vs 221 us per layer);
-    # larger groups keep the separate all-reduce kernel until measured
+    # measured (8B layer at 1024 tokens, fused vs separate): 2 GPUs 209 vs 221
+    # us per layer; 4 GPUs 198 vs 182 (each rank stores its whole partial into
+    # three peers from the GEMM epilogue)
     FUSED_AUTO_MAX_WORLD = 2
 
     def _ensure_peer(self, m: int, d: int) -> PeerBuffer:
