@@ -130,8 +130,8 @@ class TensorParallelSvdMlp:
     def _ensure_peer(self, m: int, d: int) -> PeerBuffer:
         """The peer buffer for m rows (collective when it has to grow):
         partial [m, cols] fp16, the reduction's scratch, XU [m, 2 rp_gu] fp16,
-        y [m, d] bf16, and the fused exchange's slots (two sets of one fp16
-        [m, cols] slot per rank)."""
+        y [m, d] bf16, and, when the exchange is fused, its slots (two sets of
+        one fp16 [m, cols] slot per rank)."""
         if self._peer is not None and self._peer_m >= m:
             return self._peer
         if self._peer is not None:
@@ -142,7 +142,7 @@ class TensorParallelSvdMlp:
         lib = _lib.load()
         signal = int(lib.svdmlp_peer_signal_bytes())
         scratch = int(lib.svdmlp_peer_scratch_bytes(self.world, m, cols))
-        slots = int(lib.svdmlp_peer_slots_bytes(self.world, m, cols))
+        slots = int(lib.svdmlp_peer_slots_bytes(self.world, m, cols)) if self.fused_exchange else 0
         (self._off_part, self._off_scr, self._off_xu, self._off_y, self._off_slots), total = layout(
             [m * cols * 2, scratch, m * n1 * 2, m * d * 2, slots], signal)
         self._cols, self._n1 = cols, n1
