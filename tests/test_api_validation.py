@@ -149,3 +149,36 @@ def test_peer_buffer_layout_and_arguments():
         PeerBuffer(1 << 20, rank=0, world=9)
     with pytest.raises(ValueError):
         PeerBuffer(1 << 20, rank=2, world=2)
+
+
+def test_fused_exchange_slot_checks():
+    """The fused exchange's slot geometry and the checks PeerBuffer makes
+    before any CUDA call, on a buffer object that maps nothing."""
+    import torch
+    from svdflash_b200 import _build, _lib
+    from svdflash_b200.peer import PeerBuffer, layout
+    if _build.is_stale():
+        _build.build()
+    pb = PeerBuffer.__new__(PeerBuffer)  # the arithmetic only: no allocation, no peers
+    pb.lib, pb.world, pb.rank = _lib.load(), 2, 0
+    pb.signal_bytes = int(pb.lib.svdmlp_peer_signal_bytes())
+    pb.device = torch.device("cuda", 0)
+    slot_rows, ld = 256, 2872
+    n = pb.slots_bytes(slot_rows, ld)
+    assert n == 2 * 2 * slot_rows * ld * 2          # two sets of one [slot_rows, ld] fp16 slot per rank
+    (off,), pb.nbytes = layout([n], pb.signal_bytes)
+    pb.check_slots(off, slot_rows, 1, ld)            # any m up to slot_rows
+    pb.check_slots(off, slot_rows, slot_rows, ld)
+    for bad in ((off, slot_rows, slot_rows + 1, ld),  # more rows than a slot holds
+                (off, slot_rows, 0, ld),
+                (off + 8, slot_rows, 4, ld),          # misaligned
+                (0, slot_rows, 4, ld),                # in the signal area
+                (off, slot_rows + 1, 4, ld),          # slots past the buffer
+                (off, slot_rows, 4, ld + 4)):         # row stride not a multiple of 8
+        with pytest.raises(ValueError):
+            pb.check_slots(*bad)
+    out = torch.empty((4, ld), dtype=torch.float32)
+    with pytest.raises(ValueError):                  # fp32 out: refused before the call
+        pb.sum_f16(off, slot_rows, 4, ld, ld, out)
+    with pytest.raises(ValueError):                  # c not a multiple of 8
+        pb.sum_f16(off, slot_rows, 4, 2867, ld, torch.empty((4, ld), dtype=torch.float16))
