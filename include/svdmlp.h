@@ -284,8 +284,9 @@ int svdmlp_down_finish_f16(const svdmlp_layout* layout, const void* packed, cons
                            int64_t ld_partial, int m, void* y, int64_t ld_y, const void* residual,
                            int64_t ld_residual, void* workspace, int64_t workspace_bytes, void* stream);
 
-/* The all-gather split of the replicated stages (the survey's "next" item:
- * shard X . [u_g|u_u] over M, then all-gather).  Per rank of P:
+/* The all-gather split of the replicated stages (X . [u_g|u_u] sharded over
+ * M, then all-gathered; for layers whose replicated stages outweigh two more
+ * collectives).  Per rank of P:
  *   svdmlp_xu_project on its M/P rows -> fp16 XU rows [M/P, 2*rp_gu];
  *   all-gather XU over ranks (rows);
  *   svdmlp_partial_from_xu_f16 on all M rows (this rank's ff shard) -> fp16
