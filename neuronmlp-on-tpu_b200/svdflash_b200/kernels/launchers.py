@@ -88,18 +88,21 @@ def svd_mlp_with_fused_kernel(x, u_up, v_up, u_gate, v_gate, u_down, v_down, up_
 
 def fused_mlp_up_T(x, u_gate, v_gate, u_up, v_up, *, mixed_precision=True, interpret=False, async_dma=True,
                    **tile_params):
-    """Transposed activation [I, S] = (silu(X.Ug.Vg) * (X.Uu.Vu))^T."""
+    """Transposed activation [I, S] = (silu(X.Ug.Vg) * (X.Uu.Vu))^T, as a
+    transposed view of the kernel's row-major [S, I] output (no copy;
+    fused_three_mm_XTUV reads it back without one either)."""
     return ops.fused_gate_up(x, u_gate, v_gate, u_up, v_up, mixed_precision=mixed_precision,
-                             interpret=interpret).t().contiguous()
+                             interpret=interpret).t()
 
 
 def fused_three_mm_XTUV(hidden_t, u_down, v_down, *, mixed_precision=True, interpret=False, async_dma=True,
                         **tile_params):
-    """[S, H] = (hidden_t^T . U) . V for a transposed activation [I, S]."""
+    """[S, H] = (hidden_t^T . U) . V for a transposed activation [I, S]; a
+    transposed view of a row-major [S, I] (fused_mlp_up_T's output) is read in
+    place, any other layout is copied once."""
     if hidden_t.shape[0] != u_down.shape[0] or u_down.shape[1] != v_down.shape[0]:
         raise ValueError("hidden, U, V contraction dimensions do not match")
-    return ops.xuv_matmul(hidden_t.t().contiguous(), u_down, v_down, mixed_precision=mixed_precision,
-                          interpret=interpret)
+    return ops.xuv_matmul(hidden_t.t(), u_down, v_down, mixed_precision=mixed_precision, interpret=interpret)
 
 
 def nki_mm(x, up_v_proj, up_u_proj, gate_v_proj, gate_u_proj, down_v_proj, down_u_proj, *, mixed_precision=True,

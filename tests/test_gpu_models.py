@@ -38,9 +38,13 @@ def test_launcher_names(cuda_device):
     assert_close(to_np(y), orc.svd_mlp(x, *f), what="svd_mlp_with_fused_kernel")
     ht = launchers.fused_mlp_up_T(xd, ug, vg, uu, vu)
     assert tuple(ht.shape) == (i, s)
+    assert ht.t().is_contiguous()  # a view of the row-major [S, I] output, no copy
     y2 = launchers.fused_three_mm_XTUV(ht, ud, vd)
     hb = orc.bf16_round(orc.fused_gate_up(x, *f[:4]))
     assert_close(to_np(y2), orc.fused_xuv(hb, f[4], f[5]), what="XTUV")
+    # a row-major [I, S] activation (any other producer) gives the same result
+    y2c = launchers.fused_three_mm_XTUV(ht.contiguous(), ud, vd)
+    assert torch.equal(y2c, y2)
     y3 = launchers.nki_mm(xd, uu.t(), vu.t(), ug.t(), vg.t(), ud.t(), vd.t())
     assert_close(to_np(y3), orc.svd_mlp(x, *f), what="nki_mm")
     wg, wu, wd = orc.make_dense(33, h, i)
